@@ -1,0 +1,103 @@
+/*
+ * spilltune_b200 — C ABI of the B200-native frozen-linear hot path.
+ *
+ * Plain pointers and sizes only.  Every pointer argument is a CUDA device
+ * pointer on the calling thread's current device unless stated otherwise;
+ * `stream` is a cudaStream_t (NULL = legacy default stream).  Calls enqueue
+ * work on `stream` and return without synchronising.  Every entry point returns
+ * FL_OK (0) or an FL_ERR_* code; fl_last_error() gives the message (per thread).
+ *
+ * Frozen weights use the reference's unchanged group-128 record layout
+ * (ram_vram_finetune/quantization/codecs.py:34-43, :55-64, :93-105):
+ *   payload : uint8[ceil(numel/128) * 64], two 4-bit codes per byte, the even
+ *             element in the low nibble;
+ *   scales  : float32[ceil(numel/128)], one per 128 consecutive flat elements;
+ *   lut16   : float32[16] codebook; element value = bf16(lut16[code] * scale).
+ * For the reference's int4-sym-g128 format lut16[c] = c - 8; the NF4 group-128
+ * variant passes the NF4 codebook.  A projection weight W has shape [N, K]
+ * (out_features x in_features, row-major), numel = N*K.
+ *
+ * Activations and outputs are row-major bf16 (passed as uint16_t bit
+ * patterns); LoRA factors are fp32 A[rank, K] and B[N, rank] exactly as
+ * LoRAProjection stores them (ram_vram_finetune/finetune/lora.py:97-110).
+ */
+#ifndef SPILLTUNE_B200_H
+#define SPILLTUNE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FL_OK 0
+#define FL_ERR_ARG 1          /* invalid shape, alignment or null pointer */
+#define FL_ERR_UNSUPPORTED 2  /* valid request this build does not implement */
+#define FL_ERR_CUDA 3         /* CUDA runtime/driver error */
+#define FL_ERR_DEVICE 4       /* a kernel reported a bounded-wait timeout */
+
+#define FL_MAX_RANK 64
+
+/* Library version (major*10000 + minor*100 + patch). */
+int fl_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* fl_last_error(void);
+
+/* Reads the device status word of the current device: 0 when every kernel so
+ * far completed its pipeline, otherwise FL_STATUS_* bits of kernels whose
+ * bounded waits expired.  Synchronises the device.  reset != 0 clears it. */
+int fl_status(int reset, uint32_t* status_out);
+
+/*
+ * Dequantize one group-128 record into a BF16 buffer, bit-exact with the
+ * reference's decode_into (ram_vram_finetune/quantization/codecs.py:158-170,
+ * called per matrix by SlotSession.load, ram_vram_finetune/memory.py:224-229).
+ * numel may be any positive count (ragged tail groups allowed).
+ */
+int fl_dequant(const uint8_t* payload, const float* scales, const float* lut16, int64_t numel,
+               uint16_t* out_bf16, void* stream);
+
+/* Scratch bytes fl_fwd needs for a given token count (the scaled low-rank
+ * activations Ts = bf16(s * X.A^T), padded to 64 columns). */
+size_t fl_fwd_workspace_bytes(int64_t M, int rank);
+
+/*
+ * Frozen projection forward with the LoRA branch
+ *   Y[M,N] = X[M,K] . W^T + scale * (X . A^T) . B^T
+ * Replaces LoRAProjection.forward (ram_vram_finetune/finetune/lora.py:205-220)
+ * for a weight the slot holds in packed form (the reference decodes it with
+ * decode_into first, memory.py:224-229), and the NF4 path's linear_cuda
+ * (ram_vram_finetune/quantization/nf4_backend_cuda.py:888-917).
+ * rank = 0 computes the plain frozen F.linear (dense.py:122-124 without LoRA).
+ * Requires K % 128 == 0, rank <= 64, 16-byte aligned pointers, bias-free
+ * projections.  workspace: >= fl_fwd_workspace_bytes(M, rank) bytes (may be
+ * NULL when rank == 0).
+ */
+int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, const float* scales,
+           const float* lut16, int64_t N, const float* A, const float* B, int rank, float scale, uint16_t* Y,
+           void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes fl_bwd needs (Us = bf16(s * dY.B) and Ts, 64 columns each). */
+size_t fl_bwd_workspace_bytes(int64_t M, int rank);
+
+/*
+ * Recomputed-backward of the same projection (the autograd VJP that
+ * StreamingBlockFunction.backward takes, ram_vram_finetune/training/recompute.py:85-127):
+ *   dX = dY . W + scale * (dY . B) . A                        (bf16 out)
+ *   dA = scale * (dY . B)^T . X,  dB = scale * dY^T . (X . A^T)  (fp32 out)
+ * accumulate != 0 adds into dA/dB (grad_A/grad_B.add_, recompute.py:124-127);
+ * accumulate == 0 overwrites them.  dA/dB may be NULL when rank == 0.
+ * Requires K % 128 == 0, N % 64 == 0, rank <= 64.
+ */
+int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* payload,
+           const float* scales, const float* lut16, const float* A, const float* B, int rank, float scale,
+           uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace, size_t workspace_bytes,
+           void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPILLTUNE_B200_H */

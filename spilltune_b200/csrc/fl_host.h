@@ -1,0 +1,36 @@
+// Host-side internals shared by the .cu translation units of libspilltune_b200.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/spilltune_b200.h"
+
+namespace fl {
+
+// Records a formatted message for fl_last_error() and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+uint32_t* status_word(int device);  // device status word of the calling device
+
+int launch_tc_gemm(bool bwd, const void* act, const void* low, const uint8_t* codes, const float* scales,
+                   const float* lut, const float* lora, int rank, void* out, int M, int N, int K,
+                   uint32_t* status, cudaStream_t stream);
+
+int launch_dequant(const uint8_t* payload, const float* scales, const float* lut, int64_t numel, void* out,
+                   cudaStream_t stream);
+
+// out[m, j] = bf16(s * sum_r P[m, r] * Q(j, r)), j < rank, zero for rank <= j < 64.
+// Q(j, r) = q[j * q_sj + r * q_sr] (fp32).
+int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
+                     float s, void* out64, cudaStream_t stream);
+
+// out(p, j) (+)= sum_m P[m, p] * Q[m, j]  (P bf16 [M, Pdim], Q bf16 [M, 64]),
+// out(p, j) = out[p * o_sp + j * o_sj] fp32, j < rank.
+int launch_lora_grad(const void* P, int M, int Pdim, const void* Q, int rank, float* out, int64_t o_sp,
+                     int64_t o_sj, int accumulate, cudaStream_t stream);
+
+int launch_smallm_fwd(const void* X, const void* Ts, const uint8_t* codes, const float* scales,
+                      const float* lut, const float* lora, int rank, void* Y, int M, int N, int K,
+                      cudaStream_t stream);
+
+}  // namespace fl

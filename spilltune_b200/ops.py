@@ -1,0 +1,155 @@
+"""Torch-facing frozen-linear operators over the C ABI.
+
+``frozen_lora_linear(x, weight, A, B, scale)`` is the drop-in for the
+reference's ``LoRAProjection.forward(x, base_weight)`` (finetune/lora.py:205-220)
+when the slot hands the projection its packed record instead of a decoded BF16
+matrix.  Its autograd backward returns ``(dX, dA, dB)`` in one fused call, so
+``torch.autograd.grad(output, [hidden, A0, B0, ...])`` inside the reference's
+``StreamingBlockFunction.backward`` (training/recompute.py:102-127) works
+unchanged and accumulates into ``grad_A``/``grad_B`` exactly as before.
+
+All work runs on the current CUDA stream.  CPU tensors are rejected: the path
+has no CPU fallback.
+"""
+import torch
+
+from . import _lib
+from .codec import PackedWeight
+
+FL_MAX_RANK = 64
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("unsupported_capability: spilltune_b200 ops need CUDA tensors (no CPU fallback)")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def dequant(weight: PackedWeight, out=None):
+    """Decode a packed record into a BF16 [N, K] tensor (bit-exact decode_into)."""
+    _need_cuda(weight.payload, weight.scales, weight.lut)
+    if out is None:
+        out = torch.empty(weight.shape, dtype=torch.bfloat16, device=weight.device)
+    if out.dtype != torch.bfloat16 or not out.is_contiguous() or out.numel() != weight.numel:
+        raise ValueError("dequant destination must be a contiguous bf16 tensor of the record's numel")
+    _lib.call("fl_dequant", _ptr(weight.payload), _ptr(weight.scales), _ptr(weight.lut), weight.numel,
+              _ptr(out), _stream())
+    return out
+
+
+def _flat(x, K):
+    if x.shape[-1] != K:
+        raise ValueError(f"input width mismatch: expected {K}, got {x.shape[-1]}")
+    x2 = x.reshape(-1, K)
+    if x2.dtype != torch.bfloat16:
+        raise ValueError("activations must be bf16")
+    return x2.contiguous()
+
+
+def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0):
+    """Y = x . W^T + scale * (x . A^T) . B^T  (bf16 out; plain frozen linear if A is None)."""
+    N, K = weight.shape
+    x2 = _flat(x, K)
+    rank = 0 if A is None else A.shape[0]
+    _need_cuda(x2, weight.payload, A, B)
+    if rank:
+        if A.dtype != torch.float32 or B.dtype != torch.float32 or tuple(A.shape) != (rank, K) \
+                or tuple(B.shape) != (N, rank):
+            raise ValueError("LoRA factors must be fp32 A[rank, K] and B[N, rank]")
+        A = A.detach().contiguous()
+        B = B.detach().contiguous()
+    M = x2.shape[0]
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x2.device)
+    ws_bytes = _lib.load().fl_fwd_workspace_bytes(M, rank)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device) if ws_bytes else None
+    if M:
+        _lib.call("fl_fwd", _ptr(x2), M, K, _ptr(weight.payload), _ptr(weight.scales), _ptr(weight.lut), N,
+                  _ptr(A), _ptr(B), rank, float(scale), _ptr(y), _ptr(ws), ws_bytes, _stream())
+    return y.view(*x.shape[:-1], N)
+
+
+def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False):
+    """Returns (dX, dA, dB) of fwd(); dA/dB are fp32 (accumulated into when given and accumulate)."""
+    N, K = weight.shape
+    dy2 = _flat(dy, N)
+    rank = 0 if A is None else A.shape[0]
+    M = dy2.shape[0]
+    x2 = _flat(x, K) if rank else None
+    _need_cuda(dy2, x2, weight.payload, A, B)
+    dx = torch.empty((M, K), dtype=torch.bfloat16, device=dy2.device)
+    if rank:
+        A = A.detach().contiguous()
+        B = B.detach().contiguous()
+        if dA is None:
+            dA = torch.empty((rank, K), dtype=torch.float32, device=dy2.device)
+            accumulate = False
+        if dB is None:
+            dB = torch.empty((N, rank), dtype=torch.float32, device=dy2.device)
+            accumulate = False
+    ws_bytes = _lib.load().fl_bwd_workspace_bytes(M, rank)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dy2.device) if ws_bytes else None
+    if M:
+        _lib.call("fl_bwd", _ptr(dy2), _ptr(x2), M, N, K, _ptr(weight.payload), _ptr(weight.scales),
+                  _ptr(weight.lut), _ptr(A), _ptr(B), rank, float(scale), _ptr(dx), _ptr(dA), _ptr(dB),
+                  int(bool(accumulate)), _ptr(ws), ws_bytes, _stream())
+    elif rank and not accumulate:
+        dA.zero_()
+        dB.zero_()
+    return dx.view(*dy.shape[:-1], K), dA, dB
+
+
+class FrozenLoRALinear(torch.autograd.Function):
+    """Autograd node of the fused frozen projection (weight frozen, A/B trainable)."""
+
+    @staticmethod
+    def forward(ctx, x, A, B, weight, scale):
+        ctx.weight = weight
+        ctx.scale = scale
+        ctx.has_lora = A is not None
+        if ctx.has_lora:
+            ctx.save_for_backward(x, A, B)
+        else:
+            ctx.save_for_backward(x)
+        return fwd(x, weight, A, B, scale)
+
+    @staticmethod
+    def backward(ctx, dy):
+        if ctx.has_lora:
+            x, A, B = ctx.saved_tensors
+            dx, dA, dB = bwd(dy.contiguous(), x, ctx.weight, A, B, ctx.scale)
+            return dx, dA, dB, None, None
+        (x,) = ctx.saved_tensors
+        dx, _, _ = bwd(dy.contiguous(), x, ctx.weight)
+        return dx, None, None, None, None
+
+
+def frozen_lora_linear(x, weight: PackedWeight, A=None, B=None, scale=0.0):
+    """Autograd-capable Y = x . W^T + scale * (x . A^T) . B^T over a packed frozen weight."""
+    return FrozenLoRALinear.apply(x, A, B, weight, float(scale))
+
+
+def lora_projection_forward(proj, x, weight: PackedWeight, base_bias=None):
+    """``LoRAProjection.forward(x, base_weight, base_bias)`` with a packed base weight.
+
+    Same argument meaning and error behaviour as finetune/lora.py:205-220
+    (shape checks raise ValueError); bias-carrying projections are rejected
+    because the fused kernels have no bias term.
+    """
+    if tuple(weight.shape) != tuple(proj.base_weight_shape):
+        raise ValueError(
+            f"{proj.target_path} base weight shape mismatch: expected "
+            f"{tuple(proj.base_weight_shape)}, got {tuple(weight.shape)}")
+    if x.shape[-1] != proj.in_features:
+        raise ValueError(
+            f"{proj.target_path} input width mismatch: expected {proj.in_features}, got {x.shape[-1]}")
+    if base_bias is not None:
+        raise ValueError("unsupported_capability: fused frozen linear has no bias term")
+    return frozen_lora_linear(x, weight, proj.A, proj.B, proj.scale)

@@ -1,0 +1,77 @@
+"""The C-ABI library builds for sm_100a, loads, exports every declared entry point
+and validates arguments before touching the GPU (runs without a GPU)."""
+import ctypes
+import os
+import re
+import shutil
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    names = []
+    for f in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if f.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", f)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names += re.findall(r"\b(fl_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from spilltune_b200 import build, _lib
+    if not os.path.exists(build.LIB) and not (shutil.which("nvcc") or os.path.exists("/usr/local/cuda/bin/nvcc")):
+        pytest.skip("nvcc unavailable and library not prebuilt")
+    build.build()
+    return _lib.load()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = _declared()
+    assert "fl_fwd" in names and "fl_bwd" in names and "fl_dequant" in names
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_python_binding_covers_header():
+    from spilltune_b200 import _lib
+    assert set(_declared()) <= set(_lib.SIGNATURES)
+
+
+def test_version_and_workspace_sizes(lib):
+    assert lib.fl_version() >= 100
+    assert lib.fl_fwd_workspace_bytes(8192, 16) == 8192 * 128
+    assert lib.fl_fwd_workspace_bytes(8192, 0) == 0
+    assert lib.fl_bwd_workspace_bytes(100, 8) == 100 * 256
+
+
+def _fwd(lib, M=16, K=256, N=128, rank=0, ptr=1024, ws=0):
+    P = ptr
+    return lib.fl_fwd(P, M, K, P, P, P, N, P if rank else None, P if rank else None, rank, 2.0, P,
+                      P if ws else None, ws, None)
+
+
+def test_argument_validation_without_gpu(lib):
+    from spilltune_b200._lib import FL_ERR_ARG, FL_ERR_UNSUPPORTED
+    assert _fwd(lib, K=100) == FL_ERR_ARG
+    assert b"multiple of 128" in lib.fl_last_error()
+    assert _fwd(lib, rank=65) == FL_ERR_UNSUPPORTED
+    assert _fwd(lib, rank=16, ws=0) == FL_ERR_ARG
+    assert _fwd(lib, ptr=1032) == FL_ERR_ARG  # misaligned payload
+    assert lib.fl_dequant(None, None, None, 10, None, None) == FL_ERR_ARG
+    assert lib.fl_dequant(None, None, None, 0, None, None) == 0
+    P = 1024
+    rc = lib.fl_bwd(P, P, 16, 100, 256, P, P, P, None, None, 0, 1.0, P, None, None, 0, None, 0, None)
+    assert rc == FL_ERR_ARG and b"multiple of 64" in lib.fl_last_error()
+
+
+def test_ops_reject_cpu_tensors():
+    from spilltune_b200 import codec, ops
+    w = codec.encode_int4_sym(torch.randn(128, 256) * 0.02)
+    x = torch.randn(4, 256).to(torch.bfloat16)
+    with pytest.raises(ValueError, match="no CPU fallback"):
+        ops.fwd(x, w)

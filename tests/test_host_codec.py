@@ -1,0 +1,43 @@
+"""Host-side record handling of the product package, checked against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+import oracle.codec as oc
+from spilltune_b200 import codec
+
+
+@pytest.mark.parametrize("shape", [(1, 128), (1, 129), (3, 257), (64, 384)])
+def test_host_int4_encoder_matches_oracle(shape):
+    g = torch.Generator().manual_seed(sum(shape))
+    w = torch.randn(*shape, generator=g) * 0.03
+    w[0, :64] = 0
+    pw = codec.encode_int4_sym(w)
+    p, s = oc.encode_int4_sym(w.numpy())
+    assert np.array_equal(pw.payload.numpy(), p)
+    assert np.array_equal(pw.scales.numpy(), s)
+
+
+@pytest.mark.parametrize("shape", [(2, 256), (5, 129)])
+def test_host_nf4_encoder_matches_oracle(shape):
+    g = torch.Generator().manual_seed(7)
+    w = torch.randn(*shape, generator=g) * 0.02
+    pw = codec.encode_nf4(w)
+    p, s = oc.encode_nf4(w.numpy())
+    assert np.array_equal(pw.payload.numpy(), p)
+    assert np.array_equal(pw.scales.numpy(), s)
+    assert torch.equal(pw.lut, torch.from_numpy(oc.NF4_LUT))
+
+
+def test_from_record_wraps_reference_layout():
+    d = np.load("tests/golden/codec_int4.npz")
+    spec = {"version": 1, "shape": [32, 256], "dtype": "bfloat16", "codec": "int4-sym-g128",
+            "group_size": 128, "numel": 32 * 256}
+    parts = {"payload": torch.from_numpy(d["mat32x256/payload"]), "scales": torch.from_numpy(d["mat32x256/scales"])}
+    pw = codec.from_record(spec, parts)
+    assert pw.shape == (32, 256) and pw.codec == codec.INT4_SYM
+    assert pw.payload.data_ptr() == parts["payload"].data_ptr()
+    with pytest.raises(ValueError, match="unsupported_quantization"):
+        codec.from_record(dict(spec, codec="int8-sym-g128"), parts)
+    with pytest.raises(ValueError, match="payload"):
+        codec.PackedWeight(parts["payload"][:-1], parts["scales"], codec.INT4_SYM_LUT, (32, 256))

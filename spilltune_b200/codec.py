@@ -112,28 +112,29 @@ def _groups(w):
     flat = w.detach().reshape(-1).to(torch.float32)
     n = flat.numel()
     g = (n + GROUP - 1) // GROUP
-    chunk = torch.zeros(g * GROUP, dtype=torch.float32)
+    chunk = torch.zeros(g * GROUP, dtype=torch.float32, device=flat.device)
     chunk[:n] = flat
     return chunk.view(g, GROUP), n
 
 
 def encode_int4_sym(w):
-    """int4-sym-g128 encoder (same arithmetic as codecs.py:86-105)."""
-    chunk, _ = _groups(w.cpu())
+    """int4-sym-g128 encoder (same arithmetic as codecs.py:86-105).  Runs on the
+    tensor's device (CPU, or a CUDA device for large synthetic models)."""
+    chunk, _ = _groups(w)
     if not torch.isfinite(chunk).all():
         raise ValueError("nonfinite quantization input")
     scale = chunk.abs().amax(1) / 7
     scale = torch.where(scale == 0, torch.ones_like(scale), scale)
     q = ((chunk / scale[:, None]).clamp(-7, 7).round().to(torch.uint8) + 8).flatten().view(-1, 2)
     payload = (q[:, 0] | (q[:, 1] << 4)).contiguous()
-    return PackedWeight(payload, scale.contiguous(), INT4_SYM_LUT.clone(), tuple(w.shape), INT4_SYM)
+    return PackedWeight(payload, scale.contiguous(), INT4_SYM_LUT.to(chunk.device), tuple(w.shape), INT4_SYM)
 
 
 def encode_nf4(w, lut=None):
     """NF4 group-128 encoder: scale = group absmax (1 for an all-zero group),
     code = nearest codebook entry to x/scale (first index on ties)."""
-    lut = NF4_LUT if lut is None else lut
-    chunk, _ = _groups(w.cpu())
+    chunk, _ = _groups(w)
+    lut = (NF4_LUT if lut is None else lut).to(chunk.device)
     if not torch.isfinite(chunk).all():
         raise ValueError("nonfinite quantization input")
     scale = chunk.abs().amax(1)

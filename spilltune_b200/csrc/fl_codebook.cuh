@@ -19,34 +19,42 @@ struct ProductTable {
   uint32_t hi[4];  // byte c of the plane = high byte
 };
 
-__device__ __forceinline__ ProductTable make_table(const float (&lut)[16], float scale) {
-  uint32_t p[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = pack_bf16x2(__fmul_rn(lut[2 * i], scale), __fmul_rn(lut[2 * i + 1], scale));
+// `lut` may point to shared or global memory (16 floats).
+__device__ __forceinline__ ProductTable make_table(const float* lut, float scale) {
   ProductTable t;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    t.lo[i] = prmt(p[2 * i], p[2 * i + 1], 0x6420);
-    t.hi[i] = prmt(p[2 * i], p[2 * i + 1], 0x7531);
+    const float4 a = *reinterpret_cast<const float4*>(lut + 4 * i);
+    const uint32_t p0 = pack_bf16x2(__fmul_rn(a.x, scale), __fmul_rn(a.y, scale));
+    const uint32_t p1 = pack_bf16x2(__fmul_rn(a.z, scale), __fmul_rn(a.w, scale));
+    t.lo[i] = prmt(p0, p1, 0x6420);
+    t.hi[i] = prmt(p0, p1, 0x7531);
   }
   return t;
 }
 
-// Decode the four codes held in nibbles 0..3 of `w16` (bits 0..15) into two
-// bf16x2 words: out0 = {e0 (low half), e1}, out1 = {e2, e3}.
-__device__ __forceinline__ void lookup4(const ProductTable& t, uint32_t w16, uint32_t& out0, uint32_t& out1) {
-  const uint32_t sel = w16 & 0x7777u;                 // low 3 bits of each code
-  const uint32_t mask = prmt(w16 << 4, w16, 0xD9C8);  // 0xFF per byte where code bit 3 is set
+// Look up four codes: `sel` holds their low three bits in nibbles 0..3 (bit 3
+// of each nibble clear), `mask` is 0xFF in byte i when code i has bit 3 set.
+// Returns two bf16x2 words: out0 = {e0 (low half), e1}, out1 = {e2, e3}.
+__device__ __forceinline__ void lookup4(const ProductTable& t, uint32_t sel, uint32_t mask, uint32_t& out0,
+                                        uint32_t& out1) {
   const uint32_t lo = (prmt(t.lo[0], t.lo[1], sel) & ~mask) | (prmt(t.lo[2], t.lo[3], sel) & mask);
   const uint32_t hi = (prmt(t.hi[0], t.hi[1], sel) & ~mask) | (prmt(t.hi[2], t.hi[3], sel) & mask);
   out0 = prmt(lo, hi, 0x5140);
   out1 = prmt(lo, hi, 0x7362);
 }
 
-// Eight codes of one 32-bit payload word -> four bf16x2 words in element order.
+// Eight codes of one 32-bit payload word (element i in nibble i) -> four bf16x2
+// words in element order.  The selector and bit-3 masks of both halves come
+// from one AND, one shift and two prmt (sign-replicate mode): byte i of a mask
+// copies the sign of the byte holding bit 3 of code i, either in w or in w<<4.
 __device__ __forceinline__ void lookup8(const ProductTable& t, uint32_t w, uint32_t* out) {
-  lookup4(t, w & 0xFFFFu, out[0], out[1]);
-  lookup4(t, w >> 16, out[2], out[3]);
+  const uint32_t sel = w & 0x77777777u;
+  const uint32_t w4 = w << 4;
+  const uint32_t mask_lo = prmt(w4, w, 0xD9C8);  // codes 0..3
+  const uint32_t mask_hi = prmt(w4, w, 0xFBEA);  // codes 4..7
+  lookup4(t, sel, mask_lo, out[0], out[1]);
+  lookup4(t, sel >> 16, mask_hi, out[2], out[3]);
 }
 
 }  // namespace fl

@@ -12,21 +12,31 @@
 // (ram_vram_finetune/finetune/lora.py:205-220, quantization/codecs.py:158-170)
 // and its autograd backward (training/recompute.py:85-127).
 //
-// Mapping onto the 5th-gen tensor core ("TS" form, A operand in TMEM):
-//   * MMA M (128 TMEM lanes) runs over W rows (forward) or W columns (backward);
-//     MMA N (256) runs over tokens; MMA K runs over the reduction dim in 64-wide
-//     stages.
+// Mapping onto the 5th-gen tensor core ("TS" form, A operand in TMEM), run by
+// a CTA pair (cluster of 2, tcgen05 cta_group::2):
+//   * MMA M (256 = 128 TMEM lanes in each CTA) runs over W rows (forward) or W
+//     columns (backward); MMA N (256) runs over tokens, each CTA holding the
+//     shared-memory half of its 128 tokens; MMA K runs over the reduction dim
+//     in 64-wide stages.  The pair halves the activation bytes each SM loads
+//     and stores per FLOP compared with one CTA.
 //   * A = dequantized weight tile, written straight from registers into TMEM
 //     by four dequant warps (tcgen05.st): the BF16 weight tile never touches
 //     shared memory.
-//   * B = activation tile [256 tokens x 64], TMA-loaded with the 128-byte swizzle.
+//   * B = activation tile [128 tokens x 64] per CTA, TMA-loaded (no multicast)
+//     with the 128-byte swizzle.
 //   * Packed codes arrive by TMA into a small shared-memory ring.
 //   * One extra stage appends the LoRA rank (<= 64) to the K dimension: A =
 //     bf16 LoRA factor rows, B = the scaled low-rank activations.
-//   * D = 128 x 256 fp32 accumulator in TMEM, read back by the same four warps.
+//   * D = 256 x 256 fp32 accumulator, 128 rows in each CTA's TMEM, read back by
+//     the dequant warps of that CTA.
 //
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
-// issuer, warps 2-5 dequant producers then epilogue.
+// Warp roles (448 threads per CTA): warp 0 TMA producer, warp 1 TMEM owner
+// (both CTAs) + MMA issuer (leader CTA only), warps 2-13 dequant producers in
+// three groups of four that take turns on pairs of stages (one warp per TMEM
+// lane quarter decodes the whole stage for its lanes), then epilogue.
+// Synchronisation: full[s] (local TMA bytes), afull[s] (leader only: 8 local +
+// 8 peer dequant-warp arrivals), empty[s] and accum (multicast tcgen05.commit
+// from the leader into both CTAs).
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -35,16 +45,19 @@
 
 namespace fl {
 
-constexpr int kLanes = 128;         // UMMA M
-constexpr int kTok = 256;           // UMMA N
+constexpr int kLanes = 128;         // W rows (or columns) per CTA; UMMA M = 256 per pair
+constexpr int kTok = 256;           // UMMA N (tokens per pair tile)
+constexpr int kTokHalf = 128;       // tokens whose activations each CTA holds
 constexpr int kStageK = 64;         // reduction elements per stage
-constexpr int kStages = 5;
+constexpr int kStages = 8;
+constexpr int kGroupM = 8;          // token tiles per band of the grouped tile order
 constexpr int kAccCols = 256;       // fp32 accumulator columns
 constexpr int kTmemCols = 512;      // power-of-two allocation (acc + A ring)
 constexpr int kAStageCols = kStageK / 2;  // bf16 pairs per lane per stage
-constexpr int kXBytes = kTok * kStageK * 2;  // 32 KiB activation tile
+constexpr int kXBytes = kTokHalf * kStageK * 2;  // 16 KiB activation half-tile
 constexpr int kQBytes = kLanes * kStageK / 2;  // 4 KiB packed-code tile
-constexpr int kThreads = 192;
+constexpr int kGroups = 3;                     // dequant warp groups (4 warps each)
+constexpr int kThreads = 64 + 128 * kGroups;   // 2 control warps + dequant/epilogue warps
 static_assert(kAccCols + kStages * kAStageCols <= kTmemCols, "TMEM budget");
 
 struct GemmArgs {
@@ -59,11 +72,12 @@ struct GemmArgs {
 
 struct __align__(8) GemmBarriers {
   uint64_t full[kStages];   // TMA bytes landed
-  uint64_t afull[kStages];  // dequant warps finished writing the TMEM A stage
+  uint64_t afull[kStages];  // leader: both CTAs' dequant warps finished the TMEM A stage
   uint64_t empty[kStages];  // MMAs reading the stage completed
   uint64_t accum;           // all MMAs completed
   uint32_t tmem_base;
   uint32_t abort_word;
+  alignas(16) float lut[16];  // codebook copy for the decoders
 };
 
 constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * (kXBytes + kQBytes) + sizeof(GemmBarriers);
@@ -86,8 +100,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int L = kBwd ? K : N;   // output columns (TMEM lane dimension)
   const int R = kBwd ? N : K;   // reduction dimension
   const int groups_per_row = K / 128;
-  const int l0 = blockIdx.x * kLanes;
-  const int m0 = blockIdx.y * kTok;
+  const uint32_t crank = cluster_ctarank();       // 0 = leader of the CTA pair
+  // Grouped tile order: pairs that run at the same time cover a band of
+  // kGroupM token tiles x several weight tiles, so an activation tile is
+  // requested by a handful of pairs at once instead of by every SM.
+  int w_tile, m_tile;
+  {
+    const int num_w = (L + 2 * kLanes - 1) / (2 * kLanes);
+    const int num_m = (M + kTok - 1) / kTok;
+    const int pair = blockIdx.x >> 1;
+    const int band = pair / (kGroupM * num_w);
+    const int first_m = band * kGroupM;
+    const int rows_in_band = min(kGroupM, num_m - first_m);
+    const int local = pair - band * kGroupM * num_w;
+    m_tile = first_m + local % rows_in_band;
+    w_tile = local / rows_in_band;
+  }
+  const int l0 = w_tile * (2 * kLanes) + static_cast<int>(crank) * kLanes;
+  const int m0 = m_tile * kTok;                     // first token of the pair tile
+  const int mh = m0 + static_cast<int>(crank) * kTokHalf;  // first token of this CTA's half
   const int n_main = R / kStageK;
   const bool has_lora = args.rank > 0;
   const int n_iter = n_main + (has_lora ? 1 : 0);
@@ -96,19 +127,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->afull[s], 128);
+      mbar_init(&bars->afull[s], 2 * 4);  // one arrival per dequant warp of the owning group, both CTAs
       mbar_init(&bars->empty[s], 1);
     }
     mbar_init(&bars->accum, 1);
     bars->abort_word = 0;
     fence_barrier_init();
   }
+  if (threadIdx.x < 16) {
+    bars->lut[threadIdx.x] = __ldg(args.lut + threadIdx.x);
+  }
   if (warp == 1) {
-    tmem_alloc(&bars->tmem_base, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc2(&bars->tmem_base, kTmemCols);
+    tmem_relinquish2();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // peer barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
@@ -127,14 +162,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (it < n_main) {
           const int r0 = it * kStageK;
           mbar_arrive_expect_tx(&bars->full[s], kXBytes + kQBytes);
-          tma_load_2d(xs + s * kXBytes, &tm_act, r0, m0, &bars->full[s]);
+          tma_load_2d(xs + s * kXBytes, &tm_act, r0, mh, &bars->full[s]);
           if (!kBwd)
             tma_load_2d(qs + s * kQBytes, &tm_code, r0 / 2, l0, &bars->full[s]);       // 128 rows x 32 B
           else
             tma_load_2d(qs + s * kQBytes, &tm_code, l0 / 2, r0, &bars->full[s]);       // 64 rows x 64 B
         } else {
           mbar_arrive_expect_tx(&bars->full[s], kXBytes);
-          tma_load_2d(xs + s * kXBytes, &tm_low, 0, m0, &bars->full[s]);
+          tma_load_2d(xs + s * kXBytes, &tm_low, 0, mh, &bars->full[s]);
         }
         ++issued;
       }
@@ -146,193 +181,214 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kLanes, kTok);
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (lane == 0 && crank == 0) {
+      const uint32_t idesc = idesc_bf16_f32(2 * kLanes, kTok);
       const int lora_k_steps = (args.rank + 15) / 16;
       for (int it = 0; it < n_iter; ++it) {
         const int s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) break;
-        if (!mbar_wait(&bars->afull[s], ph, abort_word, args.status, kStatusTimeoutFull)) break;
+        // Every dequant warp of both CTAs arrives only after its own CTA's
+        // TMA bytes for the stage landed, so afull covers both B halves too.
+        if (!mbar_wait_cluster(&bars->afull[s], ph, abort_word, args.status, kStatusTimeoutFull)) break;
         tc_fence_after();
         const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(xs + s * kXBytes));
         const uint32_t a_col = tmem_base + kAccCols + s * kAStageCols;
         const int ksteps = it < n_main ? kStageK / 16 : lora_k_steps;
         for (int kk = 0; kk < ksteps; ++kk)
-          mma_ts(tmem_base, a_col + kk * 8, bdesc + 2 * kk, idesc, (it | kk) != 0 ? 1u : 0u);
-        tc_commit(&bars->empty[s]);
+          mma_ts2(tmem_base, a_col + kk * 8, bdesc + 2 * kk, idesc, (it | kk) != 0 ? 1u : 0u);
+        tc_commit2_mc(&bars->empty[s], 0x3);
       }
       // Completion of every MMA issued above (also on the abort path, so TMEM
       // is never released under an in-flight MMA).
-      tc_commit(&bars->accum);
+      tc_commit2_mc(&bars->accum, 0x3);
       uint32_t dummy_abort = 0;
       mbar_wait(&bars->accum, 0, &dummy_abort, args.status, kStatusTimeoutAccum);
     }
   } else {
-    // ------------------------------------------------ dequant producers (128 threads)
+    // ----------------------------------- dequant producers (kGroups x 4 warps)
+    // Within a group: one warp per TMEM lane quarter decodes the whole stage
+    // for its 32 lanes.  Groups take turns on pairs of stages (one 128-wide
+    // scale group), so each warp has kGroups pair-times to hide its barrier,
+    // shared-memory and TMEM-store latencies.
+    const int dw = warp - 2;                   // dequant warp index
+    const int grp = dw >> 2;                   // stage-pair group of this warp
     const int quarter = warp & 3;              // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;       // lane within the 128-lane tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    float lut[16];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) lut[c] = __ldg(args.lut + c);
+    const uint32_t afull_leader = mapa_shared(smem_u32(&bars->afull[0]), 0);
+    const float* lut_s = bars->lut;
     bool ok = true;
 
     if (!kBwd) {
-      // Thread owns weight row n; each stage decodes 64 consecutive k of it.
+      // Thread owns weight row n; each stage it decodes the 64 k of the stage
+      // (32 TMEM columns).
       const int n = l0 + row;
       const bool valid = n < N;
       const float* srow = args.scales + static_cast<size_t>(valid ? n : 0) * groups_per_row;
-      float next_scale = valid ? __ldg(srow) : 0.0f;
-      ProductTable table;
-      for (int it = 0; it < n_iter && ok; ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        if (it >= kStages &&
-            !mbar_wait_warp(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
-          ok = false;
-          break;
+      float next_scale = (valid && 2 * grp < 2 * groups_per_row) ? __ldg(srow + grp) : 0.0f;
+      for (int pit = 2 * grp; pit < n_iter && ok; pit += 2 * kGroups) {
+        ProductTable table;
+        if (pit < n_main) {
+          table = make_table(lut_s, next_scale);
+          const int g_next = pit / 2 + kGroups;
+          next_scale = (valid && g_next < groups_per_row) ? __ldg(srow + g_next) : 0.0f;
         }
-        uint32_t v[32];
-        if (it < n_main) {
-          if ((it & 1) == 0) {  // new 128-element group every two stages
-            table = make_table(lut, next_scale);
-            const int g_next = it / 2 + 1;
-            next_scale = (valid && g_next < groups_per_row) ? __ldg(srow + g_next) : 0.0f;
+        for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (it >= kStages &&
+              !mbar_wait_warp(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
           }
           if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
             ok = false;
             break;
           }
-          const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + row * 32);
-          const uint4 q0 = q[0], q1 = q[1];
-          lookup8(table, q0.x, v + 0);
-          lookup8(table, q0.y, v + 4);
-          lookup8(table, q0.z, v + 8);
-          lookup8(table, q0.w, v + 12);
-          lookup8(table, q1.x, v + 16);
-          lookup8(table, q1.y, v + 20);
-          lookup8(table, q1.z, v + 24);
-          lookup8(table, q1.w, v + 28);
-        } else {
-          // LoRA stage: A row = bf16(Blora[n, 0:64]) zero padded past the rank.
+          uint32_t v[32];
+          if (it < n_main) {
+            const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + row * 32);
+            const uint4 q0 = q[0], q1 = q[1];
+            lookup8(table, q0.x, v + 0);
+            lookup8(table, q0.y, v + 4);
+            lookup8(table, q0.z, v + 8);
+            lookup8(table, q0.w, v + 12);
+            lookup8(table, q1.x, v + 16);
+            lookup8(table, q1.y, v + 20);
+            lookup8(table, q1.z, v + 24);
+            lookup8(table, q1.w, v + 28);
+          } else {
+            // LoRA stage: A row = bf16(Blora[n, 0:64]) zero padded past the rank.
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int c0 = 2 * j, c1 = 2 * j + 1;
-            const float a = (valid && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(n) * args.rank + c0) : 0.f;
-            const float b = (valid && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(n) * args.rank + c1) : 0.f;
-            v[j] = pack_bf16x2(a, b);
+            for (int j = 0; j < 32; ++j) {
+              const int c0 = 2 * j, c1 = c0 + 1;
+              const float a = (valid && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(n) * args.rank + c0) : 0.f;
+              const float b = (valid && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(n) * args.rank + c1) : 0.f;
+              v[j] = pack_bf16x2(a, b);
+            }
           }
+          tc_fence_after();
+          tmem_st_32x32b_x32(tmem_base + lane_addr + kAccCols + s * kAStageCols, v);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(afull_leader + s * 8);
         }
-        tc_fence_after();
-        tmem_st_32x32b_x32(tmem_base + lane_addr + kAccCols + s * kAStageCols, v);
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bars->afull[s]);
       }
     } else {
-      // Backward: lanes are W columns k, the stage reduces over 64 W rows n.
-      // Natural-orientation bytes are decoded into 8x8 bf16 blocks in mma
-      // fragment order, transposed in registers with movmatrix, and stored
-      // with the 16x256b TMEM shape.  Rows are visited in the order
+      // Backward: lanes are W columns k, the stage reduces over 64 W rows n
+      // (TMEM columns: n pairs).  Natural-orientation bytes are decoded into 8x8 bf16
+      // blocks in mma fragment order, transposed in registers with movmatrix, and
+      // stored with the 16x256b TMEM shape.  Rows are visited in the order
       // n = 16*cg + 4*(i/2) + (i%2) (+2 for odd pairs) so that after the
       // transpose each thread holds exactly the n pairs its TMEM columns need.
       const int i8 = lane >> 2;     // fragment row within an 8x8 block
       const int c4 = lane & 3;      // fragment column pair
       const int kq = quarter * 32;  // this warp's 32 k lanes inside the tile
-      const int g = l0 / 128;       // all 128 lanes share one scale group
-      for (int it = 0; it < n_iter && ok; ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        if (it >= kStages &&
-            !mbar_wait_warp(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
-          ok = false;
-          break;
-        }
-        if (it < n_main) {
-          const int nbase = it * kStageK;
-          float sc[8];
-#pragma unroll
-          for (int cg = 0; cg < 4; ++cg) {
-#pragma unroll
-            for (int odd = 0; odd < 2; ++odd) {
-              const int nr = 16 * cg + 4 * (i8 >> 1) + (i8 & 1) + 2 * odd;
-              sc[cg * 2 + odd] = __ldg(args.scales + static_cast<size_t>(nbase + nr) * groups_per_row + g);
-            }
-          }
-          if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+      // All 128 lanes share one scale group.  The second CTA of the last pair
+      // may lie entirely past K: it decodes zeros and stores nothing.
+      const bool tile_valid = l0 < K;
+      const int g = tile_valid ? l0 / 128 : 0;
+      const uint32_t sel = static_cast<uint32_t>(c4) | (static_cast<uint32_t>(c4 + 4) << 4);
+      auto row_of = [&](int cg, int odd) { return 16 * cg + 4 * (i8 >> 1) + (i8 & 1) + 2 * odd; };
+      for (int pit = 2 * grp; pit < n_iter && ok; pit += 2 * kGroups) {
+        for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (it >= kStages &&
+              !mbar_wait_warp(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
             ok = false;
             break;
           }
-          tc_fence_after();
+          if (it < n_main) {
+            float sc[8];
 #pragma unroll
-          for (int cg = 0; cg < 4; ++cg) {
-            uint32_t frag[2][4];  // [odd][byte slot]
+            for (int cg = 0; cg < 4; ++cg)
 #pragma unroll
-            for (int odd = 0; odd < 2; ++odd) {
-              const int nr = 16 * cg + 4 * (i8 >> 1) + (i8 & 1) + 2 * odd;
-              const uint4 seg = *reinterpret_cast<const uint4*>(qs + s * kQBytes + nr * 64 + kq / 2);
-              // bytes c4, 4+c4, 8+c4, 12+c4 of the 16-byte segment
-              const uint32_t sel = static_cast<uint32_t>(c4) | (static_cast<uint32_t>(c4 + 4) << 4);
-              const uint32_t b01 = prmt(seg.x, seg.y, sel);
-              const uint32_t b23 = prmt(seg.z, seg.w, sel);
-              const uint32_t bytes = prmt(b01, b23, 0x5410);
-              const float scale = sc[cg * 2 + odd];
+              for (int odd = 0; odd < 2; ++odd)
+                sc[cg * 2 + odd] =
+                    tile_valid ? __ldg(args.scales + static_cast<size_t>(it * kStageK + row_of(cg, odd)) * groups_per_row + g)
+                               : 0.0f;
+            if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll 1
+            for (int cg = 0; cg < 4; ++cg) {
+              uint32_t frag[2][4];  // [odd][byte slot]
 #pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                const uint32_t byte = (bytes >> (8 * b)) & 0xFFu;
-                const float lo = __fmul_rn(lut[byte & 15u], scale);
-                const float hi = __fmul_rn(lut[byte >> 4], scale);
-                frag[odd][b] = pack_bf16x2(lo, hi);
+              for (int odd = 0; odd < 2; ++odd) {
+                const uint4 seg = *reinterpret_cast<const uint4*>(qs + s * kQBytes + row_of(cg, odd) * 64 + kq / 2);
+                // bytes c4, 4+c4, 8+c4, 12+c4 of the 16-byte segment
+                const uint32_t bytes = prmt(prmt(seg.x, seg.y, sel), prmt(seg.z, seg.w, sel), 0x5410);
+                const float scale = sc[cg * 2 + odd];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                  const uint32_t byte = (bytes >> (8 * b)) & 0xFFu;
+                  const float lo = __fmul_rn(lut_s[byte & 15u], scale);
+                  const float hi = __fmul_rn(lut_s[byte >> 4], scale);
+                  frag[odd][b] = pack_bf16x2(lo, hi);
+                }
+              }
+              // byte slot b: (h = b/2, +8 k columns when b odd)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t r0 = movmatrix_trans(frag[0][2 * h + 0]);
+                const uint32_t r1 = movmatrix_trans(frag[1][2 * h + 0]);
+                const uint32_t r2 = movmatrix_trans(frag[0][2 * h + 1]);
+                const uint32_t r3 = movmatrix_trans(frag[1][2 * h + 1]);
+                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(kq + 16 * h) << 16) + kAccCols +
+                                       s * kAStageCols + cg * 8;
+                tmem_st_16x256b_x1(taddr, r0, r1, r2, r3);
               }
             }
-            // byte slot b: (h = b/2, +8 k columns when b odd)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint32_t r0 = movmatrix_trans(frag[0][2 * h + 0]);
-              const uint32_t r1 = movmatrix_trans(frag[1][2 * h + 0]);
-              const uint32_t r2 = movmatrix_trans(frag[0][2 * h + 1]);
-              const uint32_t r3 = movmatrix_trans(frag[1][2 * h + 1]);
-              const uint32_t taddr = tmem_base + (static_cast<uint32_t>(kq + 16 * h) << 16) + kAccCols +
-                                     s * kAStageCols + cg * 8;
-              tmem_st_16x256b_x1(taddr, r0, r1, r2, r3);
+          } else {
+            // LoRA stage: lane k holds bf16(Alora[0:64, k]) zero padded past the rank.
+            if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+              ok = false;
+              break;
             }
-          }
-        } else {
-          // LoRA stage: lane k holds bf16(Alora[0:64, k]) zero padded past the rank.
-          const int k = l0 + row;
-          uint32_t v[32];
+            const int k = l0 + row;
+            uint32_t v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int c0 = 2 * j, c1 = 2 * j + 1;
-            const float a = c0 < args.rank ? __ldg(args.lora + static_cast<size_t>(c0) * K + k) : 0.f;
-            const float b = c1 < args.rank ? __ldg(args.lora + static_cast<size_t>(c1) * K + k) : 0.f;
-            v[j] = pack_bf16x2(a, b);
+            for (int j = 0; j < 32; ++j) {
+              const int c0 = 2 * j, c1 = c0 + 1;
+              const float a = (k < K && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(c0) * K + k) : 0.f;
+              const float b = (k < K && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(c1) * K + k) : 0.f;
+              v[j] = pack_bf16x2(a, b);
+            }
+            tc_fence_after();
+            tmem_st_32x32b_x32(tmem_base + lane_addr + kAccCols + s * kAStageCols, v);
           }
-          tc_fence_after();
-          tmem_st_32x32b_x32(tmem_base + lane_addr + kAccCols + s * kAStageCols, v);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(afull_leader + s * 8);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bars->afull[s]);
       }
     }
+    // A group that stopped early (abort) must not leave others waiting forever:
+    // the bounded waits and the abort word end them.
+    ok = __all_sync(0xffffffffu, ok) != 0;
 
     // ------------------------------------------------------------ epilogue
+    // The kGroups warps of each lane quarter take the 32-column token chunks
+    // round robin.
     if (ok && mbar_wait_warp(&bars->accum, 0, abort_word, args.status, kStatusTimeoutAccum)) {
       tc_fence_after();
       const int l = l0 + row;
       const bool lvalid = l < L;
 #pragma unroll 1
-      for (int c = 0; c < kTok / 32; ++c) {
+      for (int c = 32 * grp; c < kTok; c += 32 * kGroups) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + c * 32, v);
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + c, v);
         tmem_wait_ld();
         if (lvalid) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int m = m0 + c * 32 + j;
+            const int m = m0 + c + j;
             if (m < M) args.out[static_cast<size_t>(m) * L + l] = __float2bfloat16_rn(__uint_as_float(v[j]));
           }
         }
@@ -342,10 +398,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs done with TMEM and with each other's barriers
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc2(tmem_base, kTmemCols);
   }
 }
 
@@ -401,10 +458,10 @@ int launch_tc_gemm(bool bwd, const void* act, const void* low, const uint8_t* co
   const int L = bwd ? K : N, R = bwd ? N : K;
   CUtensorMap tm_act, tm_low, tm_code;
   int rc = make_map_2d(&tm_act, act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, M, static_cast<uint64_t>(R) * 2, 64,
-                       256, CU_TENSOR_MAP_SWIZZLE_128B);
+                       kTokHalf, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (rank > 0) {
-    rc = make_map_2d(&tm_low, low, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, M, 128, 64, 256,
+    rc = make_map_2d(&tm_low, low, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, M, 128, 64, kTokHalf,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   } else {
@@ -427,16 +484,31 @@ int launch_tc_gemm(bool bwd, const void* act, const void* low, const uint8_t* co
   a.N = N;
   a.K = K;
   a.rank = rank;
-  dim3 grid((L + kLanes - 1) / kLanes, (M + kTok - 1) / kTok);
+  // CTA pairs along the W dimension: grid.x is even, each pair covers 256 W rows.
+  dim3 grid(2 * ((L + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t le;
   if (!bwd) {
-    static bool attr = false;
-    if (!attr) { if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(&fl_tc_gemm_kernel<false>)))) return rc; attr = true; }
-    fl_tc_gemm_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(tm_act, tm_low, tm_code, a);
+    static bool attr_set = false;
+    if (!attr_set) { if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(&fl_tc_gemm_kernel<false>)))) return rc; attr_set = true; }
+    le = cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<false>, tm_act, tm_low, tm_code, a);
   } else {
-    static bool attr = false;
-    if (!attr) { if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(&fl_tc_gemm_kernel<true>)))) return rc; attr = true; }
-    fl_tc_gemm_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(tm_act, tm_low, tm_code, a);
+    static bool attr_set = false;
+    if (!attr_set) { if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(&fl_tc_gemm_kernel<true>)))) return rc; attr_set = true; }
+    le = cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<true>, tm_act, tm_low, tm_code, a);
   }
+  if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "tc_gemm cluster launch: %s", cudaGetErrorString(le));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "tc_gemm launch: %s", cudaGetErrorString(e));
   return FL_OK;

@@ -3,7 +3,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
-#include "../../include/spilltune_b200.h"
+#include "spilltune_b200.h"
 
 namespace fl {
 

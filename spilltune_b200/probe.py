@@ -1,0 +1,62 @@
+"""Run one frozen-linear op at a given shape, for profiling and quick timing.
+
+    python -m spilltune_b200.probe --op fwd --M 8192 --N 14336 --K 4096 [--iters 3] [--time]
+
+Each call is preceded by two warm-up calls, so an `ncu -s 2 -c 1` capture
+selects the first measured launch.  --time prints CUDA-event timings instead.
+"""
+import argparse
+import json
+
+import torch
+
+from . import codec, ops
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--op", choices=["fwd", "bwd", "dequant"], default="fwd")
+    p.add_argument("--M", type=int, default=8192)
+    p.add_argument("--N", type=int, default=14336)
+    p.add_argument("--K", type=int, default=4096)
+    p.add_argument("--rank", type=int, default=16)
+    p.add_argument("--codec", default="nf4-g128")
+    p.add_argument("--iters", type=int, default=1)
+    p.add_argument("--time", action="store_true")
+    a = p.parse_args()
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = codec.encode(torch.randn(a.N, a.K, generator=g, device=dev) * 0.02, a.codec)
+    x = torch.randn(a.M, a.K, generator=g, device=dev).to(torch.bfloat16)
+    dy = torch.randn(a.M, a.N, generator=g, device=dev).to(torch.bfloat16)
+    A = torch.randn(a.rank, a.K, generator=g, device=dev) * 0.01 if a.rank else None
+    B = torch.randn(a.N, a.rank, generator=g, device=dev) * 0.01 if a.rank else None
+    out = torch.empty(a.N, a.K, dtype=torch.bfloat16, device=dev)
+    fn = {
+        "fwd": lambda: ops.fwd(x, w, A, B, 2.0),
+        "bwd": lambda: ops.bwd(dy, x, w, A, B, 2.0),
+        "dequant": lambda: ops.dequant(w, out=out),
+    }[a.op]
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    if not a.time:
+        for _ in range(a.iters):
+            fn()
+        torch.cuda.synchronize()
+        return
+    iters = max(a.iters, 10)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) / iters * 1e3
+    flops = 2.0 * a.M * a.N * a.K * (1 if a.op != "dequant" else 0)
+    print(json.dumps({"op": a.op, "M": a.M, "N": a.N, "K": a.K, "us": us,
+                      "tflops": flops / us / 1e6 if flops else None}))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,193 @@
+"""Packed-weight layer-slot streaming: pinned host records -> bounded VRAM slots.
+
+B200 counterpart of the reference's ``SlotSession.load`` (ram_vram_finetune/
+memory.py:188-275) and ``PrefetchSession`` (ram_vram_finetune/prefetch.py:47-252),
+extended to the compressed blocks ``PrefetchSession`` refuses today
+(prefetch.py:57-60):
+
+* the packed parts (payload + scales + codebook per projection) are copied as
+  they are stored — no decoded BF16 slot, no ``decode_into``: the fused
+  kernels read the slot directly;
+* copies run on a dedicated copy stream from pinned host memory, one layer
+  ahead of the consumer (forward: +1, backward: -1, prefetch.py:203-207);
+* a slot's ``ready`` event admits use on the compute stream (prefetch.py:197);
+  its ``consumed`` event, recorded after the whole consumer scope, admits the
+  next overwrite (prefetch.py:217-218);
+* no device-wide synchronize on the load path (memory.py:204-206 does one per load).
+
+Failures poison the session, like the reference's (prefetch.py:94-101).
+"""
+from contextlib import contextmanager
+import threading
+
+import torch
+
+from .codec import PackedWeight
+
+_ALIGN = 256
+
+
+def _align(n):
+    return (n + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+def layer_bytes(layer):
+    """Slot bytes for one layer (dict name -> PackedWeight), 256-byte aligned parts."""
+    total = 0
+    for w in layer.values():
+        total = _align(total) + w.payload.numel()
+        total = _align(total) + 4 * w.scales.numel()
+        total = _align(total) + 64
+    return _align(total)
+
+
+class PackedSlotSession:
+    """Two (or more) device slots fed from pinned host layers on a copy stream."""
+
+    def __init__(self, layers, device, *, slots=2, copy_stream=None):
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("unsupported_capability: slot streaming needs a CUDA device")
+        if not layers:
+            raise ValueError("slot streaming needs a nonempty ordered layer plan")
+        if slots < 2 and len(layers) > 1:
+            raise MemoryError("resource_budget: prefetch requires two slots for a multi-layer plan")
+        for layer in layers:
+            for name, w in layer.items():
+                if not isinstance(w, PackedWeight):
+                    raise TypeError(f"{name}: slot layers hold PackedWeight records")
+                for t in (w.payload, w.scales, w.lut):
+                    if t.device.type != "cpu" or not t.is_pinned() or not t.is_contiguous():
+                        raise ValueError("host records must be contiguous pinned CPU tensors")
+        self.layers = list(layers)
+        self.capacity = max(layer_bytes(layer) for layer in self.layers)
+        with torch.cuda.device(self.device):
+            self.copy_stream = copy_stream or torch.cuda.Stream(device=self.device)
+            self.slots = []
+            for i in range(min(slots, len(self.layers))):
+                buf = torch.empty(self.capacity, dtype=torch.uint8, device=self.device)
+                self.slots.append({"id": i, "buffer": buf, "layer": None, "ready": None, "consumed": None,
+                                   "active": False, "views": None})
+            self.copy_stream.wait_stream(torch.cuda.current_stream(self.device))
+        self.poisoned = False
+        self.closed = False
+        self.h2d_bytes = 0
+        self.uploads = 0
+        self.hits = 0
+        self.copy_events = []  # (start, end, bytes) per upload, for H2D GB/s
+        self._lock = threading.Lock()
+
+    # -------------------------------------------------------------- internals
+    def _views(self, slot, idx):
+        buf = slot["buffer"]
+        out = {}
+        off = 0
+        for name, w in self.layers[idx].items():
+            off = _align(off)
+            payload = buf.narrow(0, off, w.payload.numel())
+            off = _align(off + w.payload.numel())
+            scales = buf.narrow(0, off, 4 * w.scales.numel()).view(torch.float32)
+            off = _align(off + 4 * w.scales.numel())
+            lut = buf.narrow(0, off, 64).view(torch.float32)
+            off += 64
+            out[name] = PackedWeight(payload, scales, lut, w.shape, w.codec)
+        return out
+
+    def _find(self, idx):
+        return next((s for s in self.slots if s["layer"] == idx), None)
+
+    def _victim(self, keep=None):
+        free = [s for s in self.slots if not s["active"] and (keep is None or s["layer"] != keep)]
+        if not free:
+            raise RuntimeError("no inactive slot available")
+        # Prefer an empty slot, then the one consumed longest ago (lowest id tie-break).
+        return min(free, key=lambda s: (s["layer"] is not None, s.get("last_use", -1), s["id"]))
+
+    def _enqueue(self, idx, slot):
+        if slot["active"]:
+            raise RuntimeError("cannot overwrite an active consumer slot")
+        views = self._views(slot, idx)
+        src = self.layers[idx]
+        nbytes = 0
+        with torch.cuda.stream(self.copy_stream):
+            if slot["consumed"] is not None:
+                self.copy_stream.wait_event(slot["consumed"])
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(self.copy_stream)
+            for name, w in src.items():
+                v = views[name]
+                v.payload.copy_(w.payload, non_blocking=True)
+                v.scales.copy_(w.scales, non_blocking=True)
+                v.lut.copy_(w.lut, non_blocking=True)
+                nbytes += w.payload.numel() + 4 * w.scales.numel() + 64
+            end.record(self.copy_stream)
+        slot.update(layer=idx, ready=end, views=views)
+        self.copy_events.append((start, end, nbytes))
+        self.h2d_bytes += nbytes
+        self.uploads += 1
+
+    # -------------------------------------------------------------- public
+    @contextmanager
+    def borrow(self, idx, phase):
+        """Yield {name: PackedWeight} device views of layer `idx` for the current stream.
+
+        phase 'forward' prefetches idx+1, 'backward' prefetches idx-1.
+        """
+        if self.closed or self.poisoned:
+            raise RuntimeError("slot session is closed or poisoned")
+        if phase not in ("forward", "backward"):
+            raise ValueError("unknown slot consumer phase")
+        if not self._lock.acquire(blocking=False):
+            raise RuntimeError("concurrent/reentrant slot borrow is unsupported")
+        slot = None
+        try:
+            compute = torch.cuda.current_stream(self.device)
+            slot = self._find(idx)
+            if slot is None:
+                slot = self._victim()
+                self._enqueue(idx, slot)
+            else:
+                self.hits += 1
+            slot["active"] = True
+            compute.wait_event(slot["ready"])
+            nxt = idx + (1 if phase == "forward" else -1)
+            if 0 <= nxt < len(self.layers) and self._find(nxt) is None and len(self.slots) > 1:
+                self._enqueue(nxt, self._victim(keep=idx))
+            yield slot["views"]
+        except BaseException:
+            self.poisoned = True
+            raise
+        finally:
+            try:
+                if slot is not None and slot["active"]:
+                    ev = torch.cuda.Event()
+                    ev.record(torch.cuda.current_stream(self.device))
+                    slot["consumed"] = ev
+                    slot["active"] = False
+                    self._clock = getattr(self, "_clock", 0) + 1
+                    slot["last_use"] = self._clock
+            finally:
+                self._lock.release()
+
+    def h2d_seconds(self):
+        """Sum of copy-stream durations of completed uploads (synchronizes their events)."""
+        total = 0.0
+        for s, e, _ in self.copy_events:
+            e.synchronize()
+            total += s.elapsed_time(e) / 1e3
+        return total
+
+    def reset_stats(self):
+        self.copy_events.clear()
+        self.h2d_bytes = 0
+        self.uploads = 0
+        self.hits = 0
+
+    def close(self):
+        if self._lock.locked():
+            raise RuntimeError("cannot close an active slot session")
+        if not self.closed:
+            torch.cuda.synchronize(self.device)
+            self.slots.clear()
+            self.closed = True

@@ -96,6 +96,21 @@ int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t 
            uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace, size_t workspace_bytes,
            void* stream);
 
+/*
+ * Same result as fl_fwd, for callers that cannot allocate device memory at
+ * call time (a host binding without a device allocator, a trainer whose
+ * device budget is fixed up front).  No counterpart in the reference.  It
+ * allocates nothing: the scratch lives in a 4 MiB array of this library's own
+ * device memory (held on every GPU that loads the library), so M is limited to
+ * 32768 tokens when rank > 0 (FL_ERR_ARG beyond).  The first call on a device
+ * looks up that array's address; make it before any stream capture.  All calls
+ * on a device share the array: calls whose kernels overlap on the GPU race and
+ * must be serialised by the caller.
+ */
+int fl_fwd_noalloc(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, const float* scales,
+                   const float* lut16, int64_t N, const float* A, const float* B, int rank, float scale,
+                   uint16_t* Y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

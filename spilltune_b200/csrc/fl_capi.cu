@@ -122,7 +122,7 @@ int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, cons
     rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, workspace, st);
     if (rc) return rc;
   }
-  return launch_tc_gemm(false, X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st);
+  return launch_fwd_gemm(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st);
 }
 
 int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* payload,
@@ -151,7 +151,7 @@ int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t 
     // Ts = bf16(s * X . A^T): Q(j, k) = A[j * K + k]
     if ((rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, st))) return rc;
   }
-  if ((rc = launch_tc_gemm(true, dY, us, payload, scales, lut16, A, rank, dX, (int)M, (int)N, (int)K, status, st)))
+  if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, (int)M, (int)N, (int)K, status, st)))
     return rc;
   if (rank > 0) {
     // dA[j, k] = sum_m Us[m, j] X[m, k]

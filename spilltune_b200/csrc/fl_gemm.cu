@@ -1,21 +1,19 @@
 // Fused 4-bit dequantize -> tcgen05 BF16 GEMM with the LoRA branch folded into
-// the same TMEM accumulation.  One kernel template serves the forward and the
-// weight-gradient-free backward of the frozen projection:
+// the same TMEM accumulation, forward of the frozen projection:
 //
-//   forward  (kBwd = false):  Y [M,N]  = X  [M,K] . W^T    + Ts [M,r] . Blora^T
-//   backward (kBwd = true) :  dX[M,K]  = dY [M,N] . W      + Us [M,r] . Alora
+//   Y [M,N] = X [M,K] . W^T + Ts [M,r] . Blora^T
 //
+// (the backward lives in fl_gemm_bwd.cu)
 // with W[N,K] stored as the reference's group-128 record (payload uint8
 // [N*K/2], two codes per byte, scales fp32 [N*K/128]), Ts = bf16(s * X.Alora^T)
-// and Us = bf16(s * dY.Blora) produced by fl_lora.cu.  This replaces the
-// reference's decode_into + F.linear + FP32 LoRA F.linear pair
-// (ram_vram_finetune/finetune/lora.py:205-220, quantization/codecs.py:158-170)
-// and its autograd backward (training/recompute.py:85-127).
+// produced by fl_lora.cu.  This replaces the reference's decode_into + F.linear +
+// FP32 LoRA F.linear pair (ram_vram_finetune/finetune/lora.py:205-220,
+// quantization/codecs.py:158-170).
 //
 // Mapping onto the 5th-gen tensor core ("TS" form, A operand in TMEM), run by
 // a CTA pair (cluster of 2, tcgen05 cta_group::2):
-//   * MMA M (256 = 128 TMEM lanes in each CTA) runs over W rows (forward) or W
-//     columns (backward); MMA N (256) runs over tokens, each CTA holding the
+//   * MMA M (256 = 128 TMEM lanes in each CTA) runs over W rows; MMA N (256)
+//     runs over tokens, each CTA holding the
 //     shared-memory half of its 128 tokens; MMA K runs over the reduction dim
 //     in 64-wide stages.  The pair halves the activation bytes each SM loads
 //     and stores per FLOP compared with one CTA.
@@ -26,7 +24,7 @@
 //     with the 128-byte swizzle.
 //   * Packed codes arrive by TMA into a small shared-memory ring.
 //   * One extra stage appends the LoRA rank (<= 64) to the K dimension: A =
-//     bf16 LoRA factor rows, B = the scaled low-rank activations.
+//     bf16(Blora) rows, B = the scaled low-rank activations Ts.
 //   * D = 256 x 256 fp32 accumulator, 128 rows in each CTA's TMEM, read back by
 //     the dequant warps of that CTA.
 //
@@ -82,7 +80,6 @@ struct __align__(8) GemmBarriers {
 
 constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * (kXBytes + kQBytes) + sizeof(GemmBarriers);
 
-template <bool kBwd>
 __global__ void __launch_bounds__(kThreads, 1)
     fl_tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,   // X or dY, [M, R] bf16, box {64,256}
                       const __grid_constant__ CUtensorMap tm_low,   // Ts or Us, [M, 64] bf16, box {64,256}
@@ -97,8 +94,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int M = args.M, N = args.N, K = args.K;
-  const int L = kBwd ? K : N;   // output columns (TMEM lane dimension)
-  const int R = kBwd ? N : K;   // reduction dimension
+  const int L = N;   // output columns (TMEM lane dimension)
+  const int R = K;   // reduction dimension
   const int groups_per_row = K / 128;
   const uint32_t crank = cluster_ctarank();       // 0 = leader of the CTA pair
   // Grouped tile order: pairs that run at the same time cover a band of
@@ -163,10 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int r0 = it * kStageK;
           mbar_arrive_expect_tx(&bars->full[s], kXBytes + kQBytes);
           tma_load_2d(xs + s * kXBytes, &tm_act, r0, mh, &bars->full[s]);
-          if (!kBwd)
-            tma_load_2d(qs + s * kQBytes, &tm_code, r0 / 2, l0, &bars->full[s]);       // 128 rows x 32 B
-          else
-            tma_load_2d(qs + s * kQBytes, &tm_code, l0 / 2, r0, &bars->full[s]);       // 64 rows x 64 B
+          tma_load_2d(qs + s * kQBytes, &tm_code, r0 / 2, l0, &bars->full[s]);       // 128 rows x 32 B
         } else {
           mbar_arrive_expect_tx(&bars->full[s], kXBytes);
           tma_load_2d(xs + s * kXBytes, &tm_low, 0, mh, &bars->full[s]);
@@ -220,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* lut_s = bars->lut;
     bool ok = true;
 
-    if (!kBwd) {
+    {
       // Thread owns weight row n; each stage it decodes the 64 k of the stage
       // (32 TMEM columns).
       const int n = l0 + row;
@@ -270,98 +264,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           tmem_st_32x32b_x32(tmem_base + lane_addr + kAccCols + s * kAStageCols, v);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(afull_leader + s * 8);
-        }
-      }
-    } else {
-      // Backward: lanes are W columns k, the stage reduces over 64 W rows n
-      // (TMEM columns: n pairs).  Natural-orientation bytes are decoded into 8x8 bf16
-      // blocks in mma fragment order, transposed in registers with movmatrix, and
-      // stored with the 16x256b TMEM shape.  Rows are visited in the order
-      // n = 16*cg + 4*(i/2) + (i%2) (+2 for odd pairs) so that after the
-      // transpose each thread holds exactly the n pairs its TMEM columns need.
-      const int i8 = lane >> 2;     // fragment row within an 8x8 block
-      const int c4 = lane & 3;      // fragment column pair
-      const int kq = quarter * 32;  // this warp's 32 k lanes inside the tile
-      // All 128 lanes share one scale group.  The second CTA of the last pair
-      // may lie entirely past K: it decodes zeros and stores nothing.
-      const bool tile_valid = l0 < K;
-      const int g = tile_valid ? l0 / 128 : 0;
-      const uint32_t sel = static_cast<uint32_t>(c4) | (static_cast<uint32_t>(c4 + 4) << 4);
-      auto row_of = [&](int cg, int odd) { return 16 * cg + 4 * (i8 >> 1) + (i8 & 1) + 2 * odd; };
-      for (int pit = 2 * grp; pit < n_iter && ok; pit += 2 * kGroups) {
-        for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
-          if (it >= kStages &&
-              !mbar_wait_warp(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
-            ok = false;
-            break;
-          }
-          if (it < n_main) {
-            float sc[8];
-#pragma unroll
-            for (int cg = 0; cg < 4; ++cg)
-#pragma unroll
-              for (int odd = 0; odd < 2; ++odd)
-                sc[cg * 2 + odd] =
-                    tile_valid ? __ldg(args.scales + static_cast<size_t>(it * kStageK + row_of(cg, odd)) * groups_per_row + g)
-                               : 0.0f;
-            if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-#pragma unroll 1
-            for (int cg = 0; cg < 4; ++cg) {
-              uint32_t frag[2][4];  // [odd][byte slot]
-#pragma unroll
-              for (int odd = 0; odd < 2; ++odd) {
-                const uint4 seg = *reinterpret_cast<const uint4*>(qs + s * kQBytes + row_of(cg, odd) * 64 + kq / 2);
-                // bytes c4, 4+c4, 8+c4, 12+c4 of the 16-byte segment
-                const uint32_t bytes = prmt(prmt(seg.x, seg.y, sel), prmt(seg.z, seg.w, sel), 0x5410);
-                const float scale = sc[cg * 2 + odd];
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                  const uint32_t byte = (bytes >> (8 * b)) & 0xFFu;
-                  const float lo = __fmul_rn(lut_s[byte & 15u], scale);
-                  const float hi = __fmul_rn(lut_s[byte >> 4], scale);
-                  frag[odd][b] = pack_bf16x2(lo, hi);
-                }
-              }
-              // byte slot b: (h = b/2, +8 k columns when b odd)
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const uint32_t r0 = movmatrix_trans(frag[0][2 * h + 0]);
-                const uint32_t r1 = movmatrix_trans(frag[1][2 * h + 0]);
-                const uint32_t r2 = movmatrix_trans(frag[0][2 * h + 1]);
-                const uint32_t r3 = movmatrix_trans(frag[1][2 * h + 1]);
-                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(kq + 16 * h) << 16) + kAccCols +
-                                       s * kAStageCols + cg * 8;
-                tmem_st_16x256b_x1(taddr, r0, r1, r2, r3);
-              }
-            }
-          } else {
-            // LoRA stage: lane k holds bf16(Alora[0:64, k]) zero padded past the rank.
-            if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
-              ok = false;
-              break;
-            }
-            const int k = l0 + row;
-            uint32_t v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int c0 = 2 * j, c1 = c0 + 1;
-              const float a = (k < K && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(c0) * K + k) : 0.f;
-              const float b = (k < K && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(c1) * K + k) : 0.f;
-              v[j] = pack_bf16x2(a, b);
-            }
-            tc_fence_after();
-            tmem_st_32x32b_x32(tmem_base + lane_addr + kAccCols + s * kAStageCols, v);
-          }
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
@@ -428,64 +330,52 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
-                       uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
-                       uint32_t box_outer, CUtensorMapSwizzle swz) {
+int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
   auto fn = get_encode_fn();
   if (!fn) return set_error(FL_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  (void)elem_bytes;
   CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return FL_OK;
 }
 
-static int ensure_smem_attr(const void* kernel) {
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  return FL_OK;
-}
-
-// act: [M, R] bf16 activations; low: [M, 64] bf16 low-rank activations (may be
-// null when rank == 0); codes/scales: the frozen record; out: [M, L] bf16.
-int launch_tc_gemm(bool bwd, const void* act, const void* low, const uint8_t* codes, const float* scales,
-                   const float* lut, const float* lora, int rank, void* out, int M, int N, int K,
-                   uint32_t* status, cudaStream_t stream) {
-  const int L = bwd ? K : N, R = bwd ? N : K;
+// x: [M, K] bf16 activations; ts: [M, 64] bf16 scaled low-rank activations
+// (unused when rank == 0); codes/scales/lut: the frozen record W[N, K];
+// blora: [N, rank] fp32; y: [M, N] bf16.
+int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
+                    const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
+                    cudaStream_t stream) {
   CUtensorMap tm_act, tm_low, tm_code;
-  int rc = make_map_2d(&tm_act, act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, M, static_cast<uint64_t>(R) * 2, 64,
-                       kTokHalf, CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = make_tensor_map_2d(&tm_act, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, static_cast<uint64_t>(K) * 2, 64,
+                              kTokHalf, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (rank > 0) {
-    rc = make_map_2d(&tm_low, low, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, M, 128, 64, kTokHalf,
-                     CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = make_tensor_map_2d(&tm_low, ts, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 64, M, 128, 64, kTokHalf,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   } else {
     tm_low = tm_act;
   }
-  if (!bwd)
-    rc = make_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, K / 2, 32, 128,
-                     CU_TENSOR_MAP_SWIZZLE_NONE);
-  else
-    rc = make_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, K / 2, 64, 64,
-                     CU_TENSOR_MAP_SWIZZLE_NONE);
+  rc = make_tensor_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, 32, 128,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   GemmArgs a;
   a.scales = scales;
   a.lut = lut;
-  a.lora = lora;
-  a.out = static_cast<__nv_bfloat16*>(out);
+  a.lora = blora;
+  a.out = static_cast<__nv_bfloat16*>(y);
   a.status = status;
   a.M = M;
   a.N = N;
   a.K = K;
   a.rank = rank;
-  // CTA pairs along the W dimension: grid.x is even, each pair covers 256 W rows.
-  dim3 grid(2 * ((L + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok));
+  // CTA pairs: each pair covers 256 W rows x 256 tokens.
+  dim3 grid(2 * ((N + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
@@ -498,19 +388,15 @@ int launch_tc_gemm(bool bwd, const void* act, const void* low, const uint8_t* co
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t le;
-  if (!bwd) {
-    static bool attr_set = false;
-    if (!attr_set) { if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(&fl_tc_gemm_kernel<false>)))) return rc; attr_set = true; }
-    le = cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<false>, tm_act, tm_low, tm_code, a);
-  } else {
-    static bool attr_set = false;
-    if (!attr_set) { if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(&fl_tc_gemm_kernel<true>)))) return rc; attr_set = true; }
-    le = cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<true>, tm_act, tm_low, tm_code, a);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&fl_tc_gemm_kernel),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_set = true;
   }
-  if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "tc_gemm cluster launch: %s", cudaGetErrorString(le));
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "tc_gemm launch: %s", cudaGetErrorString(e));
+  cudaError_t le = cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel, tm_act, tm_low, tm_code, a);
+  if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "fwd gemm launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }
 

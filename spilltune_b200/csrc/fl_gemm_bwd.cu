@@ -1,0 +1,364 @@
+// Backward of the frozen projection (weight-gradient free), fused with the
+// 4-bit decode and the LoRA branch:
+//
+//   dX[M,K] = dY[M,N] . W[N,K] + Us[M,r] . Alora[r,K],   Us = bf16(s * dY . Blora)
+//
+// the autograd VJP the reference takes for F.linear(x, W) + the FP32 LoRA
+// F.linears inside StreamingBlockFunction.backward
+// (ram_vram_finetune/training/recompute.py:85-127, finetune/lora.py:218-220).
+//
+// Mapping (CTA pair, tcgen05 cta_group::2, both operands in shared memory):
+//   * MMA M = 256 tokens (128 per CTA; the A operand is the dY tile, TMA-loaded
+//     K-major with the 128-byte swizzle), N = 256 columns k of W (128 per CTA;
+//     the B operand), K = the reduction over W rows n in 64-wide stages.
+//   * B = W[n0:n0+64, kb:kb+128] is decoded in its stored orientation: a thread
+//     owns one row n and 64 consecutive k, builds that row's 16-entry product
+//     table once (bit-identical to decode_into), looks codes up four at a time
+//     with prmt and writes 128-byte rows of the MN-major 128-byte-swizzled
+//     operand layout.  No transpose is needed.
+//   * Every accumulator lane is one token row of dX, so the epilogue writes 64
+//     contiguous bytes per thread per 32-column chunk.
+//   * The extra LoRA stage uses A = the Us tile, B = bf16(Alora[0:64, k]).
+// Warp roles (448 threads per CTA): warp 0 TMA producer, warp 1 TMEM owner (both
+// CTAs) + MMA issuer (leader), warps 2-13 three groups of four decode warps that
+// take turns on stages, then the epilogue.  Barriers as in fl_gemm.cu.
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "fl_codebook.cuh"
+#include "fl_ptx.cuh"
+
+namespace fl {
+namespace bwd {
+
+constexpr int kTokHalf = 128;              // tokens per CTA (A rows)
+constexpr int kColHalf = 128;              // W columns k per CTA (B rows)
+constexpr int kStageN = 64;                // reduction rows n per stage
+constexpr int kStages = 6;
+constexpr int kGroupM = 8;                 // token tiles per band of the grouped tile order
+constexpr int kGroups = 3;                 // decode warp groups
+constexpr int kThreads = 64 + 128 * kGroups;
+constexpr int kAccCols = 256;              // fp32 accumulator columns (pair N)
+constexpr int kTmemCols = 256;
+constexpr int kABytes = kTokHalf * kStageN * 2;   // 16 KiB dY (or Us) tile
+constexpr int kBBytes = kColHalf * kStageN * 2;   // 16 KiB decoded W tile
+constexpr int kQBytes = kStageN * kColHalf / 2;   // 4 KiB packed codes
+constexpr uint32_t kBLbo = 1024;           // MN-direction atom stride (64 k per atom)
+constexpr uint32_t kBSbo = 2048;           // K-direction 8-row group stride
+
+struct __align__(8) Barriers {
+  uint64_t full[kStages];
+  uint64_t afull[kStages];
+  uint64_t empty[kStages];
+  uint64_t accum;
+  uint32_t tmem_base;
+  uint32_t abort_word;
+  alignas(16) float lut[16];
+};
+
+constexpr int kSmemBytes = 1024 + kStages * (kABytes + kBBytes + kQBytes) + sizeof(Barriers);
+
+struct Args {
+  const float* scales;
+  const float* lut;
+  const float* alora;   // [r, K]
+  __nv_bfloat16* out;   // dX [M, K]
+  uint32_t* status;
+  int M, N, K, rank;
+};
+
+// Byte offset of 16-byte chunk j (k = 8j..8j+7 within the CTA's 64-k half
+// `khalf`) of reduction row r in the MN-major swizzled B tile.
+__device__ __forceinline__ uint32_t b_offset(int r, int khalf, int j) {
+  return khalf * kBLbo + (r >> 3) * kBSbo + (r & 7) * 128 + ((j ^ (r & 7)) << 4);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fl_bwd_ss_kernel(const __grid_constant__ CUtensorMap tm_dy,    // dY [M, N] bf16, box {64, 128}
+                     const __grid_constant__ CUtensorMap tm_us,    // Us [M, 64] bf16, box {64, 128}
+                     const __grid_constant__ CUtensorMap tm_code,  // payload [N, K/2] u8, box {64, 64}
+                     const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* as = smem;                                  // kStages x 16 KiB
+  uint8_t* bs = as + kStages * kABytes;                // kStages x 16 KiB
+  uint8_t* qs = bs + kStages * kBBytes;                // kStages x 4 KiB
+  Barriers* bars = reinterpret_cast<Barriers*>(qs + kStages * kQBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int M = args.M, N = args.N, K = args.K;
+  const int groups_per_row = K / 128;
+  const uint32_t crank = cluster_ctarank();
+  int k_tile, m_tile;
+  {
+    const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
+    const int num_m = (M + 2 * kTokHalf - 1) / (2 * kTokHalf);
+    const int pair = blockIdx.x >> 1;
+    const int band = pair / (kGroupM * num_k);
+    const int first_m = band * kGroupM;
+    const int rows_in_band = min(kGroupM, num_m - first_m);
+    const int local = pair - band * kGroupM * num_k;
+    m_tile = first_m + local % rows_in_band;
+    k_tile = local / rows_in_band;
+  }
+  const int k0 = k_tile * 2 * kColHalf;                       // first column of the pair tile
+  const int kb = k0 + static_cast<int>(crank) * kColHalf;     // first column of this CTA's B half
+  const int m0 = m_tile * 2 * kTokHalf;                       // first token of the pair tile
+  const int mh = m0 + static_cast<int>(crank) * kTokHalf;     // first token of this CTA's A half
+  const int n_main = N / kStageN;
+  const bool has_lora = args.rank > 0;
+  const int n_iter = n_main + (has_lora ? 1 : 0);
+  volatile uint32_t* abort_word = &bars->abort_word;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->afull[s], 2 * 4);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->accum, 1);
+    bars->abort_word = 0;
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 16) bars->lut[threadIdx.x] = __ldg(args.lut + threadIdx.x);
+  if (warp == 1) {
+    tmem_alloc2(&bars->tmem_base, kTmemCols);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_dy);
+      tma_prefetch_desc(&tm_code);
+      if (has_lora) tma_prefetch_desc(&tm_us);
+      int issued = 0;
+      for (int it = 0; it < n_iter; ++it) {
+        const int s = it % kStages;
+        if (it >= kStages &&
+            !mbar_wait(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty))
+          break;
+        if (it < n_main) {
+          const int n0 = it * kStageN;
+          mbar_arrive_expect_tx(&bars->full[s], kABytes + kQBytes);
+          tma_load_2d(as + s * kABytes, &tm_dy, n0, mh, &bars->full[s]);
+          tma_load_2d(qs + s * kQBytes, &tm_code, kb / 2, n0, &bars->full[s]);
+        } else {
+          mbar_arrive_expect_tx(&bars->full[s], kABytes);
+          tma_load_2d(as + s * kABytes, &tm_us, 0, mh, &bars->full[s]);
+        }
+        ++issued;
+      }
+      for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i) {
+        uint32_t dummy_abort = 0;
+        mbar_wait(&bars->full[i % kStages], (i / kStages) & 1, &dummy_abort, args.status, kStatusTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (lane == 0 && crank == 0) {
+      const uint32_t idesc = idesc_bf16_f32_bmn(2 * kTokHalf, 2 * kColHalf);
+      const int lora_k_steps = (args.rank + 15) / 16;
+      for (int it = 0; it < n_iter; ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        if (!mbar_wait_cluster(&bars->afull[s], ph, abort_word, args.status, kStatusTimeoutFull)) break;
+        tc_fence_after();
+        const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(as + s * kABytes));
+        const uint64_t bdesc = sdesc_mnmajor_sw128(smem_u32(bs + s * kBBytes), kBLbo, kBSbo);
+        const int ksteps = it < n_main ? kStageN / 16 : lora_k_steps;
+        for (int kk = 0; kk < ksteps; ++kk)
+          mma_ss2(tmem_base, adesc + 2 * kk, bdesc + ((2 * kBSbo) >> 4) * kk, idesc, (it | kk) != 0 ? 1u : 0u);
+        tc_commit2_mc(&bars->empty[s], 0x3);
+      }
+      tc_commit2_mc(&bars->accum, 0x3);
+      uint32_t dummy_abort = 0;
+      mbar_wait(&bars->accum, 0, &dummy_abort, args.status, kStatusTimeoutAccum);
+    }
+  } else {
+    // ------------------------------------------------------------ decode warps
+    const int dw = warp - 2;
+    const int grp = dw >> 2;                 // stage-pair group
+    const int t = (dw & 3) * 32 + lane;      // 0..127 within the group
+    const int r = t >> 1;                    // reduction row within the stage (0..63)
+    const int khalf = t & 1;                 // which 64 of the CTA's 128 columns
+    const uint32_t afull_leader = mapa_shared(smem_u32(&bars->afull[0]), 0);
+    const bool tile_valid = kb < K;
+    const int g = tile_valid ? kb / 128 : 0;  // the CTA's 128 columns share one scale group
+    bool ok = true;
+    // The row's scale for the next stage this group owns is loaded one owned
+    // stage ahead (stages 2g, 2g+1, 2g+2*kGroups, ...).
+    auto load_scale = [&](int it) {
+      return (tile_valid && it < n_main) ? __ldg(args.scales + static_cast<size_t>(it * kStageN + r) * groups_per_row + g)
+                                         : 0.0f;
+    };
+    float next_scale = load_scale(2 * grp);
+    for (int pit = 2 * grp; pit < n_iter && ok; pit += 2 * kGroups) {
+      for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        if (it >= kStages &&
+            !mbar_wait_warp(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        uint32_t v[32];
+        const float scale = next_scale;
+        next_scale = load_scale((it & 1) == 0 ? it + 1 : it + 2 * kGroups - 1);
+        if (it < n_main) {
+          const ProductTable table = make_table(bars->lut, scale);
+          if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + r * 64 + khalf * 32);
+          const uint4 q0 = q[0], q1 = q[1];
+          lookup8(table, q0.x, v + 0);
+          lookup8(table, q0.y, v + 4);
+          lookup8(table, q0.z, v + 8);
+          lookup8(table, q0.w, v + 12);
+          lookup8(table, q1.x, v + 16);
+          lookup8(table, q1.y, v + 20);
+          lookup8(table, q1.z, v + 24);
+          lookup8(table, q1.w, v + 28);
+        } else {
+          // LoRA stage: row r of B is bf16(Alora[r, kb + 64*khalf .. +64]), zero past the rank.
+          if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          const bool live = tile_valid && r < args.rank;
+          const float* src = args.alora + static_cast<size_t>(live ? r : 0) * K + kb + 64 * khalf;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float2 a = make_float2(0.f, 0.f);
+            if (live) a = __ldg(reinterpret_cast<const float2*>(src) + j);
+            v[j] = pack_bf16x2(a.x, a.y);
+          }
+        }
+        uint8_t* dst = bs + s * kBBytes;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<uint4*>(dst + b_offset(r, khalf, j)) = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(afull_leader + s * 8);
+      }
+    }
+    ok = __all_sync(0xffffffffu, ok) != 0;
+
+    // ------------------------------------------------------------ epilogue
+    // Lane quarter q holds tokens mh + 32q .. +32; each thread writes its token
+    // row's columns in 32-wide chunks, the groups taking chunks round robin.
+    const int quarter = warp & 3;
+    const int m = mh + quarter * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    if (ok && mbar_wait_warp(&bars->accum, 0, abort_word, args.status, kStatusTimeoutAccum)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 32 * grp; c < kAccCols; c += 32 * kGroups) {
+        uint32_t acc[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + c, acc);
+        tmem_wait_ld();
+        const int kcol = k0 + c;
+        if (m < M && kcol < K) {
+          uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(m) * K + kcol);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 o;
+            o.x = pack_bf16x2(__uint_as_float(acc[8 * j + 0]), __uint_as_float(acc[8 * j + 1]));
+            o.y = pack_bf16x2(__uint_as_float(acc[8 * j + 2]), __uint_as_float(acc[8 * j + 3]));
+            o.z = pack_bf16x2(__uint_as_float(acc[8 * j + 4]), __uint_as_float(acc[8 * j + 5]));
+            o.w = pack_bf16x2(__uint_as_float(acc[8 * j + 6]), __uint_as_float(acc[8 * j + 7]));
+            dst[j] = o;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace bwd
+}  // namespace fl
+
+// ------------------------------------------------------------------ host side
+#include <cuda_runtime.h>
+
+#include "fl_host.h"
+
+namespace fl {
+
+int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+
+int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
+                    const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
+                    cudaStream_t stream) {
+  using namespace bwd;
+  if ((K * 2) % 16 != 0 || N % kStageN != 0 || K % 128 != 0)
+    return set_error(FL_ERR_ARG, "bwd gemm: needs N %% 64 == 0 and K %% 128 == 0");
+  CUtensorMap tm_dy, tm_us, tm_code;
+  int rc = make_tensor_map_2d(&tm_dy, dy, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, static_cast<uint64_t>(N) * 2, 64,
+                              kTokHalf, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (rank > 0) {
+    rc = make_tensor_map_2d(&tm_us, us, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 64, M, 128, 64, kTokHalf,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  } else {
+    tm_us = tm_dy;
+  }
+  rc = make_tensor_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, kColHalf / 2, kStageN,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  Args a;
+  a.scales = scales;
+  a.lut = lut;
+  a.alora = alora;
+  a.out = static_cast<__nv_bfloat16*>(dx);
+  a.status = status;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.rank = rank;
+  const int pairs = ((K + 2 * kColHalf - 1) / (2 * kColHalf)) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&fl_bwd_ss_kernel),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_set = true;
+  }
+  cudaError_t le = cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel, tm_dy, tm_us, tm_code, a);
+  if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "bwd gemm launch: %s", cudaGetErrorString(le));
+  return FL_OK;
+}
+
+}  // namespace fl

@@ -12,9 +12,15 @@ int set_error(int code, const char* fmt, ...);
 
 uint32_t* status_word(int device);  // device status word of the calling device
 
-int launch_tc_gemm(bool bwd, const void* act, const void* low, const uint8_t* codes, const float* scales,
-                   const float* lut, const float* lora, int rank, void* out, int M, int N, int K,
-                   uint32_t* status, cudaStream_t stream);
+// Y[M,N] = X . W^T + Ts . Blora^T (fl_gemm.cu).
+int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
+                    const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
+                    cudaStream_t stream);
+
+// dX[M,K] = dY . W + Us . Alora (fl_gemm_bwd.cu).
+int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
+                    const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
+                    cudaStream_t stream);
 
 int launch_dequant(const uint8_t* payload, const float* scales, const float* lut, int64_t numel, void* out,
                    cudaStream_t stream);

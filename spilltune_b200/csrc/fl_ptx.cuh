@@ -293,6 +293,38 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// UMMA shared-memory descriptor, MN-major operand with the 128-byte swizzle:
+// 8 rows of 128 bytes (64 bf16 along MN) form a 1024-byte atom; atoms along MN
+// are `lbo` bytes apart, groups of 8 rows along K are `sbo` bytes apart.  The
+// 16-byte chunk j of row r sits at chunk position j ^ (r % 8) inside the atom.
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Pair MMA with both operands in shared memory (A: M/2 rows per CTA, B: N/2
+// rows per CTA, each at the same offset in both CTAs).
+__device__ __forceinline__ void mma_ss2(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (tensor core, TMA) before a barrier hands them over.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Instruction descriptor, kind::f16 with bf16 A/B, fp32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
   return (1u << 4)                                   // D format f32
@@ -301,6 +333,9 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
          | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
+
+// Same with the B operand MN-major.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int m, int n) { return idesc_bf16_f32(m, n) | (1u << 16); }
 
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

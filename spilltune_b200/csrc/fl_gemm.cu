@@ -68,7 +68,7 @@ struct GemmArgs {
   int rank;             // 0 disables the LoRA stage
 };
 
-struct __align__(8) GemmBarriers {
+struct __align__(16) GemmBarriers {
   uint64_t full[kStages];   // TMA bytes landed
   uint64_t afull[kStages];  // leader: both CTAs' dequant warps finished the TMEM A stage
   uint64_t empty[kStages];  // MMAs reading the stage completed
@@ -334,6 +334,12 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
   auto fn = get_encode_fn();
   if (!fn) return set_error(FL_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  // The encode is a driver call: make the runtime's current device's primary
+  // context current on this thread first (e.g. torch's autograd worker thread
+  // may not have touched the runtime yet).
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess)
+    return set_error(FL_ERR_CUDA, "no current CUDA device for the tensor map");
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};

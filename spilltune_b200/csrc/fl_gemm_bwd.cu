@@ -35,7 +35,7 @@ constexpr int kTokHalf = 128;              // tokens per CTA (A rows)
 constexpr int kColHalf = 128;              // W columns k per CTA (B rows)
 constexpr int kStageN = 64;                // reduction rows n per stage
 constexpr int kStages = 6;
-constexpr int kGroupM = 8;                 // token tiles per band of the grouped tile order
+constexpr int kGroupM = 4;                 // token tiles per band: a band's pairs fit in one wave, so each dY slab is read once
 constexpr int kGroups = 3;                 // decode warp groups
 constexpr int kThreads = 64 + 128 * kGroups;
 constexpr int kAccCols = 256;              // fp32 accumulator columns (pair N)
@@ -46,7 +46,7 @@ constexpr int kQBytes = kStageN * kColHalf / 2;   // 4 KiB packed codes
 constexpr uint32_t kBLbo = 1024;           // MN-direction atom stride (64 k per atom)
 constexpr uint32_t kBSbo = 2048;           // K-direction 8-row group stride
 
-struct __align__(8) Barriers {
+struct __align__(16) Barriers {
   uint64_t full[kStages];
   uint64_t afull[kStages];
   uint64_t empty[kStages];

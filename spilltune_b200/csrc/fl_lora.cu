@@ -1,18 +1,15 @@
-// Low-rank (LoRA) side kernels of the frozen projection.
+// LoRA weight gradients of the frozen projection (lora_down lives in
+// fl_lora_down.cu):
 //
-//   lora_down : Lo[m, j] = bf16(s * sum_r P[m, r] * Q(j, r)),  j < rank (<= 64),
-//               zero for rank <= j < 64.  Forward: P = X, Q = Alora  -> Ts.
-//               Backward: P = dY, Q = Blora^T -> Us.
-//               (reference: the FP32 F.linear(x.float(), A) and its VJP
-//               dY.float() @ B, finetune/lora.py:219, training/recompute.py:102)
 //   lora_grad : out(p, j) (+)= sum_m P[m, p] * Lo[m, j]          (fp32 out)
-//               dA = Us^T . X  (P = X),  dB = dY^T . Ts (P = dY).
+//               dA = Us^T . X  (P = X),  dB = dY^T . Ts (P = dY)
+//   (reference: the FP32 autograd of F.linear(F.linear(x.float(), A), B),
+//   training/recompute.py:102-127)
 //
-// Both are skinny reductions that stream one large BF16 activation once; they
-// run on the warp-level BF16 tensor-core path (mma.sync m16n8k16, fp32
-// accumulate).  The FP32 LoRA factors enter as a BF16 hi/lo pair (two MMAs),
-// keeping ~16 mantissa bits of the factor; the reduction dimension is permuted
-// consistently on both operands so that every thread reads 16-byte vectors.
+// A skinny reduction over tokens that streams one large BF16 activation once,
+// on the warp-level BF16 tensor-core path (mma.sync m16n8k16, fp32
+// accumulate); movmatrix turns row-major activation tiles into the transposed
+// fragments the reduction over tokens needs.
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -35,89 +32,6 @@ __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uin
   hi = pack_bf16x2(x0, x1);
   const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xFFFF0000u);
   lo = pack_bf16x2(x0 - h0, x1 - h1);
-}
-
-// ---------------------------------------------------------------- lora_down
-// CTA = 4 warps on the same 16 rows; warp w reduces the r-slice w of every
-// 32-wide chunk; partial sums meet in shared memory.  Thread (g = lane/4,
-// c = lane%4) loads 8 consecutive elements of rows g and g+8; the 32 chunk
-// positions are assigned to MMA k-slots as (step q, slot 2c[+1]) -> r = 8c+4q
-// [+1], (slot 2c+8[+9]) -> r = 8c+4q+2[+3], and the Q fragment uses the same map.
-template <int JT>  // number of 8-wide rank tiles (rank <= 8*JT)
-__global__ void __launch_bounds__(128) lora_down_kernel(const __nv_bfloat16* __restrict__ P, int M, int R,
-                                                        const float* __restrict__ q, int64_t q_sj, int64_t q_sr,
-                                                        int rank, float s, __nv_bfloat16* __restrict__ out) {
-  __shared__ float red[4][16][8 * JT + 1];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, c = lane & 3;
-  const int m0 = blockIdx.x * 16;
-  float acc[JT][4];
-#pragma unroll
-  for (int t = 0; t < JT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
-  const int rowA = min(m0 + g, M - 1), rowB = min(m0 + g + 8, M - 1);
-  const __nv_bfloat16* pa = P + static_cast<size_t>(rowA) * R;
-  const __nv_bfloat16* pb = P + static_cast<size_t>(rowB) * R;
-  for (int r0 = warp * 32; r0 < R; r0 += 128) {
-    const uint4 xa = __ldg(reinterpret_cast<const uint4*>(pa + r0 + 8 * c));
-    const uint4 xb = __ldg(reinterpret_cast<const uint4*>(pb + r0 + 8 * c));
-    const uint32_t wa[4] = {xa.x, xa.y, xa.z, xa.w};
-    const uint32_t wb[4] = {xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-    for (int t = 0; t < JT; ++t) {
-      const int j = t * 8 + g;
-      float qv[8];
-      if (j < rank) {
-        const float* qp = q + j * q_sj + static_cast<int64_t>(r0 + 8 * c) * q_sr;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) qv[e] = __ldg(qp + e * q_sr);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) qv[e] = 0.f;
-      }
-#pragma unroll
-      for (int qs = 0; qs < 2; ++qs) {
-        uint32_t bh0, bl0, bh1, bl1;
-        split_pair(qv[4 * qs + 0], qv[4 * qs + 1], bh0, bl0);
-        split_pair(qv[4 * qs + 2], qv[4 * qs + 3], bh1, bl1);
-        mma_bf16_16816(acc[t], wa[2 * qs], wb[2 * qs], wa[2 * qs + 1], wb[2 * qs + 1], bh0, bh1);
-        mma_bf16_16816(acc[t], wa[2 * qs], wb[2 * qs], wa[2 * qs + 1], wb[2 * qs + 1], bl0, bl1);
-      }
-    }
-  }
-#pragma unroll
-  for (int t = 0; t < JT; ++t) {
-    red[warp][g][t * 8 + 2 * c] = acc[t][0];
-    red[warp][g][t * 8 + 2 * c + 1] = acc[t][1];
-    red[warp][g + 8][t * 8 + 2 * c] = acc[t][2];
-    red[warp][g + 8][t * 8 + 2 * c + 1] = acc[t][3];
-  }
-  __syncthreads();
-  // 16 rows x 64 output columns (bf16), zero past the rank / past 8*JT.
-  for (int idx = threadIdx.x; idx < 16 * 64; idx += 128) {
-    const int rr = idx >> 6, j = idx & 63;
-    const int m = m0 + rr;
-    if (m >= M) continue;
-    float v = 0.f;
-    if (j < rank && j < 8 * JT) v = s * (red[0][rr][j] + red[1][rr][j] + red[2][rr][j] + red[3][rr][j]);
-    out[static_cast<size_t>(m) * 64 + j] = __float2bfloat16_rn(v);
-  }
-}
-
-int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank, float s,
-                     void* out64, cudaStream_t stream) {
-  if (R % 128 != 0) return set_error(FL_ERR_ARG, "lora_down: reduction dim %d not a multiple of 128", R);
-  dim3 grid((M + 15) / 16);
-  auto p = static_cast<const __nv_bfloat16*>(P);
-  auto o = static_cast<__nv_bfloat16*>(out64);
-  if (rank <= 16)
-    lora_down_kernel<2><<<grid, 128, 0, stream>>>(p, M, R, q, q_sj, q_sr, rank, s, o);
-  else if (rank <= 32)
-    lora_down_kernel<4><<<grid, 128, 0, stream>>>(p, M, R, q, q_sj, q_sr, rank, s, o);
-  else
-    lora_down_kernel<8><<<grid, 128, 0, stream>>>(p, M, R, q, q_sj, q_sr, rank, s, o);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down launch: %s", cudaGetErrorString(e));
-  return FL_OK;
 }
 
 // ---------------------------------------------------------------- lora_grad

@@ -184,3 +184,25 @@ def test_no_kernel_reported_timeouts(cuda_lib):
     v = ctypes.c_uint32(0)
     assert cuda_lib.fl_status(0, ctypes.byref(v)) == 0
     assert v.value == 0
+
+
+def test_backward_from_a_fresh_thread(cuda_lib):
+    """torch runs CUDA backward on its autograd worker thread; the ops must not
+    depend on a CUDA context already being current there."""
+    import threading
+    from spilltune_b200 import ops
+    pw, x, A, B, dy = _problem(256, 256, 256, 16, "nf4-g128", seed=9)
+    pw, x, A, B, dy = pw.to("cuda"), x.cuda(), A.cuda(), B.cuda(), dy.cuda()
+    ref = ops.bwd(dy, x, pw, A, B, 2.0)
+    torch.cuda.synchronize()
+    out = {}
+
+    def work():
+        out["r"] = ops.bwd(dy, x, pw, A, B, 2.0)
+        torch.cuda.synchronize()
+
+    t = threading.Thread(target=work)
+    t.start()
+    t.join()
+    for a, b in zip(out["r"], ref):
+        assert ol.rel_l2(a.cpu(), b.cpu()) < 1e-6

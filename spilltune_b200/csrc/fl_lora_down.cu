@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int it = 0; it < n_iter; ++it) {
         const int st = it % C::kStages;
         if (it >= C::kStages &&
-            !mbar_wait(&bars->empty[st], ((it / C::kStages) - 1) & 1, abort_word, status, kStatusTimeoutEmpty))
+            !mbar_wait_short(&bars->empty[st], ((it / C::kStages) - 1) & 1, abort_word, status, kStatusTimeoutEmpty))
           break;
         mbar_arrive_expect_tx(&bars->pfull[st], kPBytes);
         tma_load_2d(ps + st * kPBytes, &tm_p, (c_begin + it) * kStageR, m0, &bars->pfull[st]);
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int i = issued > C::kStages ? issued - C::kStages : 0; i < issued; ++i) {
         uint32_t dummy = 0;
-        mbar_wait(&bars->pfull[i % C::kStages], (i / C::kStages) & 1, &dummy, status, kStatusTimeoutDrain);
+        mbar_wait_short(&bars->pfull[i % C::kStages], (i / C::kStages) & 1, &dummy, status, kStatusTimeoutDrain);
       }
     }
   } else if (warp == 1) {
@@ -114,8 +114,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int it = 0; it < n_iter; ++it) {
         const int st = it % C::kStages;
         const uint32_t ph = (it / C::kStages) & 1;
-        if (!mbar_wait(&bars->pfull[st], ph, abort_word, status, kStatusTimeoutFull)) break;
-        if (!mbar_wait(&bars->qfull[st], ph, abort_word, status, kStatusTimeoutFull)) break;
+        if (!mbar_wait_short(&bars->pfull[st], ph, abort_word, status, kStatusTimeoutFull)) break;
+        if (!mbar_wait_short(&bars->qfull[st], ph, abort_word, status, kStatusTimeoutFull)) break;
         tc_fence_after();
         const uint64_t pd = sdesc_kmajor_sw128(smem_u32(ps + st * kPBytes));
         const uint64_t hd = sdesc_kmajor_sw128(smem_u32(qh + st * C::kQBytes));
@@ -128,43 +128,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_commit(&bars->accum);
       uint32_t dummy = 0;
-      mbar_wait(&bars->accum, 0, &dummy, status, kStatusTimeoutAccum);
+      mbar_wait_short(&bars->accum, 0, &dummy, status, kStatusTimeoutAccum);
     }
   } else {
     // Factor converters: chunk (j, 8 consecutive r) -> 16-byte hi and lo pieces
-    // at row j, chunk position c ^ (j % 8) of the 128-byte-swizzled tile.
+    // at row j, chunk position c ^ (j % 8) of the 128-byte-swizzled tile.  The
+    // FP32 chunks of the next kAhead stages are loaded into registers before the
+    // current one is converted, so the global-load latency overlaps.
+    constexpr int kPer = NQ / 8;                 // chunks per thread per stage (NQ*8 chunks, 64 threads)
+    constexpr int kAhead = NQ <= 32 ? 2 : 1;
     const int t = threadIdx.x - 64;
-    for (int it = 0; it < n_iter && ok; ++it) {
-      const int st = it % C::kStages;
-      if (it >= C::kStages &&
-          !mbar_wait_warp(&bars->empty[st], ((it / C::kStages) - 1) & 1, abort_word, status, kStatusTimeoutEmpty)) {
-        ok = false;
-        break;
-      }
+    float buf[kAhead + 1][kPer][8];
+    auto fetch = [&](int it, float (&v)[kPer][8]) {
       const int r0 = (c_begin + it) * kStageR;
-      for (int idx = t; idx < NQ * 8; idx += 64) {
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int idx = t + 64 * u;
         const int j = idx >> 3, c = idx & 7;
-        float v[8];
-        if (j < rank) {
+        if (it < n_iter && j < rank) {
           const float* src = q + j * q_sj + static_cast<int64_t>(r0 + 8 * c) * q_sr;
           if (q_sr == 1) {
             const float4 a = __ldg(reinterpret_cast<const float4*>(src));
             const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
+            v[u][4] = b.x; v[u][5] = b.y; v[u][6] = b.z; v[u][7] = b.w;
           } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __ldg(src + e * q_sr);
+            for (int e = 0; e < 8; ++e) v[u][e] = __ldg(src + e * q_sr);
           }
         } else {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = 0.f;
+          for (int e = 0; e < 8; ++e) v[u][e] = 0.f;
         }
+      }
+    };
+#pragma unroll
+    for (int a = 0; a < kAhead; ++a) fetch(a, buf[a]);
+    for (int it = 0; it < n_iter && ok; ++it) {
+      const int st = it % C::kStages;
+      fetch(it + kAhead, buf[kAhead]);
+      if (it >= C::kStages &&
+          !mbar_wait_short_warp(&bars->empty[st], ((it / C::kStages) - 1) & 1, abort_word, status, kStatusTimeoutEmpty)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int idx = t + 64 * u;
+        const int j = idx >> 3, c = idx & 7;
         uint32_t h[4], l[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          h[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+          h[e] = pack_bf16x2(buf[0][u][2 * e], buf[0][u][2 * e + 1]);
           const float h0 = __uint_as_float(h[e] << 16), h1 = __uint_as_float(h[e] & 0xFFFF0000u);
-          l[e] = pack_bf16x2(v[2 * e] - h0, v[2 * e + 1] - h1);
+          l[e] = pack_bf16x2(buf[0][u][2 * e] - h0, buf[0][u][2 * e + 1] - h1);
         }
         const uint32_t off = j * 128 + ((c ^ (j & 7)) << 4);
         *reinterpret_cast<uint4*>(qh + st * C::kQBytes + off) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -173,6 +190,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->qfull[st]);
+#pragma unroll
+      for (int a = 0; a < kAhead; ++a)
+#pragma unroll
+        for (int u = 0; u < kPer; ++u)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) buf[a][u][e] = buf[a + 1][u][e];
     }
   }
 
@@ -181,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int row = warp * 32 + lane;
   float acc[NQ];
   bool have = false;
-  if (n_iter > 0 && mbar_wait_warp(&bars->accum, 0, abort_word, status, kStatusTimeoutAccum)) {
+  if (n_iter > 0 && mbar_wait_short_warp(&bars->accum, 0, abort_word, status, kStatusTimeoutAccum)) {
     tc_fence_after();
 #pragma unroll
     for (int c0 = 0; c0 < NQ; c0 += 16) {

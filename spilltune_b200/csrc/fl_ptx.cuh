@@ -67,6 +67,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Short-latency variant (system-default suspend window) for pipelines whose
+// per-stage latency is exposed rather than hidden behind deep buffering.
+__device__ __forceinline__ bool mbar_try_wait_short(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_short(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_word,
+                                                uint32_t* status, uint32_t err_bit) {
+  if (mbar_try_wait_short(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_short(bar, parity)) return true;
+    if (*abort_word) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort_word = 1u;
+      atomicOr(status, err_bit);
+      return false;
+    }
+  }
+}
+
 // Bounded wait for the phase with the given parity.  Returns false (after
 // setting `err_bit` in *status and in the CTA-local abort word) on timeout or
 // when another thread of the CTA already aborted.
@@ -147,6 +176,27 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+
+__device__ __forceinline__ bool mbar_wait_short_warp(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_word,
+                                                     uint32_t* status, uint32_t err_bit) {
+  const bool ok = mbar_wait_short(bar, parity, abort_word, status, err_bit);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
+// Ampere-style asynchronous copies (global -> shared, per thread).
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -206,3 +206,28 @@ def test_backward_from_a_fresh_thread(cuda_lib):
     t.join()
     for a, b in zip(out["r"], ref):
         assert ol.rel_l2(a.cpu(), b.cpu()) < 1e-6
+
+
+SMALLM_CASES = [
+    # M, N, K, rank
+    (1, 4096, 4096, 16),
+    (5, 1024, 4096, 0),
+    (8, 384, 256, 8),
+    (16, 14336, 4096, 16),
+    (16, 4096, 14336, 16),
+    (13, 200, 512, 64),      # ragged rows and tokens
+]
+
+
+@pytest.mark.parametrize("codec_name", ["int4-sym-g128", "nf4-g128"])
+@pytest.mark.parametrize("M,N,K,rank", SMALLM_CASES)
+def test_small_m_fwd_parity(cuda_lib, codec_name, M, N, K, rank):
+    """M <= 16 runs the decode-step kernel (operand bf16(lut), scale on the partial sums)."""
+    from spilltune_b200 import ops
+    pw, x, A, B, _ = _problem(M, N, K, rank, codec_name, seed=M * 11 + N + K)
+    s = 2.0
+    y = ops.fwd(x.cuda(), pw.to("cuda"), _cuda(A), _cuda(B), s).cpu()
+    W = _decode_cpu(pw)
+    ref = ol.lora_forward_fp32(x, W, A, B, s) if rank else x.float() @ W.float().t()
+    err = ol.rel_l2(y, ref)
+    assert err <= BAR and err <= TIGHT, err

@@ -191,7 +191,6 @@ class Step:
         self.timed_name = timed_name
         self.record = False
         self.events = []
-        self.comm_stream = torch.cuda.Stream() if world > 1 else None
         self.launches = 0
 
     def _fwd(self, x, w, A, B, name):
@@ -214,7 +213,8 @@ class Step:
                 for name, _N, _K, src in PROJ:
                     A, B = self.loras[l][name]
                     self._fwd(x[src], W[name], A, B, name)
-        pending = []
+        from spilltune_b200.dp import LoRAGradReducer
+        reducer = LoRAGradReducer(average=True)
         for l in reversed(range(L)):
             x, dy = self.bufs[l % 2]
             with self.weights_for(l, "backward") as W:
@@ -224,22 +224,10 @@ class Step:
                     self.ops.bwd(dy[name], x[src], W[name], A, B, self.scale, dA=A.grad, dB=B.grad,
                                  accumulate=False)
                     self.launches += 5
-            if self.world > 1:
-                import torch.distributed as dist
-                grads = [t.grad for name, _N, _K, _s in PROJ for t in self.loras[l][name]]
-                self.comm_stream.wait_stream(torch.cuda.current_stream())
-                with torch.cuda.stream(self.comm_stream):
-                    flat = torch.cat([g.reshape(-1) for g in grads])
-                    dist.all_reduce(flat)
-                    flat.div_(self.world)
-                    off = 0
-                    for g in grads:
-                        n = g.numel()
-                        g.copy_(flat[off:off + n].view_as(g))
-                        off += n
-                pending.append(flat)
-        if self.world > 1:
-            torch.cuda.current_stream().wait_stream(self.comm_stream)
+            # Data parallel: this layer's LoRA gradients are final; all-reduce
+            # them on a side stream while the next layer recomputes.
+            reducer.reduce([t.grad for name, _N, _K, _s in PROJ for t in self.loras[l][name]])
+        reducer.finish()
         self.opt.step()
 
 

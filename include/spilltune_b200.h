@@ -115,6 +115,38 @@ int fl_fwd_noalloc(const uint16_t* X, int64_t M, int64_t K, const uint8_t* paylo
                    const float* lut16, int64_t N, const float* A, const float* B, int rank, float scale,
                    uint16_t* Y, void* stream);
 
+/*
+ * Grouped (MoE expert) frozen projections.  Replaces the per-expert loop of
+ * moe_feed_forward (ram_vram_finetune/adapters/qwen3_moe.py:103-112: gather
+ * flat[tokens], F.linear(current, gate_up_proj[e]), F.linear(., down_proj[e]))
+ * and its DeepSeek twin (adapters/deepseek.py:159-177) with one launch chain
+ * over all experts, plus an optional per-expert LoRA branch.
+ *
+ * Rows are the routed (token, slot) pairs sorted by expert; seg[0..E] (device
+ * int32) are the prefix offsets of each expert's segment: seg[0] == 0,
+ * seg[E] == rows, non-decreasing.  Invalid segments write nothing and set
+ * FL_STATUS bit 4 (read with fl_status).  The experts' weights form one
+ * stacked record: payload [E, N, K/2], scales [E, N, K/128]; LoRA factors are
+ * stacked FP32 A [E, rank, K], B [E, N, rank], gradients dA/dB likewise.
+ *
+ * fl_grouped_fwd: Y[m] = X[m] . W_e^T + s (X[m] . A_e^T) . B_e^T for m in
+ * segment e, with the same rounding as fl_fwd.  fl_grouped_bwd: dX (and, when
+ * rank > 0, dA_e/dB_e summed over the expert's rows) as fl_bwd.  Workspace of
+ * fl_grouped_workspace_bytes(rows, E, N, K, rank) bytes, 16-byte aligned, for
+ * either call; the segment offsets are read on the device (no host sync), so
+ * both calls may be captured in a CUDA graph.
+ * Requires K % 128 == 0, N % 64 == 0, rank <= 64.
+ */
+size_t fl_grouped_workspace_bytes(int64_t rows, int experts, int64_t N, int64_t K, int rank);
+int fl_grouped_fwd(const uint16_t* X, const int32_t* seg, int64_t rows, int64_t K, int experts,
+                   const uint8_t* payload, const float* scales, const float* lut16, int64_t N, const float* A,
+                   const float* B, int rank, float scale, uint16_t* Y, void* workspace, size_t workspace_bytes,
+                   void* stream);
+int fl_grouped_bwd(const uint16_t* dY, const uint16_t* X, const int32_t* seg, int64_t rows, int64_t N, int64_t K,
+                   int experts, const uint8_t* payload, const float* scales, const float* lut16, const float* A,
+                   const float* B, int rank, float scale, uint16_t* dX, float* dA, float* dB, int accumulate,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,18 +42,21 @@ def lut_for(codec):
 
 @dataclass
 class PackedWeight:
-    """One frozen [N, K] matrix in group-128 4-bit form."""
-    payload: torch.Tensor  # uint8 [ceil(N*K/128)*64]
-    scales: torch.Tensor   # float32 [ceil(N*K/128)]
+    """One frozen [N, K] matrix, or a stack of E expert matrices [E, N, K]
+    (the layout of ``mlp.experts.gate_up_proj`` / ``down_proj``), in group-128
+    4-bit form.  Groups run over the flattened row-major tensor, so with
+    K % 128 == 0 expert e's groups are a contiguous slice of the record."""
+    payload: torch.Tensor  # uint8 [ceil(numel/128)*64]
+    scales: torch.Tensor   # float32 [ceil(numel/128)]
     lut: torch.Tensor      # float32 [16]
-    shape: tuple           # (N, K)
+    shape: tuple           # (N, K) or (E, N, K)
     codec: str = INT4_SYM
 
     def __post_init__(self):
         self.shape = tuple(int(s) for s in self.shape)
-        if len(self.shape) != 2 or min(self.shape) < 1:
+        if len(self.shape) not in (2, 3) or min(self.shape) < 1:
             raise ValueError("invalid stored weight shape")
-        numel = self.shape[0] * self.shape[1]
+        numel = math.prod(self.shape)
         groups = (numel + GROUP - 1) // GROUP
         if self.payload.dtype != torch.uint8 or tuple(self.payload.shape) != (groups * 64,):
             raise ValueError("invalid quantized part inventory/shape/dtype: payload")
@@ -66,15 +69,20 @@ class PackedWeight:
 
     @property
     def out_features(self):
-        return self.shape[0]
+        return self.shape[-2]
 
     @property
     def in_features(self):
-        return self.shape[1]
+        return self.shape[-1]
+
+    @property
+    def experts(self):
+        """Number of stacked expert matrices (1 for a plain [N, K] record)."""
+        return self.shape[0] if len(self.shape) == 3 else 1
 
     @property
     def numel(self):
-        return self.shape[0] * self.shape[1]
+        return math.prod(self.shape)
 
     @property
     def device(self):
@@ -102,8 +110,8 @@ def from_record(spec, parts):
     if spec.get("group_size") != GROUP or spec.get("dtype") != "bfloat16":
         raise ValueError("invalid quantized storage schema")
     shape = tuple(spec["shape"])
-    if len(shape) != 2 or spec.get("numel") != math.prod(shape):
-        raise ValueError("frozen projection records must be 2-D with a matching numel")
+    if len(shape) not in (2, 3) or spec.get("numel") != math.prod(shape):
+        raise ValueError("frozen projection records must be 2-D (or 3-D stacked experts) with a matching numel")
     lut = lut_for(codec).to(parts["payload"].device)
     return PackedWeight(parts["payload"], parts["scales"], lut, shape, codec)
 

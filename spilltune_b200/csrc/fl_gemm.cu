@@ -66,6 +66,10 @@ struct GemmArgs {
   uint32_t* status;     // device status word
   int M, N, K;          // problem dims of the frozen weight W[N,K] and tokens M
   int rank;             // 0 disables the LoRA stage
+  // Grouped (MoE) launches: tile list {expert, first row, end row, weight tile}
+  // over expert-sorted token rows, its length on the device; null for one weight.
+  const int4* tiles;
+  const int* tile_count;
 };
 
 struct __align__(16) GemmBarriers {
@@ -98,11 +102,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int R = K;   // reduction dimension
   const int groups_per_row = K / 128;
   const uint32_t crank = cluster_ctarank();       // 0 = leader of the CTA pair
-  // Grouped tile order: pairs that run at the same time cover a band of
-  // kGroupM token tiles x several weight tiles, so an activation tile is
-  // requested by a handful of pairs at once instead of by every SM.
   int w_tile, m_tile;
-  {
+  int expert = 0, m_end = M;
+  int m0;                                           // first token of the pair tile
+  if (args.tiles != nullptr) {
+    // MoE: one tile of <= 256 rows of one expert's token segment.  Both CTAs
+    // of the pair read the same entry, so they leave together.
+    const int pair = blockIdx.x >> 1;
+    if (pair >= *args.tile_count) return;
+    const int4 t = args.tiles[pair];
+    expert = t.x;
+    m0 = t.y;
+    m_end = t.z;
+    w_tile = t.w;
+    m_tile = 0;
+  } else {
+    // Grouped tile order: pairs that run at the same time cover a band of
+    // kGroupM token tiles x several weight tiles, so an activation tile is
+    // requested by a handful of pairs at once instead of by every SM.
     const int num_w = (L + 2 * kLanes - 1) / (2 * kLanes);
     const int num_m = (M + kTok - 1) / kTok;
     const int pair = blockIdx.x >> 1;
@@ -112,9 +129,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int local = pair - band * kGroupM * num_w;
     m_tile = first_m + local % rows_in_band;
     w_tile = local / rows_in_band;
+    m0 = m_tile * kTok;
   }
   const int l0 = w_tile * (2 * kLanes) + static_cast<int>(crank) * kLanes;
-  const int m0 = m_tile * kTok;                     // first token of the pair tile
+  const int wrow0 = expert * N;                     // this expert's first row in the stacked record
   const int mh = m0 + static_cast<int>(crank) * kTokHalf;  // first token of this CTA's half
   const int n_main = R / kStageK;
   const bool has_lora = args.rank > 0;
@@ -160,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int r0 = it * kStageK;
           mbar_arrive_expect_tx(&bars->full[s], kXBytes + kQBytes);
           tma_load_2d(xs + s * kXBytes, &tm_act, r0, mh, &bars->full[s]);
-          tma_load_2d(qs + s * kQBytes, &tm_code, r0 / 2, l0, &bars->full[s]);       // 128 rows x 32 B
+          tma_load_2d(qs + s * kQBytes, &tm_code, r0 / 2, wrow0 + l0, &bars->full[s]);  // 128 rows x 32 B
         } else {
           mbar_arrive_expect_tx(&bars->full[s], kXBytes);
           tma_load_2d(xs + s * kXBytes, &tm_low, 0, mh, &bars->full[s]);
@@ -219,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (32 TMEM columns).
       const int n = l0 + row;
       const bool valid = n < N;
-      const float* srow = args.scales + static_cast<size_t>(valid ? n : 0) * groups_per_row;
+      const float* srow = args.scales + static_cast<size_t>(wrow0 + (valid ? n : 0)) * groups_per_row;
       float next_scale = (valid && 2 * grp < 2 * groups_per_row) ? __ldg(srow + grp) : 0.0f;
       for (int pit = 2 * grp; pit < n_iter && ok; pit += 2 * kGroups) {
         ProductTable table;
@@ -257,8 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int c0 = 2 * j, c1 = c0 + 1;
-              const float a = (valid && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(n) * args.rank + c0) : 0.f;
-              const float b = (valid && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(n) * args.rank + c1) : 0.f;
+              const float a = (valid && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c0) : 0.f;
+              const float b = (valid && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c1) : 0.f;
               v[j] = pack_bf16x2(a, b);
             }
           }
@@ -291,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = m0 + c + j;
-            if (m < M) args.out[static_cast<size_t>(m) * L + l] = __float2bfloat16_rn(__uint_as_float(v[j]));
+            if (m < m_end) args.out[static_cast<size_t>(m) * L + l] = __float2bfloat16_rn(__uint_as_float(v[j]));
           }
         }
       }
@@ -355,7 +373,7 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 // blora: [N, rank] fp32; y: [M, N] bf16.
 int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
                     const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles) {
   CUtensorMap tm_act, tm_low, tm_code;
   int rc = make_tensor_map_2d(&tm_act, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, static_cast<uint64_t>(K) * 2, 64,
                               kTokHalf, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -367,8 +385,8 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
   } else {
     tm_low = tm_act;
   }
-  rc = make_tensor_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, 32, 128,
-                          CU_TENSOR_MAP_SWIZZLE_NONE);
+  rc = make_tensor_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, static_cast<uint64_t>(N) * experts,
+                          K / 2, 32, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   GemmArgs a;
   a.scales = scales;
@@ -380,8 +398,10 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
   a.N = N;
   a.K = K;
   a.rank = rank;
-  // CTA pairs: each pair covers 256 W rows x 256 tokens.
-  dim3 grid(2 * ((N + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok));
+  a.tiles = tiles;
+  a.tile_count = tile_count;
+  // CTA pairs: each pair covers 256 W rows x 256 tokens (grouped: one listed tile).
+  dim3 grid(tiles ? 2 * max_tiles : 2 * ((N + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);

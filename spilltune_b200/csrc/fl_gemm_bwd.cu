@@ -65,6 +65,8 @@ struct Args {
   __nv_bfloat16* out;   // dX [M, K]
   uint32_t* status;
   int M, N, K, rank;
+  const int4* tiles;    // MoE: {expert, first row, end row, column tile}; null for one weight
+  const int* tile_count;
 };
 
 // Byte offset of 16-byte chunk j (k = 8j..8j+7 within the CTA's 64-k half
@@ -90,8 +92,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int M = args.M, N = args.N, K = args.K;
   const int groups_per_row = K / 128;
   const uint32_t crank = cluster_ctarank();
-  int k_tile, m_tile;
-  {
+  int k_tile, m_tile = 0;
+  int expert = 0, m_end = M, m0;
+  if (args.tiles != nullptr) {
+    const int pair = blockIdx.x >> 1;
+    if (pair >= *args.tile_count) return;
+    const int4 t = args.tiles[pair];
+    expert = t.x;
+    m0 = t.y;
+    m_end = t.z;
+    k_tile = t.w;
+  } else {
     const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
     const int num_m = (M + 2 * kTokHalf - 1) / (2 * kTokHalf);
     const int pair = blockIdx.x >> 1;
@@ -101,10 +112,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int local = pair - band * kGroupM * num_k;
     m_tile = first_m + local % rows_in_band;
     k_tile = local / rows_in_band;
+    m0 = m_tile * 2 * kTokHalf;                               // first token of the pair tile
   }
   const int k0 = k_tile * 2 * kColHalf;                       // first column of the pair tile
   const int kb = k0 + static_cast<int>(crank) * kColHalf;     // first column of this CTA's B half
-  const int m0 = m_tile * 2 * kTokHalf;                       // first token of the pair tile
+  const int wrow0 = expert * N;                               // expert's first row in the stacked record
+  const float* alora = args.alora + static_cast<size_t>(expert) * args.rank * K;
   const int mh = m0 + static_cast<int>(crank) * kTokHalf;     // first token of this CTA's A half
   const int n_main = N / kStageN;
   const bool has_lora = args.rank > 0;
@@ -148,7 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int n0 = it * kStageN;
           mbar_arrive_expect_tx(&bars->full[s], kABytes + kQBytes);
           tma_load_2d(as + s * kABytes, &tm_dy, n0, mh, &bars->full[s]);
-          tma_load_2d(qs + s * kQBytes, &tm_code, kb / 2, n0, &bars->full[s]);
+          tma_load_2d(qs + s * kQBytes, &tm_code, kb / 2, wrow0 + n0, &bars->full[s]);
         } else {
           mbar_arrive_expect_tx(&bars->full[s], kABytes);
           tma_load_2d(as + s * kABytes, &tm_us, 0, mh, &bars->full[s]);
@@ -195,8 +208,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The row's scale for the next stage this group owns is loaded one owned
     // stage ahead (stages 2g, 2g+1, 2g+2*kGroups, ...).
     auto load_scale = [&](int it) {
-      return (tile_valid && it < n_main) ? __ldg(args.scales + static_cast<size_t>(it * kStageN + r) * groups_per_row + g)
-                                         : 0.0f;
+      return (tile_valid && it < n_main)
+                 ? __ldg(args.scales + static_cast<size_t>(wrow0 + it * kStageN + r) * groups_per_row + g)
+                 : 0.0f;
     };
     float next_scale = load_scale(2 * grp);
     for (int pit = 2 * grp; pit < n_iter && ok; pit += 2 * kGroups) {
@@ -234,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const bool live = tile_valid && r < args.rank;
-          const float* src = args.alora + static_cast<size_t>(live ? r : 0) * K + kb + 64 * khalf;
+          const float* src = alora + static_cast<size_t>(live ? r : 0) * K + kb + 64 * khalf;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float2 a = make_float2(0.f, 0.f);
@@ -267,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(tmem_base + lane_addr + c, acc);
         tmem_wait_ld();
         const int kcol = k0 + c;
-        if (m < M && kcol < K) {
+        if (m < m_end && kcol < K) {
           uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(m) * K + kcol);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -308,7 +322,7 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles) {
   using namespace bwd;
   if ((K * 2) % 16 != 0 || N % kStageN != 0 || K % 128 != 0)
     return set_error(FL_ERR_ARG, "bwd gemm: needs N %% 64 == 0 and K %% 128 == 0");
@@ -323,8 +337,8 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   } else {
     tm_us = tm_dy;
   }
-  rc = make_tensor_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, kColHalf / 2, kStageN,
-                          CU_TENSOR_MAP_SWIZZLE_NONE);
+  rc = make_tensor_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, static_cast<uint64_t>(N) * experts,
+                          K / 2, kColHalf / 2, kStageN, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   Args a;
   a.scales = scales;
@@ -336,7 +350,10 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   a.N = N;
   a.K = K;
   a.rank = rank;
-  const int pairs = ((K + 2 * kColHalf - 1) / (2 * kColHalf)) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf));
+  a.tiles = tiles;
+  a.tile_count = tile_count;
+  const int pairs = tiles ? max_tiles
+                          : ((K + 2 * kColHalf - 1) / (2 * kColHalf)) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);

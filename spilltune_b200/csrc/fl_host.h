@@ -13,27 +13,49 @@ int set_error(int code, const char* fmt, ...);
 uint32_t* status_word(int device);  // device status word of the calling device
 
 // Y[M,N] = X . W^T + Ts . Blora^T (fl_gemm.cu).
+// Grouped (MoE) form: `tiles`/`tile_count` from launch_moe_plan, the weight a
+// stacked [experts, N, K] record, blora [experts, N, rank]; grid sized for
+// `max_tiles`.  tiles == nullptr: one weight, experts = 1.
 int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
                     const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
-                    cudaStream_t stream);
+                    cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
+                    int experts = 1, int max_tiles = 0);
+
+// Tile list over expert segments: seg[0..E] (device int32 prefix offsets of the
+// expert-sorted rows); each entry {expert, first row, end row, column tile} for
+// `rows` rows x `col_tiles` column tiles; count written to *count.
+// Invalid segments (not monotone, seg[0] != 0 or seg[E] != total_rows) or a
+// list longer than max_tiles: count = 0 and kStatusBadLaunch in *status.
+int launch_moe_plan(const int* seg, int experts, int total_rows, int rows, int col_tiles, int4* tiles,
+                    int max_tiles, int* count, uint32_t* status, cudaStream_t stream);
+int moe_max_tiles(int total_rows, int experts, int rows, int col_tiles);
 
 // dX[M,K] = dY . W + Us . Alora (fl_gemm_bwd.cu).
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
-                    cudaStream_t stream);
+                    cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
+                    int experts = 1, int max_tiles = 0);
 
 int launch_dequant(const uint8_t* payload, const float* scales, const float* lut, int64_t numel, void* out,
                    cudaStream_t stream);
 
 // out[m, j] = bf16(s * sum_r P[m, r] * Q(j, r)), j < rank, zero for rank <= j < 64.
 // Q(j, r) = q[j * q_sj + r * q_sr] (fp32).
+// Grouped (MoE) form: 128-row tiles over expert-sorted rows, the factor of tile
+// t at q + tiles[t].x * q_expert_stride.
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
-                     float s, void* out64, cudaStream_t stream);
+                     float s, void* out64, cudaStream_t stream, const int4* tiles = nullptr,
+                     const int* tile_count = nullptr, int max_tiles = 0, int64_t q_expert_stride = 0);
 
 // out(p, j) (+)= sum_m P[m, p] * Q[m, j]  (P bf16 [M, Pdim], Q bf16 [M, 64]),
 // out(p, j) = out[p * o_sp + j * o_sj] fp32, j < rank.
+// Grouped (MoE) form: token slices {expert, first row, end row, 0} over
+// expert-sorted rows; slice t accumulates into out + tiles[t].x * out_expert_stride
+// (out then holds all experts: `out_total` floats are cleared when !accumulate).
 int launch_lora_grad(const void* P, int M, int Pdim, const void* Q, int rank, float* out, int64_t o_sp,
-                     int64_t o_sj, int accumulate, cudaStream_t stream);
+                     int64_t o_sj, int accumulate, cudaStream_t stream, const int4* tiles = nullptr,
+                     const int* tile_count = nullptr, int max_tiles = 0, int64_t out_expert_stride = 0,
+                     int64_t out_total = 0);
 
 int launch_smallm_fwd(const void* X, const void* Ts, const uint8_t* codes, const float* scales,
                       const float* lut, const float* lora, int rank, void* Y, int M, int N, int K,

@@ -45,13 +45,23 @@ template <int JT>
 __global__ void __launch_bounds__(128) lora_grad_kernel(const __nv_bfloat16* __restrict__ P, int M, int Pdim,
                                                         const __nv_bfloat16* __restrict__ Q, int rank,
                                                         float* __restrict__ out, int64_t o_sp, int64_t o_sj,
-                                                        int m_per_cta) {
+                                                        int m_per_cta, const int4* __restrict__ tiles,
+                                                        const int* __restrict__ tile_count,
+                                                        int64_t out_expert_stride) {
   __shared__ float red[4][32][8 * JT + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int p0 = blockIdx.x * 32;
-  const int mbeg = blockIdx.y * m_per_cta;
-  const int mend = min(M, mbeg + m_per_cta);
+  int mbeg = blockIdx.y * m_per_cta;
+  int mend = min(M, mbeg + m_per_cta);
+  if (tiles != nullptr) {
+    // MoE: one token slice of one expert; its gradient is that expert's.
+    if (static_cast<int>(blockIdx.y) >= *tile_count) return;
+    const int4 t = tiles[blockIdx.y];
+    mbeg = t.y;
+    mend = t.z;
+    out += t.x * out_expert_stride;
+  }
   float acc[2][JT][4];
 #pragma unroll
   for (int pt = 0; pt < 2; ++pt)
@@ -102,11 +112,13 @@ __global__ void __launch_bounds__(128) lora_grad_kernel(const __nv_bfloat16* __r
 }
 
 int launch_lora_grad(const void* P, int M, int Pdim, const void* Q, int rank, float* out, int64_t o_sp,
-                     int64_t o_sj, int accumulate, cudaStream_t stream) {
+                     int64_t o_sj, int accumulate, cudaStream_t stream, const int4* tiles, const int* tile_count,
+                     int max_tiles, int64_t out_expert_stride, int64_t out_total) {
   if (Pdim % 32 != 0) return set_error(FL_ERR_ARG, "lora_grad: dim %d not a multiple of 32", Pdim);
   if (!accumulate) {
-    // out is a dense [Pdim, rank] or [rank, Pdim] fp32 matrix.
-    cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(Pdim) * rank * sizeof(float), stream);
+    // out is a dense [Pdim, rank] or [rank, Pdim] fp32 matrix (per expert).
+    const size_t n = tiles ? static_cast<size_t>(out_total) : static_cast<size_t>(Pdim) * rank;
+    cudaError_t e = cudaMemsetAsync(out, 0, n * sizeof(float), stream);
     if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_grad memset: %s", cudaGetErrorString(e));
   }
   const int ptiles = Pdim / 32;
@@ -117,15 +129,20 @@ int launch_lora_grad(const void* P, int M, int Pdim, const void* Q, int rank, fl
   int m_per_cta = (M + splits - 1) / splits;
   m_per_cta = (m_per_cta + 63) / 64 * 64;
   splits = (M + m_per_cta - 1) / m_per_cta;
+  if (tiles) splits = max_tiles;
+  if (splits < 1) return FL_OK;
   dim3 grid(ptiles, splits);
   auto p = static_cast<const __nv_bfloat16*>(P);
   auto qq = static_cast<const __nv_bfloat16*>(Q);
   if (rank <= 16)
-    lora_grad_kernel<2><<<grid, 128, 0, stream>>>(p, M, Pdim, qq, rank, out, o_sp, o_sj, m_per_cta);
+    lora_grad_kernel<2><<<grid, 128, 0, stream>>>(p, M, Pdim, qq, rank, out, o_sp, o_sj, m_per_cta, tiles,
+                                                         tile_count, out_expert_stride);
   else if (rank <= 32)
-    lora_grad_kernel<4><<<grid, 128, 0, stream>>>(p, M, Pdim, qq, rank, out, o_sp, o_sj, m_per_cta);
+    lora_grad_kernel<4><<<grid, 128, 0, stream>>>(p, M, Pdim, qq, rank, out, o_sp, o_sj, m_per_cta, tiles,
+                                                         tile_count, out_expert_stride);
   else
-    lora_grad_kernel<8><<<grid, 128, 0, stream>>>(p, M, Pdim, qq, rank, out, o_sp, o_sj, m_per_cta);
+    lora_grad_kernel<8><<<grid, 128, 0, stream>>>(p, M, Pdim, qq, rank, out, o_sp, o_sj, m_per_cta, tiles,
+                                                         tile_count, out_expert_stride);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_grad launch: %s", cudaGetErrorString(e));
   return FL_OK;

@@ -51,7 +51,7 @@ template <int NQ>
 __global__ void __launch_bounds__(kThreads, 1)
     lora_down_tc_kernel(const __grid_constant__ CUtensorMap tm_p, const float* __restrict__ q, int64_t q_sj,
                         int64_t q_sr, int rank, float s, __nv_bfloat16* __restrict__ out, int M, int R,
-                        uint32_t* status) {
+                        uint32_t* status, const int4* tiles, const int* tile_count, int64_t q_expert_stride) {
   using C = Cfg<NQ>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -62,7 +62,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t crank = cluster_ctarank();
-  const int m0 = (blockIdx.x / kSplit) * kRows;
+  int m0 = (blockIdx.x / kSplit) * kRows;
+  int m_end = M;
+  if (tiles != nullptr) {
+    // MoE: one <= 128-row tile of one expert's segment; its factor is that
+    // expert's.  The 4 CTAs of the cluster read the same entry.
+    const int ti = blockIdx.x / kSplit;
+    if (ti >= *tile_count) return;
+    const int4 t = tiles[ti];
+    m0 = t.y;
+    m_end = t.z;
+    q += t.x * q_expert_stride;
+  }
   const int n_chunks = R / kStageR;
   const int c_begin = static_cast<int>(crank) * n_chunks / kSplit;
   const int c_end = (static_cast<int>(crank) + 1) * n_chunks / kSplit;
@@ -240,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int e = 0; e < NQ; ++e) acc[e] += pr[e];
     }
     const int m = m0 + row;
-    if (m < M) {
+    if (m < m_end) {
       uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(m) * 64);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
@@ -265,7 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int NQ>
 static int launch_nq(const CUtensorMap& tm, const float* q, int64_t q_sj, int64_t q_sr, int rank, float s,
-                     void* out, int M, int R, cudaStream_t stream) {
+                     void* out, int M, int R, cudaStream_t stream, const int4* tiles, const int* tile_count,
+                     int max_tiles, int64_t q_expert_stride) {
   using C = Cfg<NQ>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -278,7 +290,7 @@ static int launch_nq(const CUtensorMap& tm, const float* q, int64_t q_sj, int64_
   cudaGetDevice(&dev);
   uint32_t* status = status_word(dev);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kSplit * ((M + kRows - 1) / kRows));
+  cfg.gridDim = dim3(kSplit * (tiles ? max_tiles : (M + kRows - 1) / kRows));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
@@ -290,7 +302,8 @@ static int launch_nq(const CUtensorMap& tm, const float* q, int64_t q_sj, int64_
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t le = cudaLaunchKernelEx(&cfg, lora_down_tc_kernel<NQ>, tm, q, q_sj, q_sr, rank, s,
-                                      static_cast<__nv_bfloat16*>(out), M, R, status);
+                                      static_cast<__nv_bfloat16*>(out), M, R, status, tiles, tile_count,
+                                      q_expert_stride);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }
@@ -301,7 +314,8 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
 
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank, float s,
-                     void* out64, cudaStream_t stream) {
+                     void* out64, cudaStream_t stream, const int4* tiles, const int* tile_count, int max_tiles,
+                     int64_t q_expert_stride) {
   if (R % 128 != 0) return set_error(FL_ERR_ARG, "lora_down: reduction dim %d not a multiple of 128", R);
   if (rank < 1 || rank > 64) return set_error(FL_ERR_ARG, "lora_down: rank %d outside [1, 64]", rank);
   if (q_sr == 1 && (reinterpret_cast<uintptr_t>(q) & 15u))
@@ -310,9 +324,14 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
   int rc = make_tensor_map_2d(&tm, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, R, M, static_cast<uint64_t>(R) * 2, 64,
                               ld::kRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if (rank <= 16) return ld::launch_nq<16>(tm, q, q_sj, q_sr, rank, s, out64, M, R, stream);
-  if (rank <= 32) return ld::launch_nq<32>(tm, q, q_sj, q_sr, rank, s, out64, M, R, stream);
-  return ld::launch_nq<64>(tm, q, q_sj, q_sr, rank, s, out64, M, R, stream);
+  if (rank <= 16)
+    return ld::launch_nq<16>(tm, q, q_sj, q_sr, rank, s, out64, M, R, stream, tiles, tile_count, max_tiles,
+                             q_expert_stride);
+  if (rank <= 32)
+    return ld::launch_nq<32>(tm, q, q_sj, q_sr, rank, s, out64, M, R, stream, tiles, tile_count, max_tiles,
+                             q_expert_stride);
+  return ld::launch_nq<64>(tm, q, q_sj, q_sr, rank, s, out64, M, R, stream, tiles, tile_count, max_tiles,
+                           q_expert_stride);
 }
 
 }  // namespace fl

@@ -54,9 +54,15 @@ def _flat(x, K):
     return x2.contiguous()
 
 
+def _matrix_shape(weight: PackedWeight):
+    if len(weight.shape) != 2:
+        raise ValueError("stacked expert records [E, N, K] go through spilltune_b200.moe (grouped ops)")
+    return weight.shape
+
+
 def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0):
     """Y = x . W^T + scale * (x . A^T) . B^T  (bf16 out; plain frozen linear if A is None)."""
-    N, K = weight.shape
+    N, K = _matrix_shape(weight)
     x2 = _flat(x, K)
     rank = 0 if A is None else A.shape[0]
     _need_cuda(x2, weight.payload, A, B)
@@ -78,7 +84,7 @@ def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0):
 
 def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False):
     """Returns (dX, dA, dB) of fwd(); dA/dB are fp32 (accumulated into when given and accumulate)."""
-    N, K = weight.shape
+    N, K = _matrix_shape(weight)
     dy2 = _flat(dy, N)
     rank = 0 if A is None else A.shape[0]
     M = dy2.shape[0]

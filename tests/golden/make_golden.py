@@ -14,6 +14,13 @@ reference; they only read these committed vectors.
 * ``lora_small.npz`` — ``LoRAProjection.forward`` (``finetune/lora.py:205-220``)
   on the decoded matrix plus the autograd backward (dX, dA, dB) for a seeded
   problem with M=18 (ragged), K=256, N=384, rank 8, alpha 16.
+* ``moe_small.npz`` — the reference's Qwen3-MoE ``moe_feed_forward``
+  (``adapters/qwen3_moe.py:95-113``) on int4-sym-g128-encoded stacked experts
+  (E=6, top-2, hidden 128, expert intermediate 128, 24 tokens, expert 5 never
+  routed), its output and the autograd gradient of the hidden states.
+* ``deepseek_route.npz`` — the reference's DeepSeek-V3 router
+  (``adapters/deepseek.py:115-126``): 16 experts in 4 groups, 2 kept, top-4,
+  normalised, scale 2.5; indices and weights sorted by expert id per token.
 """
 import os
 import sys
@@ -23,6 +30,8 @@ import torch
 
 from ram_vram_finetune.quantization import codecs
 from ram_vram_finetune.finetune.lora import LoRAProjection
+from ram_vram_finetune.adapters.qwen3_moe import moe_feed_forward
+from ram_vram_finetune.adapters.deepseek import route as deepseek_route
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -79,8 +88,49 @@ def lora_case():
         Y_bf16=bits(y.detach()), dX_bf16=bits(dx), dA=da.numpy(), dB=db.numpy())
 
 
+def moe_case():
+    T, H, I, E, top_k = 24, 128, 128, 6, 2
+    g = torch.Generator().manual_seed(23)
+    hidden = torch.randn(2, T // 2, H, generator=g)
+    hidden[..., 0] = 3.0
+    hidden = hidden.to(torch.bfloat16)
+    gate = torch.randn(E, H, generator=g) * 0.3
+    gate[5, 0] = -5.0  # expert 5 never reaches the top-2
+    gate = gate.to(torch.bfloat16)
+    gate_up = torch.randn(E, 2 * I, H, generator=g) * 0.05
+    down = torch.randn(E, H, I, generator=g) * 0.05
+    rec_gu = codecs.encode(gate_up.contiguous(), "int4-sym-g128")
+    rec_dn = codecs.encode(down.contiguous(), "int4-sym-g128")
+    weights = {"mlp.gate.weight": gate, "mlp.experts.gate_up_proj": codecs.materialize(rec_gu),
+               "mlp.experts.down_proj": codecs.materialize(rec_dn)}
+    h = hidden.clone().requires_grad_(True)
+    out = moe_feed_forward(h, weights, num_experts=E, top_k=top_k, norm_topk_prob=True)
+    dout = torch.randn(out.shape, generator=g).to(torch.bfloat16)
+    (dh,) = torch.autograd.grad(out, (h,), dout)
+    np.savez_compressed(
+        os.path.join(HERE, "moe_small.npz"),
+        T=T, H=H, I=I, E=E, top_k=top_k, norm_topk_prob=1,
+        hidden_bf16=bits(hidden), gate_bf16=bits(gate),
+        gate_up_payload=rec_gu.parts["payload"].numpy(), gate_up_scales=rec_gu.parts["scales"].numpy(),
+        down_payload=rec_dn.parts["payload"].numpy(), down_scales=rec_dn.parts["scales"].numpy(),
+        out_bf16=bits(out.detach()), dout_bf16=bits(dout), dhidden_bf16=bits(dh))
+
+    # DeepSeek-V3 router: 16 experts in 4 groups, 2 groups kept, top-4.
+    T, H, E = 32, 64, 16
+    flat = (torch.randn(T, H, generator=g)).to(torch.bfloat16)
+    wr = torch.randn(E, H, generator=g) * 0.2
+    bias = torch.randn(E, generator=g) * 0.1
+    _, rw, ri = deepseek_route(flat, wr, bias, groups=4, group_k=2, top_k=4, normalize=True, scale=2.5)
+    order = torch.argsort(ri, dim=-1)
+    np.savez_compressed(
+        os.path.join(HERE, "deepseek_route.npz"),
+        flat_bf16=bits(flat), weight=wr.numpy(), bias=bias.numpy(), groups=4, group_k=2, top_k=4,
+        scale=2.5, indices=torch.gather(ri, 1, order).numpy(), weights=torch.gather(rw, 1, order).numpy())
+
+
 if __name__ == "__main__":
     torch.set_num_threads(1)
     codec_cases()
     lora_case()
+    moe_case()
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")), file=sys.stderr)

@@ -86,9 +86,12 @@ def test_two_rank_gradient_reduction_sharding_and_normalisation():
 
 def _worker_dead_peer(rank, world, port, q):
     _init(rank, world, port, timeout_s=3)
+    # One complete step first, so the group is fully connected before a rank
+    # leaves (a rank that leaves during rendezvous tests something else).
+    t = torch.ones(4)
+    dist.all_reduce(t)
     if rank == 1:
-        # This rank leaves between steps without joining the collective.
-        dist.destroy_process_group()
+        # This rank leaves between steps without joining the next collective.
         os._exit(0)
     try:
         t = torch.ones(4)
@@ -97,6 +100,10 @@ def _worker_dead_peer(rank, world, port, q):
     except Exception as e:  # gloo reports the missing peer (timeout / connection closed)
         q.put((rank, type(e).__name__))
     finally:
+        # Queue.put hands the item to a feeder thread: flush it before the
+        # hard exit, or the parent may never receive it.
+        q.close()
+        q.join_thread()
         os._exit(0)
 
 

@@ -59,9 +59,11 @@ int fl_status(int reset, uint32_t* status_out);
 int fl_dequant(const uint8_t* payload, const float* scales, const float* lut16, int64_t numel,
                uint16_t* out_bf16, void* stream);
 
-/* Scratch bytes fl_fwd needs for a given token count (the scaled low-rank
- * activations Ts = bf16(s * X.A^T), padded to 64 columns). */
-size_t fl_fwd_workspace_bytes(int64_t M, int rank);
+/* Scratch bytes fl_fwd needs: the scaled low-rank activations
+ * Ts = bf16(s * X.A^T) (M x 64 bf16) and A converted to a bf16 hi/lo pair
+ * (4 * rank' * K bytes, rank' = rank rounded up to 16, 32 or 64); 0 when
+ * rank == 0. */
+size_t fl_fwd_workspace_bytes(int64_t M, int64_t K, int rank);
 
 /*
  * Frozen projection forward with the LoRA branch
@@ -76,15 +78,16 @@ size_t fl_fwd_workspace_bytes(int64_t M, int rank);
  * (exact for int4-sym, the bf16-rounded codebook for NF4) and the scale
  * multiplies the FP32 partial sum.
  * Requires K % 128 == 0, rank <= 64, 16-byte aligned pointers, bias-free
- * projections.  workspace: >= fl_fwd_workspace_bytes(M, rank) bytes (may be
- * NULL when rank == 0).
+ * projections.  workspace: >= fl_fwd_workspace_bytes(M, K, rank) bytes,
+ * 16-byte aligned (may be NULL when rank == 0).
  */
 int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, const float* scales,
            const float* lut16, int64_t N, const float* A, const float* B, int rank, float scale, uint16_t* Y,
            void* workspace, size_t workspace_bytes, void* stream);
 
-/* Scratch bytes fl_bwd needs (Us = bf16(s * dY.B) and Ts, 64 columns each). */
-size_t fl_bwd_workspace_bytes(int64_t M, int rank);
+/* Scratch bytes fl_bwd needs: Us = bf16(s * dY.B) and Ts (M x 64 bf16 each)
+ * and the converted factors (4 * rank' * (N + K) bytes); 0 when rank == 0. */
+size_t fl_bwd_workspace_bytes(int64_t M, int64_t N, int64_t K, int rank);
 
 /*
  * Recomputed-backward of the same projection (the autograd VJP that
@@ -104,9 +107,10 @@ int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t 
  * Same result as fl_fwd, for callers that cannot allocate device memory at
  * call time (a host binding without a device allocator, a trainer whose
  * device budget is fixed up front).  No counterpart in the reference.  It
- * allocates nothing: the scratch lives in a 4 MiB array of this library's own
- * device memory (held on every GPU that loads the library), so M is limited to
- * 32768 tokens when rank > 0 (FL_ERR_ARG beyond).  The first call on a device
+ * allocates nothing: the scratch lives in a 12 MiB array of this library's own
+ * device memory (held on every GPU that loads the library), so when rank > 0 M
+ * is limited to 32768 tokens and rank' * K to 2^21 (rank' = rank rounded up to
+ * 16, 32 or 64; FL_ERR_ARG beyond).  The first call on a device
  * looks up that array's address; make it before any stream capture.  All calls
  * on a device share the array: calls whose kernels overlap on the GPU race and
  * must be serialised by the caller.

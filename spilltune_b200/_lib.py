@@ -30,9 +30,9 @@ SIGNATURES = {
     "fl_last_error": ([], ctypes.c_char_p),
     "fl_status": ([_INT, _P], _INT),
     "fl_dequant": ([_P, _P, _P, _I64, _P, _P], _INT),
-    "fl_fwd_workspace_bytes": ([_I64, _INT], _SZ),
+    "fl_fwd_workspace_bytes": ([_I64, _I64, _INT], _SZ),
     "fl_fwd": ([_P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _INT, _F, _P, _P, _SZ, _P], _INT),
-    "fl_bwd_workspace_bytes": ([_I64, _INT], _SZ),
+    "fl_bwd_workspace_bytes": ([_I64, _I64, _I64, _INT], _SZ),
     "fl_bwd": ([_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _INT, _F, _P, _P, _P, _INT, _P, _SZ, _P], _INT),
     "fl_fwd_noalloc": ([_P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _INT, _F, _P, _P], _INT),
     "fl_grouped_workspace_bytes": ([_I64, _INT, _I64, _I64, _INT], _SZ),

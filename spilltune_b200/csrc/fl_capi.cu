@@ -54,7 +54,7 @@ using namespace fl;
 
 extern "C" {
 
-int fl_version(void) { return 100; }
+int fl_version(void) { return 101; }
 
 const char* fl_last_error(void) { return g_err; }
 
@@ -84,12 +84,16 @@ int fl_dequant(const uint8_t* payload, const float* scales, const float* lut16, 
   return launch_dequant(payload, scales, lut16, numel, out_bf16, static_cast<cudaStream_t>(stream));
 }
 
-size_t fl_fwd_workspace_bytes(int64_t M, int rank) {
-  return rank > 0 ? static_cast<size_t>(M) * 64 * 2 : 0;
+// fl_fwd workspace: [Ts: M x 64 bf16][A converted: lora_factor_bytes(K)]
+size_t fl_fwd_workspace_bytes(int64_t M, int64_t K, int rank) {
+  if (rank <= 0 || M <= 0 || K <= 0) return 0;
+  return static_cast<size_t>(M) * 128 + lora_factor_bytes(K, rank);
 }
 
-size_t fl_bwd_workspace_bytes(int64_t M, int rank) {
-  return rank > 0 ? static_cast<size_t>(M) * 64 * 2 * 2 : 0;
+// fl_bwd workspace: [Us][Ts] (M x 64 bf16 each) [B^T converted: N][A converted: K]
+size_t fl_bwd_workspace_bytes(int64_t M, int64_t N, int64_t K, int rank) {
+  if (rank <= 0 || M <= 0 || N <= 0 || K <= 0) return 0;
+  return static_cast<size_t>(M) * 256 + lora_factor_bytes(N, rank) + lora_factor_bytes(K, rank);
 }
 
 static int check_common(const char* who, int64_t M, int64_t N, int64_t K, int rank, const void* payload,
@@ -112,14 +116,15 @@ int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, cons
   if (!aligned16(X)) return set_error(FL_ERR_ARG, "fl_fwd: X must be 16-byte aligned");
   if (rank > 0) {
     if (!A || !B) return set_error(FL_ERR_ARG, "fl_fwd: null LoRA factor");
-    if (!workspace || workspace_bytes < fl_fwd_workspace_bytes(M, rank) || !aligned16(workspace))
+    if (!workspace || workspace_bytes < fl_fwd_workspace_bytes(M, K, rank) || !aligned16(workspace))
       return set_error(FL_ERR_ARG, "fl_fwd: workspace missing, short or misaligned");
   }
   uint32_t* status = nullptr;
   if ((rc = current_status(&status))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (rank > 0) {
-    rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, workspace, st);
+    void* qc = static_cast<uint8_t*>(workspace) + static_cast<size_t>(M) * 128;
+    rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, workspace, qc, st);
     if (rc) return rc;
   }
   // Decode-like steps (M <= 16) are bound by the weight bytes: dedicated kernel.
@@ -139,7 +144,7 @@ int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t 
   if (rank > 0) {
     if (!X || !A || !B || !dA || !dB) return set_error(FL_ERR_ARG, "fl_bwd: null X or LoRA factor/gradient");
     if (!aligned16(X)) return set_error(FL_ERR_ARG, "fl_bwd: X must be 16-byte aligned");
-    if (!workspace || workspace_bytes < fl_bwd_workspace_bytes(M, rank) || !aligned16(workspace))
+    if (!workspace || workspace_bytes < fl_bwd_workspace_bytes(M, N, K, rank) || !aligned16(workspace))
       return set_error(FL_ERR_ARG, "fl_bwd: workspace missing, short or misaligned");
   }
   uint32_t* status = nullptr;
@@ -148,10 +153,12 @@ int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t 
   uint8_t* us = static_cast<uint8_t*>(workspace);
   uint8_t* ts = us ? us + static_cast<size_t>(M) * 128 : nullptr;
   if (rank > 0) {
+    uint8_t* qc_b = ts + static_cast<size_t>(M) * 128;
+    uint8_t* qc_a = qc_b + lora_factor_bytes(N, rank);
     // Us = bf16(s * dY . B): Q(j, n) = B[n * rank + j]
-    if ((rc = launch_lora_down(dY, (int)M, (int)N, B, 1, rank, rank, scale, us, st))) return rc;
+    if ((rc = launch_lora_down(dY, (int)M, (int)N, B, 1, rank, rank, scale, us, qc_b, st))) return rc;
     // Ts = bf16(s * X . A^T): Q(j, k) = A[j * K + k]
-    if ((rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, st))) return rc;
+    if ((rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, qc_a, st))) return rc;
   }
   if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, (int)M, (int)N, (int)K, status, st)))
     return rc;

@@ -28,13 +28,21 @@
 //   * D = 256 x 256 fp32 accumulator, 128 rows in each CTA's TMEM, read back by
 //     the dequant warps of that CTA.
 //
+// Persistent: one CTA pair per resident cluster slot walks a static list of
+// tiles; stage counters run on across tiles, so TMA prefetch and decode of the
+// next tile overlap the end of the current one.  The accumulator is drained
+// into a 64 KiB shared-memory staging tile and leaves by an asynchronous TMA
+// store (or 16-byte stores for a grouped tile that ends inside the box).
+//
 // Warp roles (448 threads per CTA): warp 0 TMA producer, warp 1 TMEM owner
 // (both CTAs) + MMA issuer (leader CTA only), warps 2-13 dequant producers in
 // three groups of four that take turns on pairs of stages (one warp per TMEM
-// lane quarter decodes the whole stage for its lanes), then epilogue.
+// lane quarter decodes the whole stage for its lanes) and drain the
+// accumulator after their first stage pair of the next tile.
 // Synchronisation: full[s] (local TMA bytes), afull[s] (leader only: 8 local +
 // 8 peer dequant-warp arrivals), empty[s] and accum (multicast tcgen05.commit
-// from the leader into both CTAs).
+// from the leader into both CTAs), acc_empty (leader only: 12 local + 12 peer
+// epilogue-warp arrivals before the next tile's first MMA).
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -61,11 +69,12 @@ static_assert(kAccCols + kStages * kAStageCols <= kTmemCols, "TMEM budget");
 struct GemmArgs {
   const float* scales;  // fp32 [N * K/128]
   const float* lut;     // fp32 [16]
-  const float* lora;    // forward: Blora [N, r]; backward: Alora [r, K]
+  const float* lora;    // Blora [N, r]
   __nv_bfloat16* out;   // [M, L]
   uint32_t* status;     // device status word
   int M, N, K;          // problem dims of the frozen weight W[N,K] and tokens M
   int rank;             // 0 disables the LoRA stage
+  int tma_store;        // 1: full tiles leave through the output tensor map
   // Grouped (MoE) launches: tile list {expert, first row, end row, weight tile}
   // over expert-sorted token rows, its length on the device; null for one weight.
   const int4* tiles;
@@ -76,24 +85,64 @@ struct __align__(16) GemmBarriers {
   uint64_t full[kStages];   // TMA bytes landed
   uint64_t afull[kStages];  // leader: both CTAs' dequant warps finished the TMEM A stage
   uint64_t empty[kStages];  // MMAs reading the stage completed
-  uint64_t accum;           // all MMAs completed
+  uint64_t accum;           // all MMAs of the current tile completed (one phase per tile)
+  uint64_t acc_empty;       // leader: both CTAs' epilogue warps drained the accumulator
   uint32_t tmem_base;
   uint32_t abort_word;
   alignas(16) float lut[16];  // codebook copy for the decoders
 };
 
-constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * (kXBytes + kQBytes) + sizeof(GemmBarriers);
+constexpr int kYBytes = kTok * kLanes * 2;  // 64 KiB bf16 output staging tile [256 tokens][128 columns]
+constexpr int kEpiWarps = 4 * kGroups;
+constexpr int kSmemBytes =
+    1024 /*align slack*/ + kStages * (kXBytes + kQBytes) + kYBytes + static_cast<int>(sizeof(GemmBarriers));
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
+// Tile t of the launch: grouped launches read the list; dense ones walk a
+// banded order in which pairs that run at the same time cover a band of
+// kGroupM token tiles x several weight tiles, so an activation tile is
+// requested by a handful of pairs at once instead of by every SM.
+struct Tile {
+  int expert, m0, m_end, w_tile;
+};
+__device__ __forceinline__ Tile tile_at(const GemmArgs& args, int t, int num_w, int num_m) {
+  Tile r;
+  if (args.tiles != nullptr) {
+    const int4 v = args.tiles[t];
+    r.expert = v.x;
+    r.m0 = v.y;
+    r.m_end = v.z;
+    r.w_tile = v.w;
+  } else {
+    const int band = t / (kGroupM * num_w);
+    const int first_m = band * kGroupM;
+    const int rows_in_band = min(kGroupM, num_m - first_m);
+    const int local = t - band * kGroupM * num_w;
+    r.expert = 0;
+    r.m0 = (first_m + local % rows_in_band) * kTok;
+    r.m_end = args.M;
+    r.w_tile = local / rows_in_band;
+  }
+  return r;
+}
+
+// Persistent: each CTA pair walks tiles pair, pair + P, ... (P pairs in the
+// grid, all resident).  The stage ring counters run on across tiles, so the
+// producer prefetches the next tile while the current one finishes; the
+// accumulator is drained into a shared-memory staging tile (released to the
+// MMA issuer as soon as it is read) and leaves by an asynchronous TMA store.
 __global__ void __launch_bounds__(kThreads, 1)
-    fl_tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,   // X or dY, [M, R] bf16, box {64,256}
-                      const __grid_constant__ CUtensorMap tm_low,   // Ts or Us, [M, 64] bf16, box {64,256}
-                      const __grid_constant__ CUtensorMap tm_code,  // payload [N, K/2] u8
+    fl_tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,   // X, [M, K] bf16, box {64, 128}
+                      const __grid_constant__ CUtensorMap tm_low,   // Ts, [M, 64] bf16, box {64, 128}
+                      const __grid_constant__ CUtensorMap tm_code,  // payload [E*N, K/2] u8
+                      const __grid_constant__ CUtensorMap tm_out,   // Y [M, N] bf16, box {128, 256}
                       const GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* xs = smem;                                   // kStages x 32 KiB (1024-aligned)
+  uint8_t* xs = smem;                                   // kStages x 16 KiB (1024-aligned)
   uint8_t* qs = smem + kStages * kXBytes;               // kStages x 4 KiB
-  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(qs + kStages * kQBytes);
+  __nv_bfloat16* ys = reinterpret_cast<__nv_bfloat16*>(qs + kStages * kQBytes);  // 64 KiB staging
+  GemmBarriers* bars = reinterpret_cast<GemmBarriers*>(qs + kStages * kQBytes + kYBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -102,38 +151,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int R = K;   // reduction dimension
   const int groups_per_row = K / 128;
   const uint32_t crank = cluster_ctarank();       // 0 = leader of the CTA pair
-  int w_tile, m_tile;
-  int expert = 0, m_end = M;
-  int m0;                                           // first token of the pair tile
-  if (args.tiles != nullptr) {
-    // MoE: one tile of <= 256 rows of one expert's token segment.  Both CTAs
-    // of the pair read the same entry, so they leave together.
-    const int pair = blockIdx.x >> 1;
-    if (pair >= *args.tile_count) return;
-    const int4 t = args.tiles[pair];
-    expert = t.x;
-    m0 = t.y;
-    m_end = t.z;
-    w_tile = t.w;
-    m_tile = 0;
-  } else {
-    // Grouped tile order: pairs that run at the same time cover a band of
-    // kGroupM token tiles x several weight tiles, so an activation tile is
-    // requested by a handful of pairs at once instead of by every SM.
-    const int num_w = (L + 2 * kLanes - 1) / (2 * kLanes);
-    const int num_m = (M + kTok - 1) / kTok;
-    const int pair = blockIdx.x >> 1;
-    const int band = pair / (kGroupM * num_w);
-    const int first_m = band * kGroupM;
-    const int rows_in_band = min(kGroupM, num_m - first_m);
-    const int local = pair - band * kGroupM * num_w;
-    m_tile = first_m + local % rows_in_band;
-    w_tile = local / rows_in_band;
-    m0 = m_tile * kTok;
-  }
-  const int l0 = w_tile * (2 * kLanes) + static_cast<int>(crank) * kLanes;
-  const int wrow0 = expert * N;                     // this expert's first row in the stacked record
-  const int mh = m0 + static_cast<int>(crank) * kTokHalf;  // first token of this CTA's half
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_w = (L + 2 * kLanes - 1) / (2 * kLanes);
+  const int num_m = (M + kTok - 1) / kTok;
+  const int n_tiles = args.tiles != nullptr ? *args.tile_count : num_w * num_m;
   const int n_main = R / kStageK;
   const bool has_lora = args.rank > 0;
   const int n_iter = n_main + (has_lora ? 1 : 0);
@@ -146,6 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->empty[s], 1);
     }
     mbar_init(&bars->accum, 1);
+    mbar_init(&bars->acc_empty, 2 * kEpiWarps);
     bars->abort_word = 0;
     fence_barrier_init();
   }
@@ -168,25 +191,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_act);
       tma_prefetch_desc(&tm_code);
       if (has_lora) tma_prefetch_desc(&tm_low);
-      int issued = 0;
-      for (int it = 0; it < n_iter; ++it) {
-        const int s = it % kStages;
-        if (it >= kStages &&
-            !mbar_wait(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty))
-          break;
-        if (it < n_main) {
-          const int r0 = it * kStageK;
-          mbar_arrive_expect_tx(&bars->full[s], kXBytes + kQBytes);
-          tma_load_2d(xs + s * kXBytes, &tm_act, r0, mh, &bars->full[s]);
-          tma_load_2d(qs + s * kQBytes, &tm_code, r0 / 2, wrow0 + l0, &bars->full[s]);  // 128 rows x 32 B
-        } else {
-          mbar_arrive_expect_tx(&bars->full[s], kXBytes);
-          tma_load_2d(xs + s * kXBytes, &tm_low, 0, mh, &bars->full[s]);
+      int g = 0;  // stage counter over all tiles of this pair
+      bool ok = true;
+      for (int t = pair; t < n_tiles && ok; t += num_pairs) {
+        const Tile tile = tile_at(args, t, num_w, num_m);
+        const int l0 = tile.w_tile * (2 * kLanes) + static_cast<int>(crank) * kLanes;
+        const int mh = tile.m0 + static_cast<int>(crank) * kTokHalf;
+        const int wrow0 = tile.expert * N;
+        for (int it = 0; it < n_iter; ++it, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages &&
+              !mbar_wait(&bars->empty[s], ((g / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (it < n_main) {
+            const int r0 = it * kStageK;
+            mbar_arrive_expect_tx(&bars->full[s], kXBytes + kQBytes);
+            tma_load_2d(xs + s * kXBytes, &tm_act, r0, mh, &bars->full[s]);
+            tma_load_2d(qs + s * kQBytes, &tm_code, r0 / 2, wrow0 + l0, &bars->full[s]);  // 128 rows x 32 B
+          } else {
+            mbar_arrive_expect_tx(&bars->full[s], kXBytes);
+            tma_load_2d(xs + s * kXBytes, &tm_low, 0, mh, &bars->full[s]);
+          }
         }
-        ++issued;
       }
       // Drain: never leave the CTA with bulk copies still landing in its smem.
-      for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i) {
+      for (int i = g > kStages ? g - kStages : 0; i < g; ++i) {
         const int s = i % kStages;
         uint32_t dummy_abort = 0;
         mbar_wait(&bars->full[s], (i / kStages) & 1, &dummy_abort, args.status, kStatusTimeoutDrain);
@@ -197,123 +228,196 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && crank == 0) {
       const uint32_t idesc = idesc_bf16_f32(2 * kLanes, kTok);
       const int lora_k_steps = (args.rank + 15) / 16;
-      for (int it = 0; it < n_iter; ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        // Every dequant warp of both CTAs arrives only after its own CTA's
-        // TMA bytes for the stage landed, so afull covers both B halves too.
-        if (!mbar_wait_cluster(&bars->afull[s], ph, abort_word, args.status, kStatusTimeoutFull)) break;
+      int g = 0, tl = 0;
+      bool ok = true;
+      for (int t = pair; t < n_tiles && ok; t += num_pairs, ++tl) {
+        // The previous tile's accumulator must have been read out by both CTAs.
+        if (tl > 0 &&
+            !mbar_wait_cluster(&bars->acc_empty, (tl - 1) & 1, abort_word, args.status, kStatusTimeoutAccum))
+          break;
         tc_fence_after();
-        const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(xs + s * kXBytes));
-        const uint32_t a_col = tmem_base + kAccCols + s * kAStageCols;
-        const int ksteps = it < n_main ? kStageK / 16 : lora_k_steps;
-        for (int kk = 0; kk < ksteps; ++kk)
-          mma_ts2(tmem_base, a_col + kk * 8, bdesc + 2 * kk, idesc, (it | kk) != 0 ? 1u : 0u);
-        tc_commit2_mc(&bars->empty[s], 0x3);
+        for (int it = 0; it < n_iter; ++it, ++g) {
+          const int s = g % kStages;
+          const uint32_t ph = (g / kStages) & 1;
+          // Every dequant warp of both CTAs arrives only after its own CTA's
+          // TMA bytes for the stage landed, so afull covers both B halves too.
+          if (!mbar_wait_cluster(&bars->afull[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(xs + s * kXBytes));
+          const uint32_t a_col = tmem_base + kAccCols + s * kAStageCols;
+          const int ksteps = it < n_main ? kStageK / 16 : lora_k_steps;
+          for (int kk = 0; kk < ksteps; ++kk)
+            mma_ts2(tmem_base, a_col + kk * 8, bdesc + 2 * kk, idesc, (it | kk) != 0 ? 1u : 0u);
+          tc_commit2_mc(&bars->empty[s], 0x3);
+        }
+        // Completion of every MMA of the tile (also on the abort path, so TMEM
+        // is never released under an in-flight MMA).
+        tc_commit2_mc(&bars->accum, 0x3);
       }
-      // Completion of every MMA issued above (also on the abort path, so TMEM
-      // is never released under an in-flight MMA).
-      tc_commit2_mc(&bars->accum, 0x3);
-      uint32_t dummy_abort = 0;
-      mbar_wait(&bars->accum, 0, &dummy_abort, args.status, kStatusTimeoutAccum);
+      if (tl > 0) {
+        uint32_t dummy_abort = 0;
+        // The last commit (phase tl-1) covers every MMA this thread issued.
+        mbar_wait(&bars->accum, (tl - 1) & 1, &dummy_abort, args.status, kStatusTimeoutAccum);
+      }
     }
   } else {
     // ----------------------------------- dequant producers (kGroups x 4 warps)
     // Within a group: one warp per TMEM lane quarter decodes the whole stage
     // for its 32 lanes.  Groups take turns on pairs of stages (one 128-wide
     // scale group), so each warp has kGroups pair-times to hide its barrier,
-    // shared-memory and TMEM-store latencies.
+    // shared-memory and TMEM-store latencies.  After the tile's last stage
+    // the same warps drain the accumulator.  Every epilogue warp walks every
+    // tile of the pair (also after an abort) so the named barriers match.
     const int dw = warp - 2;                   // dequant warp index
     const int grp = dw >> 2;                   // stage-pair group of this warp
     const int quarter = warp & 3;              // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;       // lane within the 128-lane tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t afull_leader = mapa_shared(smem_u32(&bars->afull[0]), 0);
+    const uint32_t acc_empty_leader = mapa_shared(smem_u32(&bars->acc_empty), 0);
     const float* lut_s = bars->lut;
+    const bool elected = dw == 0 && lane == 0;  // issues and retires the output TMA stores
     bool ok = true;
 
-    {
+    // Epilogue of tile `tile` (the pair's tl-th): drain the accumulator into
+    // the staging tile, release it to the MMA issuer, store.
+    auto epilogue = [&](const Tile& tile, int tl) {
+      const int l0 = tile.w_tile * (2 * kLanes) + static_cast<int>(crank) * kLanes;
+      // The staging tile is free once the previous tile's store has read it.
+      if (elected) bulk_wait_group_read0();
+      named_barrier_sync(1, 32 * kEpiWarps);
+      bool drained = false;
+      if (ok && mbar_wait_warp(&bars->accum, tl & 1, abort_word, args.status, kStatusTimeoutAccum)) {
+        tc_fence_after();
+        // The kGroups warps of each lane quarter take the 32-column token
+        // chunks round robin: ys[token][row].
+#pragma unroll 1
+        for (int c = 32 * grp; c < kTok; c += 32 * kGroups) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_addr + c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ys[(c + j) * kLanes + row] = __float2bfloat16_rn(__uint_as_float(v[j]));
+        }
+        tc_fence_before();
+        drained = true;
+      } else {
+        ok = false;
+      }
+      // Accumulator read out (or abandoned): release it to the MMA issuer.
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+      fence_proxy_async_smem();
+      named_barrier_sync(1, 32 * kEpiWarps);
+      if (!drained) return;
+      const int rows_here = min(tile.m0 + kTok, M) - tile.m0;
+      const bool partial = tile.m_end < tile.m0 + rows_here;
+      if (args.tma_store && !partial) {
+        if (elected) {
+          tma_store_2d(&tm_out, ys, l0, tile.m0);
+          bulk_commit_group();
+        }
+      } else {
+        // Rows [m0, m_end) only (a grouped tile ends inside the box), or no
+        // output tensor map: 16-byte vectors where the row allows.
+        const int rows = min(tile.m_end, M) - tile.m0;
+        const int tid = threadIdx.x - 64;
+        const bool vec_ok = (L % 8) == 0 && ((reinterpret_cast<uintptr_t>(args.out) & 15u) == 0);
+        for (int idx = tid; idx < rows * (kLanes / 8); idx += 32 * kEpiWarps) {
+          const int r = idx / (kLanes / 8), cc = (idx % (kLanes / 8)) * 8;
+          const int col = l0 + cc;
+          const __nv_bfloat16* src = ys + r * kLanes + cc;
+          __nv_bfloat16* dst = args.out + static_cast<size_t>(tile.m0 + r) * L + col;
+          if (vec_ok && col + 8 <= L) {
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+          } else {
+            for (int e = 0; e < 8 && col + e < L; ++e) dst[e] = src[e];
+          }
+        }
+      }
+    };
+
+    // Order per tile: the group's first stage pair of this tile, then the
+    // previous tile's epilogue, then the rest of this tile.  The first pairs of
+    // all groups fill the stage ring, so the MMA issuer restarts on decoded
+    // stages as soon as the accumulator is released.  Every epilogue warp
+    // walks every tile of the pair (also after an abort): the named barriers
+    // inside the epilogue always match.
+    int g0 = 0;  // stage counter at the start of the tile
+    int tl = 0;
+    Tile prev{};
+    for (int t = pair; t < n_tiles; t += num_pairs, g0 += n_iter, ++tl) {
+      const Tile tile = tile_at(args, t, num_w, num_m);
+      const int l0 = tile.w_tile * (2 * kLanes) + static_cast<int>(crank) * kLanes;
+      const int wrow0 = tile.expert * N;
       // Thread owns weight row n; each stage it decodes the 64 k of the stage
       // (32 TMEM columns).
       const int n = l0 + row;
       const bool valid = n < N;
       const float* srow = args.scales + static_cast<size_t>(wrow0 + (valid ? n : 0)) * groups_per_row;
-      float next_scale = (valid && 2 * grp < 2 * groups_per_row) ? __ldg(srow + grp) : 0.0f;
-      for (int pit = 2 * grp; pit < n_iter && ok; pit += 2 * kGroups) {
-        ProductTable table;
-        if (pit < n_main) {
-          table = make_table(lut_s, next_scale);
-          const int g_next = pit / 2 + kGroups;
-          next_scale = (valid && g_next < groups_per_row) ? __ldg(srow + g_next) : 0.0f;
-        }
-        for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
-          if (it >= kStages &&
-              !mbar_wait_warp(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
-            ok = false;
-            break;
+      float next_scale = (valid && grp < groups_per_row) ? __ldg(srow + grp) : 0.0f;
+      for (int pit = 2 * grp; pit < n_iter || (pit == 2 * grp && tl > 0); pit += 2 * kGroups) {
+        if (pit < n_iter && ok) {
+          ProductTable table;
+          if (pit < n_main) {
+            table = make_table(lut_s, next_scale);
+            const int g_next = pit / 2 + kGroups;
+            next_scale = (valid && g_next < groups_per_row) ? __ldg(srow + g_next) : 0.0f;
           }
-          if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
-            ok = false;
-            break;
-          }
-          uint32_t v[32];
-          if (it < n_main) {
-            const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + row * 32);
-            const uint4 q0 = q[0], q1 = q[1];
-            lookup8(table, q0.x, v + 0);
-            lookup8(table, q0.y, v + 4);
-            lookup8(table, q0.z, v + 8);
-            lookup8(table, q0.w, v + 12);
-            lookup8(table, q1.x, v + 16);
-            lookup8(table, q1.y, v + 20);
-            lookup8(table, q1.z, v + 24);
-            lookup8(table, q1.w, v + 28);
-          } else {
-            // LoRA stage: A row = bf16(Blora[n, 0:64]) zero padded past the rank.
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int c0 = 2 * j, c1 = c0 + 1;
-              const float a = (valid && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c0) : 0.f;
-              const float b = (valid && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c1) : 0.f;
-              v[j] = pack_bf16x2(a, b);
+          for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
+            const int gi = g0 + it;
+            const int s = gi % kStages;
+            const uint32_t ph = (gi / kStages) & 1;
+            if (gi >= kStages &&
+                !mbar_wait_warp(&bars->empty[s], ((gi / kStages) - 1) & 1, abort_word, args.status,
+                                kStatusTimeoutEmpty)) {
+              ok = false;
+              break;
             }
-          }
-          tc_fence_after();
-          tmem_st_32x32b_x32(tmem_base + lane_addr + kAccCols + s * kAStageCols, v);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(afull_leader + s * 8);
-        }
-      }
-    }
-    // A group that stopped early (abort) must not leave others waiting forever:
-    // the bounded waits and the abort word end them.
-    ok = __all_sync(0xffffffffu, ok) != 0;
-
-    // ------------------------------------------------------------ epilogue
-    // The kGroups warps of each lane quarter take the 32-column token chunks
-    // round robin.
-    if (ok && mbar_wait_warp(&bars->accum, 0, abort_word, args.status, kStatusTimeoutAccum)) {
-      tc_fence_after();
-      const int l = l0 + row;
-      const bool lvalid = l < L;
-#pragma unroll 1
-      for (int c = 32 * grp; c < kTok; c += 32 * kGroups) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + c, v);
-        tmem_wait_ld();
-        if (lvalid) {
+            if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            uint32_t v[32];
+            if (it < n_main) {
+              const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + row * 32);
+              const uint4 q0 = q[0], q1 = q[1];
+              lookup8(table, q0.x, v + 0);
+              lookup8(table, q0.y, v + 4);
+              lookup8(table, q0.z, v + 8);
+              lookup8(table, q0.w, v + 12);
+              lookup8(table, q1.x, v + 16);
+              lookup8(table, q1.y, v + 20);
+              lookup8(table, q1.z, v + 24);
+              lookup8(table, q1.w, v + 28);
+            } else {
+              // LoRA stage: A row = bf16(Blora[n, 0:64]) zero padded past the rank.
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = m0 + c + j;
-            if (m < m_end) args.out[static_cast<size_t>(m) * L + l] = __float2bfloat16_rn(__uint_as_float(v[j]));
+              for (int j = 0; j < 32; ++j) {
+                const int c0 = 2 * j, c1 = c0 + 1;
+                const float a = (valid && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c0) : 0.f;
+                const float b = (valid && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c1) : 0.f;
+                v[j] = pack_bf16x2(a, b);
+              }
+            }
+            tc_fence_after();
+            tmem_st_32x32b_x32(tmem_base + lane_addr + kAccCols + s * kAStageCols, v);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(afull_leader + s * 8);
           }
+          ok = __all_sync(0xffffffffu, ok) != 0;
         }
+        if (pit == 2 * grp && tl > 0) epilogue(prev, tl - 1);
       }
+      prev = tile;
     }
+    if (tl > 0) epilogue(prev, tl - 1);
+    if (elected) bulk_wait_group0();
   }
 
   tc_fence_before();
@@ -331,6 +435,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------------ host side
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "fl_host.h"
 
@@ -368,6 +476,45 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
   return FL_OK;
 }
 
+// Number of 2-CTA clusters of `kernel` (1 CTA per SM, `smem` dynamic bytes)
+// that fit on the current device at once; sets the kernel's shared-memory
+// limit on first use per device.
+int resident_pairs(const void* kernel, int threads, int smem, int* pairs) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> cache;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({kernel, dev});
+  if (it != cache.end()) {
+    *pairs = it->second;
+    return FL_OK;
+  }
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+  if (e != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    return set_error(FL_ERR_CUDA, "cluster occupancy query failed: %s", cudaGetErrorString(e));
+  }
+  cache[{kernel, dev}] = n;
+  *pairs = n;
+  return FL_OK;
+}
+
 // x: [M, K] bf16 activations; ts: [M, 64] bf16 scaled low-rank activations
 // (unused when rank == 0); codes/scales/lut: the frozen record W[N, K];
 // blora: [N, rank] fp32; y: [M, N] bf16.
@@ -388,6 +535,14 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
   rc = make_tensor_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, static_cast<uint64_t>(N) * experts,
                           K / 2, 32, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
+  // Output tiles leave by TMA when the row pitch and base allow it.
+  const bool tma_store = (N % 8) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+  CUtensorMap tm_out = tm_act;
+  if (tma_store) {
+    rc = make_tensor_map_2d(&tm_out, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, static_cast<uint64_t>(N) * 2, kLanes,
+                            kTok, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
   GemmArgs a;
   a.scales = scales;
   a.lut = lut;
@@ -398,12 +553,19 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
   a.N = N;
   a.K = K;
   a.rank = rank;
+  a.tma_store = tma_store ? 1 : 0;
   a.tiles = tiles;
   a.tile_count = tile_count;
-  // CTA pairs: each pair covers 256 W rows x 256 tokens (grouped: one listed tile).
-  dim3 grid(tiles ? 2 * max_tiles : 2 * ((N + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok));
+  // Persistent CTA pairs (each tile: 256 W rows x 256 tokens), no more than
+  // can be resident at once.
+  const int tiles_max = tiles ? max_tiles : ((N + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok);
+  int pairs = 0;
+  if ((rc = resident_pairs(reinterpret_cast<const void*>(&fl_tc_gemm_kernel), kThreads, kSmemBytes, &pairs)))
+    return rc;
+  if (pairs > tiles_max) pairs = tiles_max;
+  if (pairs < 1) return FL_OK;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
+  cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
@@ -414,14 +576,7 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&fl_tc_gemm_kernel),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    attr_set = true;
-  }
-  cudaError_t le = cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel, tm_act, tm_low, tm_code, a);
+  cudaError_t le = cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel, tm_act, tm_low, tm_code, tm_out, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "fwd gemm launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }

@@ -19,9 +19,13 @@
 //   * Every accumulator lane is one token row of dX, so the epilogue writes 64
 //     contiguous bytes per thread per 32-column chunk.
 //   * The extra LoRA stage uses A = the Us tile, B = bf16(Alora[0:64, k]).
+// Persistent CTA pairs over a static tile list with two TMEM accumulators
+// (512 columns): tile t+1 accumulates while tile t drains.
 // Warp roles (448 threads per CTA): warp 0 TMA producer, warp 1 TMEM owner (both
 // CTAs) + MMA issuer (leader), warps 2-13 three groups of four decode warps that
-// take turns on stages, then the epilogue.  Barriers as in fl_gemm.cu.
+// take turns on stages and drain the previous tile's accumulator after their
+// first stage pair of the next one.  Barriers as in fl_gemm.cu, with
+// accum/acc_empty per accumulator.
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -38,8 +42,9 @@ constexpr int kStages = 6;
 constexpr int kGroupM = 4;                 // token tiles per band: a band's pairs fit in one wave, so each dY slab is read once
 constexpr int kGroups = 3;                 // decode warp groups
 constexpr int kThreads = 64 + 128 * kGroups;
+constexpr int kEpiWarps = 4 * kGroups;
 constexpr int kAccCols = 256;              // fp32 accumulator columns (pair N)
-constexpr int kTmemCols = 256;
+constexpr int kTmemCols = 2 * kAccCols;    // two accumulators: tile t+1 accumulates while tile t drains
 constexpr int kABytes = kTokHalf * kStageN * 2;   // 16 KiB dY (or Us) tile
 constexpr int kBBytes = kColHalf * kStageN * 2;   // 16 KiB decoded W tile
 constexpr int kQBytes = kStageN * kColHalf / 2;   // 4 KiB packed codes
@@ -50,7 +55,8 @@ struct __align__(16) Barriers {
   uint64_t full[kStages];
   uint64_t afull[kStages];
   uint64_t empty[kStages];
-  uint64_t accum;
+  uint64_t accum[2];        // accumulator b holds a finished tile (one phase per use)
+  uint64_t acc_empty[2];    // leader: both CTAs' epilogue warps drained accumulator b
   uint32_t tmem_base;
   uint32_t abort_word;
   alignas(16) float lut[16];
@@ -61,7 +67,7 @@ constexpr int kSmemBytes = 1024 + kStages * (kABytes + kBBytes + kQBytes) + size
 struct Args {
   const float* scales;
   const float* lut;
-  const float* alora;   // [r, K]
+  const float* alora;   // [r, K] (grouped: [E, r, K])
   __nv_bfloat16* out;   // dX [M, K]
   uint32_t* status;
   int M, N, K, rank;
@@ -75,10 +81,40 @@ __device__ __forceinline__ uint32_t b_offset(int r, int khalf, int j) {
   return khalf * kBLbo + (r >> 3) * kBSbo + (r & 7) * 128 + ((j ^ (r & 7)) << 4);
 }
 
+struct Tile {
+  int expert, m0, m_end, k_tile;
+};
+// Tile t: grouped launches read the list; dense ones walk bands of kGroupM
+// token tiles x all column tiles, so a band's dY slab is read by pairs that
+// run together.
+__device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int num_m) {
+  Tile r;
+  if (args.tiles != nullptr) {
+    const int4 v = args.tiles[t];
+    r.expert = v.x;
+    r.m0 = v.y;
+    r.m_end = v.z;
+    r.k_tile = v.w;
+  } else {
+    const int band = t / (kGroupM * num_k);
+    const int first_m = band * kGroupM;
+    const int rows_in_band = min(kGroupM, num_m - first_m);
+    const int local = t - band * kGroupM * num_k;
+    r.expert = 0;
+    r.m0 = (first_m + local % rows_in_band) * 2 * kTokHalf;
+    r.m_end = args.M;
+    r.k_tile = local / rows_in_band;
+  }
+  return r;
+}
+
+// Persistent: each CTA pair walks tiles pair, pair + P, ...; stage counters
+// run on across tiles and the two TMEM accumulators alternate, so the MMAs of
+// the next tile overlap the drain of the previous one.
 __global__ void __launch_bounds__(kThreads, 1)
     fl_bwd_ss_kernel(const __grid_constant__ CUtensorMap tm_dy,    // dY [M, N] bf16, box {64, 128}
                      const __grid_constant__ CUtensorMap tm_us,    // Us [M, 64] bf16, box {64, 128}
-                     const __grid_constant__ CUtensorMap tm_code,  // payload [N, K/2] u8, box {64, 64}
+                     const __grid_constant__ CUtensorMap tm_code,  // payload [E*N, K/2] u8, box {64, 64}
                      const Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -92,33 +128,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int M = args.M, N = args.N, K = args.K;
   const int groups_per_row = K / 128;
   const uint32_t crank = cluster_ctarank();
-  int k_tile, m_tile = 0;
-  int expert = 0, m_end = M, m0;
-  if (args.tiles != nullptr) {
-    const int pair = blockIdx.x >> 1;
-    if (pair >= *args.tile_count) return;
-    const int4 t = args.tiles[pair];
-    expert = t.x;
-    m0 = t.y;
-    m_end = t.z;
-    k_tile = t.w;
-  } else {
-    const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
-    const int num_m = (M + 2 * kTokHalf - 1) / (2 * kTokHalf);
-    const int pair = blockIdx.x >> 1;
-    const int band = pair / (kGroupM * num_k);
-    const int first_m = band * kGroupM;
-    const int rows_in_band = min(kGroupM, num_m - first_m);
-    const int local = pair - band * kGroupM * num_k;
-    m_tile = first_m + local % rows_in_band;
-    k_tile = local / rows_in_band;
-    m0 = m_tile * 2 * kTokHalf;                               // first token of the pair tile
-  }
-  const int k0 = k_tile * 2 * kColHalf;                       // first column of the pair tile
-  const int kb = k0 + static_cast<int>(crank) * kColHalf;     // first column of this CTA's B half
-  const int wrow0 = expert * N;                               // expert's first row in the stacked record
-  const float* alora = args.alora + static_cast<size_t>(expert) * args.rank * K;
-  const int mh = m0 + static_cast<int>(crank) * kTokHalf;     // first token of this CTA's A half
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
+  const int num_m = (M + 2 * kTokHalf - 1) / (2 * kTokHalf);
+  const int n_tiles = args.tiles != nullptr ? *args.tile_count : num_k * num_m;
   const int n_main = N / kStageN;
   const bool has_lora = args.rank > 0;
   const int n_iter = n_main + (has_lora ? 1 : 0);
@@ -130,7 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->afull[s], 2 * 4);
       mbar_init(&bars->empty[s], 1);
     }
-    mbar_init(&bars->accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->accum[b], 1);
+      mbar_init(&bars->acc_empty[b], 2 * kEpiWarps);
+    }
     bars->abort_word = 0;
     fence_barrier_init();
   }
@@ -151,24 +168,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_dy);
       tma_prefetch_desc(&tm_code);
       if (has_lora) tma_prefetch_desc(&tm_us);
-      int issued = 0;
-      for (int it = 0; it < n_iter; ++it) {
-        const int s = it % kStages;
-        if (it >= kStages &&
-            !mbar_wait(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty))
-          break;
-        if (it < n_main) {
-          const int n0 = it * kStageN;
-          mbar_arrive_expect_tx(&bars->full[s], kABytes + kQBytes);
-          tma_load_2d(as + s * kABytes, &tm_dy, n0, mh, &bars->full[s]);
-          tma_load_2d(qs + s * kQBytes, &tm_code, kb / 2, wrow0 + n0, &bars->full[s]);
-        } else {
-          mbar_arrive_expect_tx(&bars->full[s], kABytes);
-          tma_load_2d(as + s * kABytes, &tm_us, 0, mh, &bars->full[s]);
+      int g = 0;
+      bool ok = true;
+      for (int t = pair; t < n_tiles && ok; t += num_pairs) {
+        const Tile tile = tile_at(args, t, num_k, num_m);
+        const int kb = tile.k_tile * 2 * kColHalf + static_cast<int>(crank) * kColHalf;
+        const int mh = tile.m0 + static_cast<int>(crank) * kTokHalf;
+        const int wrow0 = tile.expert * N;
+        for (int it = 0; it < n_iter; ++it, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages &&
+              !mbar_wait(&bars->empty[s], ((g / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (it < n_main) {
+            const int n0 = it * kStageN;
+            mbar_arrive_expect_tx(&bars->full[s], kABytes + kQBytes);
+            tma_load_2d(as + s * kABytes, &tm_dy, n0, mh, &bars->full[s]);
+            tma_load_2d(qs + s * kQBytes, &tm_code, kb / 2, wrow0 + n0, &bars->full[s]);
+          } else {
+            mbar_arrive_expect_tx(&bars->full[s], kABytes);
+            tma_load_2d(as + s * kABytes, &tm_us, 0, mh, &bars->full[s]);
+          }
         }
-        ++issued;
       }
-      for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i) {
+      for (int i = g > kStages ? g - kStages : 0; i < g; ++i) {
         uint32_t dummy_abort = 0;
         mbar_wait(&bars->full[i % kStages], (i / kStages) & 1, &dummy_abort, args.status, kStatusTimeoutDrain);
       }
@@ -178,21 +203,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && crank == 0) {
       const uint32_t idesc = idesc_bf16_f32_bmn(2 * kTokHalf, 2 * kColHalf);
       const int lora_k_steps = (args.rank + 15) / 16;
-      for (int it = 0; it < n_iter; ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait_cluster(&bars->afull[s], ph, abort_word, args.status, kStatusTimeoutFull)) break;
+      int g = 0, tl = 0;
+      bool ok = true;
+      for (int t = pair; t < n_tiles && ok; t += num_pairs, ++tl) {
+        const int b = tl & 1;
+        // Accumulator b was last used by tile tl-2: both CTAs must have drained it.
+        if (tl >= 2 &&
+            !mbar_wait_cluster(&bars->acc_empty[b], ((tl >> 1) - 1) & 1, abort_word, args.status, kStatusTimeoutAccum))
+          break;
         tc_fence_after();
-        const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(as + s * kABytes));
-        const uint64_t bdesc = sdesc_mnmajor_sw128(smem_u32(bs + s * kBBytes), kBLbo, kBSbo);
-        const int ksteps = it < n_main ? kStageN / 16 : lora_k_steps;
-        for (int kk = 0; kk < ksteps; ++kk)
-          mma_ss2(tmem_base, adesc + 2 * kk, bdesc + ((2 * kBSbo) >> 4) * kk, idesc, (it | kk) != 0 ? 1u : 0u);
-        tc_commit2_mc(&bars->empty[s], 0x3);
+        const uint32_t acc = tmem_base + b * kAccCols;
+        for (int it = 0; it < n_iter; ++it, ++g) {
+          const int s = g % kStages;
+          const uint32_t ph = (g / kStages) & 1;
+          if (!mbar_wait_cluster(&bars->afull[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(as + s * kABytes));
+          const uint64_t bdesc = sdesc_mnmajor_sw128(smem_u32(bs + s * kBBytes), kBLbo, kBSbo);
+          const int ksteps = it < n_main ? kStageN / 16 : lora_k_steps;
+          for (int kk = 0; kk < ksteps; ++kk)
+            mma_ss2(acc, adesc + 2 * kk, bdesc + ((2 * kBSbo) >> 4) * kk, idesc, (it | kk) != 0 ? 1u : 0u);
+          tc_commit2_mc(&bars->empty[s], 0x3);
+        }
+        tc_commit2_mc(&bars->accum[b], 0x3);
       }
-      tc_commit2_mc(&bars->accum, 0x3);
-      uint32_t dummy_abort = 0;
-      mbar_wait(&bars->accum, 0, &dummy_abort, args.status, kStatusTimeoutAccum);
+      if (tl > 0) {
+        // The last commit covers every MMA this thread issued.
+        uint32_t dummy_abort = 0;
+        const int last = tl - 1;
+        mbar_wait(&bars->accum[last & 1], (last >> 1) & 1, &dummy_abort, args.status, kStatusTimeoutAccum);
+      }
     }
   } else {
     // ------------------------------------------------------------ decode warps
@@ -202,99 +245,129 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = t >> 1;                    // reduction row within the stage (0..63)
     const int khalf = t & 1;                 // which 64 of the CTA's 128 columns
     const uint32_t afull_leader = mapa_shared(smem_u32(&bars->afull[0]), 0);
-    const bool tile_valid = kb < K;
-    const int g = tile_valid ? kb / 128 : 0;  // the CTA's 128 columns share one scale group
-    bool ok = true;
-    // The row's scale for the next stage this group owns is loaded one owned
-    // stage ahead (stages 2g, 2g+1, 2g+2*kGroups, ...).
-    auto load_scale = [&](int it) {
-      return (tile_valid && it < n_main)
-                 ? __ldg(args.scales + static_cast<size_t>(wrow0 + it * kStageN + r) * groups_per_row + g)
-                 : 0.0f;
-    };
-    float next_scale = load_scale(2 * grp);
-    for (int pit = 2 * grp; pit < n_iter && ok; pit += 2 * kGroups) {
-      for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        if (it >= kStages &&
-            !mbar_wait_warp(&bars->empty[s], ((it / kStages) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) {
-          ok = false;
-          break;
-        }
-        uint32_t v[32];
-        const float scale = next_scale;
-        next_scale = load_scale((it & 1) == 0 ? it + 1 : it + 2 * kGroups - 1);
-        if (it < n_main) {
-          const ProductTable table = make_table(bars->lut, scale);
-          if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
-            ok = false;
-            break;
-          }
-          const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + r * 64 + khalf * 32);
-          const uint4 q0 = q[0], q1 = q[1];
-          lookup8(table, q0.x, v + 0);
-          lookup8(table, q0.y, v + 4);
-          lookup8(table, q0.z, v + 8);
-          lookup8(table, q0.w, v + 12);
-          lookup8(table, q1.x, v + 16);
-          lookup8(table, q1.y, v + 20);
-          lookup8(table, q1.z, v + 24);
-          lookup8(table, q1.w, v + 28);
-        } else {
-          // LoRA stage: row r of B is bf16(Alora[r, kb + 64*khalf .. +64]), zero past the rank.
-          if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
-            ok = false;
-            break;
-          }
-          const bool live = tile_valid && r < args.rank;
-          const float* src = alora + static_cast<size_t>(live ? r : 0) * K + kb + 64 * khalf;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float2 a = make_float2(0.f, 0.f);
-            if (live) a = __ldg(reinterpret_cast<const float2*>(src) + j);
-            v[j] = pack_bf16x2(a.x, a.y);
-          }
-        }
-        uint8_t* dst = bs + s * kBBytes;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<uint4*>(dst + b_offset(r, khalf, j)) = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(afull_leader + s * 8);
-      }
-    }
-    ok = __all_sync(0xffffffffu, ok) != 0;
-
-    // ------------------------------------------------------------ epilogue
-    // Lane quarter q holds tokens mh + 32q .. +32; each thread writes its token
-    // row's columns in 32-wide chunks, the groups taking chunks round robin.
+    const uint32_t acc_empty_leader = mapa_shared(smem_u32(&bars->acc_empty[0]), 0);
     const int quarter = warp & 3;
-    const int m = mh + quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    if (ok && mbar_wait_warp(&bars->accum, 0, abort_word, args.status, kStatusTimeoutAccum)) {
-      tc_fence_after();
+    bool ok = true;
+
+    // Epilogue of the pair's tl-th tile: lane quarter q holds tokens
+    // mh + 32q .. +32; each thread writes its token row's columns in 32-wide
+    // chunks (64 contiguous bytes), the groups taking chunks round robin.
+    auto epilogue = [&](const Tile& tile, int tl) {
+      const int b = tl & 1;
+      const int m = tile.m0 + static_cast<int>(crank) * kTokHalf + quarter * 32 + lane;
+      const int k0 = tile.k_tile * 2 * kColHalf;
+      if (ok && mbar_wait_warp(&bars->accum[b], (tl >> 1) & 1, abort_word, args.status, kStatusTimeoutAccum)) {
+        tc_fence_after();
 #pragma unroll 1
-      for (int c = 32 * grp; c < kAccCols; c += 32 * kGroups) {
-        uint32_t acc[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + c, acc);
-        tmem_wait_ld();
-        const int kcol = k0 + c;
-        if (m < m_end && kcol < K) {
-          uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(m) * K + kcol);
+        for (int c = 32 * grp; c < kAccCols; c += 32 * kGroups) {
+          uint32_t acc[32];
+          tmem_ld_32x32b_x32(tmem_base + b * kAccCols + lane_addr + c, acc);
+          tmem_wait_ld();
+          const int kcol = k0 + c;
+          if (m < tile.m_end && kcol < K) {
+            uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(m) * K + kcol);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 o;
-            o.x = pack_bf16x2(__uint_as_float(acc[8 * j + 0]), __uint_as_float(acc[8 * j + 1]));
-            o.y = pack_bf16x2(__uint_as_float(acc[8 * j + 2]), __uint_as_float(acc[8 * j + 3]));
-            o.z = pack_bf16x2(__uint_as_float(acc[8 * j + 4]), __uint_as_float(acc[8 * j + 5]));
-            o.w = pack_bf16x2(__uint_as_float(acc[8 * j + 6]), __uint_as_float(acc[8 * j + 7]));
-            dst[j] = o;
+            for (int j = 0; j < 4; ++j) {
+              uint4 o;
+              o.x = pack_bf16x2(__uint_as_float(acc[8 * j + 0]), __uint_as_float(acc[8 * j + 1]));
+              o.y = pack_bf16x2(__uint_as_float(acc[8 * j + 2]), __uint_as_float(acc[8 * j + 3]));
+              o.z = pack_bf16x2(__uint_as_float(acc[8 * j + 4]), __uint_as_float(acc[8 * j + 5]));
+              o.w = pack_bf16x2(__uint_as_float(acc[8 * j + 6]), __uint_as_float(acc[8 * j + 7]));
+              dst[j] = o;
+            }
           }
         }
+        tc_fence_before();
+      } else {
+        ok = false;
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader + b * 8);
+    };
+
+    // Per tile: the group's first stage pair, then the previous tile's
+    // epilogue, then the rest; the other accumulator keeps the MMAs busy.
+    int g0 = 0;
+    int tl = 0;
+    Tile prev{};
+    for (int tt = pair; tt < n_tiles; tt += num_pairs, g0 += n_iter, ++tl) {
+      const Tile tile = tile_at(args, tt, num_k, num_m);
+      const int kb = tile.k_tile * 2 * kColHalf + static_cast<int>(crank) * kColHalf;
+      const int wrow0 = tile.expert * N;
+      const float* alora = args.alora + static_cast<size_t>(tile.expert) * args.rank * K;
+      const bool tile_valid = kb < K;
+      const int gsc = tile_valid ? kb / 128 : 0;  // the CTA's 128 columns share one scale group
+      // The row's scale for the next stage this group owns is loaded one owned
+      // stage ahead (stages 2g, 2g+1, 2g+2*kGroups, ...).
+      auto load_scale = [&](int it) {
+        return (tile_valid && it < n_main)
+                   ? __ldg(args.scales + static_cast<size_t>(wrow0 + it * kStageN + r) * groups_per_row + gsc)
+                   : 0.0f;
+      };
+      float next_scale = load_scale(2 * grp);
+      for (int pit = 2 * grp; pit < n_iter || (pit == 2 * grp && tl > 0); pit += 2 * kGroups) {
+        if (pit < n_iter && ok) {
+          for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
+            const int gi = g0 + it;
+            const int s = gi % kStages;
+            const uint32_t ph = (gi / kStages) & 1;
+            if (gi >= kStages &&
+                !mbar_wait_warp(&bars->empty[s], ((gi / kStages) - 1) & 1, abort_word, args.status,
+                                kStatusTimeoutEmpty)) {
+              ok = false;
+              break;
+            }
+            uint32_t v[32];
+            const float scale = next_scale;
+            next_scale = load_scale((it & 1) == 0 ? it + 1 : it + 2 * kGroups - 1);
+            if (it < n_main) {
+              const ProductTable table = make_table(bars->lut, scale);
+              if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+                ok = false;
+                break;
+              }
+              const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + r * 64 + khalf * 32);
+              const uint4 q0 = q[0], q1 = q[1];
+              lookup8(table, q0.x, v + 0);
+              lookup8(table, q0.y, v + 4);
+              lookup8(table, q0.z, v + 8);
+              lookup8(table, q0.w, v + 12);
+              lookup8(table, q1.x, v + 16);
+              lookup8(table, q1.y, v + 20);
+              lookup8(table, q1.z, v + 24);
+              lookup8(table, q1.w, v + 28);
+            } else {
+              // LoRA stage: row r of B is bf16(Alora[r, kb + 64*khalf .. +64]), zero past the rank.
+              if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
+                ok = false;
+                break;
+              }
+              const bool live = tile_valid && r < args.rank;
+              const float* src = alora + static_cast<size_t>(live ? r : 0) * K + kb + 64 * khalf;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float2 a = make_float2(0.f, 0.f);
+                if (live) a = __ldg(reinterpret_cast<const float2*>(src) + j);
+                v[j] = pack_bf16x2(a.x, a.y);
+              }
+            }
+            uint8_t* dst = bs + s * kBBytes;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<uint4*>(dst + b_offset(r, khalf, j)) =
+                  make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(afull_leader + s * 8);
+          }
+          ok = __all_sync(0xffffffffu, ok) != 0;
+        }
+        if (pit == 2 * grp && tl > 0) epilogue(prev, tl - 1);
+      }
+      prev = tile;
     }
+    if (tl > 0) epilogue(prev, tl - 1);
   }
 
   tc_fence_before();
@@ -320,6 +393,8 @@ namespace fl {
 int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
 
+// Persistent CTA pairs, no more than can be resident at once (each tile:
+// 256 tokens x 256 columns of dX).
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles) {
@@ -352,8 +427,13 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   a.rank = rank;
   a.tiles = tiles;
   a.tile_count = tile_count;
-  const int pairs = tiles ? max_tiles
-                          : ((K + 2 * kColHalf - 1) / (2 * kColHalf)) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf));
+  const int tiles_max = tiles ? max_tiles
+                              : ((K + 2 * kColHalf - 1) / (2 * kColHalf)) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf));
+  int pairs = 0;
+  if ((rc = resident_pairs(reinterpret_cast<const void*>(&fl_bwd_ss_kernel), kThreads, kSmemBytes, &pairs)))
+    return rc;
+  if (pairs > tiles_max) pairs = tiles_max;
+  if (pairs < 1) return FL_OK;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);
@@ -366,13 +446,6 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&fl_bwd_ss_kernel),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    attr_set = true;
-  }
   cudaError_t le = cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel, tm_dy, tm_us, tm_code, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "bwd gemm launch: %s", cudaGetErrorString(le));
   return FL_OK;

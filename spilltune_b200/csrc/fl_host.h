@@ -21,6 +21,10 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
                     cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
                     int experts = 1, int max_tiles = 0);
 
+// 2-CTA clusters of `kernel` that can be resident at once on the current
+// device (also raises the kernel's dynamic shared-memory limit to `smem`).
+int resident_pairs(const void* kernel, int threads, int smem, int* pairs);
+
 // Tile list over expert segments: seg[0..E] (device int32 prefix offsets of the
 // expert-sorted rows); each entry {expert, first row, end row, column tile} for
 // `rows` rows x `col_tiles` column tiles; count written to *count.
@@ -40,12 +44,16 @@ int launch_dequant(const uint8_t* payload, const float* scales, const float* lut
                    cudaStream_t stream);
 
 // out[m, j] = bf16(s * sum_r P[m, r] * Q(j, r)), j < rank, zero for rank <= j < 64.
-// Q(j, r) = q[j * q_sj + r * q_sr] (fp32).
+// Q(j, r) = q[j * q_sj + r * q_sr] (fp32).  qc_scratch: lora_factor_bytes(R,
+// rank) per expert, 16-byte aligned (the converted factor).
 // Grouped (MoE) form: 128-row tiles over expert-sorted rows, the factor of tile
-// t at q + tiles[t].x * q_expert_stride.
+// t at q + tiles[t].x * q_expert_stride, `experts` factors converted.
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
-                     float s, void* out64, cudaStream_t stream, const int4* tiles = nullptr,
-                     const int* tile_count = nullptr, int max_tiles = 0, int64_t q_expert_stride = 0);
+                     float s, void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles = nullptr,
+                     const int* tile_count = nullptr, int max_tiles = 0, int64_t q_expert_stride = 0,
+                     int experts = 1);
+int lora_nq(int rank);                           // rank padded to 16, 32 or 64
+size_t lora_factor_bytes(int64_t R, int rank);   // converted-factor scratch for a reduction of R
 
 // out(p, j) (+)= sum_m P[m, p] * Q[m, j]  (P bf16 [M, Pdim], Q bf16 [M, 64]),
 // out(p, j) = out[p * o_sp + j * o_sj] fp32, j < rank.

@@ -6,13 +6,25 @@
 // finetune/lora.py:219) -> Ts;  backward: P = dY, Q = Blora^T (the VJP factor
 // dY.float() @ B, training/recompute.py:102-105) -> Us.
 //
-// HBM-bound: it streams P once.  Each CTA owns 128 rows of P and one slice of
-// the reduction dimension; the 4 CTAs of a cluster split the reduction and
-// add their partial sums through distributed shared memory, so no workspace
-// is needed.  P tiles arrive by TMA (128-byte swizzle); two warps turn the
-// matching chunk of the FP32 factor into a bf16 hi/lo pair (~16 mantissa bits)
-// in the same swizzled K-major layout; one thread issues tcgen05 MMAs
-// (M = 128 rows, N = padded rank, K = 64 per stage) into a TMEM accumulator.
+// HBM-bound: it streams P once, so the kernel is built for memory-level
+// parallelism.
+//  * A prepass turns the FP32 factor into a bf16 hi/lo pair (hi + lo equals
+//    the FP32 value to ~16 mantissa bits) laid out in the order the warp MMA
+//    fragments read it, [plane][unit u of 64 r][j][c][16]: a warp's fragment
+//    loads are 1 KiB contiguous and stay in L1 for the CTA's other warps.
+//  * A producer warp streams each 64-wide unit of the CTA's 128 rows into a
+//    ring of kStages shared-memory stages: one TMA box {64 columns, 128 rows}
+//    (128-byte swizzle) plus the unit's slice of the converted factor (one
+//    contiguous bulk copy per plane).  Four consumer warps (32 rows each)
+//    read both from shared memory, so the factor never competes for the
+//    small L1 left next to the stages.  Rows past the segment's end (another
+//    expert's rows in a grouped launch) are read but never stored: every
+//    output row is its own dot product.
+//    The reduction index inside a unit is permuted so that one thread's 16
+//    consecutive r feed four m16n8k16 steps: physical r = 16c + 4i + {0..3}
+//    plays logical k = {2c, 2c+1, 2c+8, 2c+9} of step i, for both operands.
+//  * The CTAs of a cluster split the reduction; their partial sums meet in
+//    distributed shared memory, each CTA finishing 1/split of the rows.
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -20,318 +32,343 @@
 #include "fl_ptx.cuh"
 
 namespace fl {
+
+int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+
 namespace ld {
 
-constexpr int kRows = 128;
-constexpr int kStageR = 64;
-constexpr int kSplit = 4;                       // CTAs per cluster along the reduction
-constexpr int kThreads = 128;
-constexpr int kPBytes = kRows * kStageR * 2;    // 16 KiB
+constexpr int kWarps = 4;                       // consumer warps
+constexpr int kRowsPerWarp = 32;
+constexpr int kRows = kWarps * kRowsPerWarp;    // 128 rows per CTA
+constexpr int kThreads = 32 * (kWarps + 1);     // + one producer warp
+constexpr int kMaxSplit = 8;
+constexpr int kStages = 4;
+constexpr int kChunks = 8;                      // 16-byte chunks per thread per unit
+constexpr int kXBytes = kRows * 128;            // 16 KiB: 128 rows x 64 bf16
 
 template <int NQ>
 struct Cfg {
-  static constexpr int kStages = NQ == 64 ? 6 : 4;
-  static constexpr int kQBytes = NQ * kStageR * 2;        // one bf16 plane of the factor chunk
-  static constexpr int kTmemCols = NQ < 32 ? 32 : NQ;
-  static constexpr int kRedBytes = (kSplit - 1) * kRows * NQ * 4;  // peers' partials (reuses P stages)
-  static_assert(kRedBytes <= kStages * kPBytes, "partial buffer must fit in the P stages");
-  static constexpr int kSmemBytes = 1024 + kStages * (kPBytes + 2 * kQBytes) + 256;
+  static constexpr int kQPlane = NQ * 128;      // one plane of a unit's converted factor
+  static constexpr int kStage = kXBytes + 2 * kQPlane;
+  static constexpr int kSmem = 1024 /*align*/ + kStages * kStage + 2 * kStages * 8 /*mbarriers*/ +
+                               kRows * (NQ + 1) * 4;
 };
 
-struct __align__(8) Bars {
-  uint64_t pfull[6];
-  uint64_t qfull[6];
-  uint64_t empty[6];
-  uint64_t accum;
-  uint32_t tmem_base;
-  uint32_t abort_word;
-};
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
-template <int NQ>
-__global__ void __launch_bounds__(kThreads, 1)
-    lora_down_tc_kernel(const __grid_constant__ CUtensorMap tm_p, const float* __restrict__ q, int64_t q_sj,
-                        int64_t q_sr, int rank, float s, __nv_bfloat16* __restrict__ out, int M, int R,
-                        uint32_t* status, const int4* tiles, const int* tile_count, int64_t q_expert_stride) {
-  using C = Cfg<NQ>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ps = smem;                                    // kStages x 16 KiB
-  uint8_t* qh = ps + C::kStages * kPBytes;               // kStages x kQBytes (hi)
-  uint8_t* ql = qh + C::kStages * C::kQBytes;            // kStages x kQBytes (lo)
-  Bars* bars = reinterpret_cast<Bars*>(ql + C::kStages * C::kQBytes);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t crank = cluster_ctarank();
-  int m0 = (blockIdx.x / kSplit) * kRows;
-  int m_end = M;
-  if (tiles != nullptr) {
-    // MoE: one <= 128-row tile of one expert's segment; its factor is that
-    // expert's.  The 4 CTAs of the cluster read the same entry.
-    const int ti = blockIdx.x / kSplit;
-    if (ti >= *tile_count) return;
-    const int4 t = tiles[ti];
-    m0 = t.y;
-    m_end = t.z;
-    q += t.x * q_expert_stride;
-  }
-  const int n_chunks = R / kStageR;
-  const int c_begin = static_cast<int>(crank) * n_chunks / kSplit;
-  const int c_end = (static_cast<int>(crank) + 1) * n_chunks / kSplit;
-  const int n_iter = c_end - c_begin;
-  volatile uint32_t* abort_word = &bars->abort_word;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < C::kStages; ++i) {
-      mbar_init(&bars->pfull[i], 1);
-      mbar_init(&bars->qfull[i], 2);
-      mbar_init(&bars->empty[i], 1);
-    }
-    mbar_init(&bars->accum, 1);
-    bars->abort_word = 0;
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(&bars->tmem_base, C::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();
-  tc_fence_after();
-  const uint32_t tmem_base = bars->tmem_base;
-  bool ok = true;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_p);
-      int issued = 0;
-      for (int it = 0; it < n_iter; ++it) {
-        const int st = it % C::kStages;
-        if (it >= C::kStages &&
-            !mbar_wait_short(&bars->empty[st], ((it / C::kStages) - 1) & 1, abort_word, status, kStatusTimeoutEmpty))
-          break;
-        mbar_arrive_expect_tx(&bars->pfull[st], kPBytes);
-        tma_load_2d(ps + st * kPBytes, &tm_p, (c_begin + it) * kStageR, m0, &bars->pfull[st]);
-        ++issued;
+// Prepass: qc[e][plane][u][j][c][16] (bf16) from Q(j, r) = q[e*q_es + j*q_sj + r*q_sr].
+// One thread per (e, j, 8 consecutive r).
+__global__ void prep_kernel(const float* __restrict__ q, int64_t q_sj, int64_t q_sr, int64_t q_es, int rank, int R,
+                            int nq, int experts, __nv_bfloat16* __restrict__ qc) {
+  const int r8s = R / 8;
+  const int64_t total = static_cast<int64_t>(experts) * nq * r8s;
+  const int64_t plane = static_cast<int64_t>(nq) * R;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r8 = static_cast<int>(idx % r8s);
+    const int j = static_cast<int>((idx / r8s) % nq);
+    const int e = static_cast<int>(idx / (static_cast<int64_t>(r8s) * nq));
+    const int r0 = r8 * 8;
+    float v[8];
+    if (j < rank) {
+      const float* src = q + e * q_es + j * q_sj + static_cast<int64_t>(r0) * q_sr;
+      if (q_sr == 1 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[t] = __ldg(src + t * q_sr);
       }
-      for (int i = issued > C::kStages ? issued - C::kStages : 0; i < issued; ++i) {
-        uint32_t dummy = 0;
-        mbar_wait_short(&bars->pfull[i % C::kStages], (i / C::kStages) & 1, &dummy, status, kStatusTimeoutDrain);
-      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] = 0.f;
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kRows, NQ);
-      for (int it = 0; it < n_iter; ++it) {
-        const int st = it % C::kStages;
-        const uint32_t ph = (it / C::kStages) & 1;
-        if (!mbar_wait_short(&bars->pfull[st], ph, abort_word, status, kStatusTimeoutFull)) break;
-        if (!mbar_wait_short(&bars->qfull[st], ph, abort_word, status, kStatusTimeoutFull)) break;
-        tc_fence_after();
-        const uint64_t pd = sdesc_kmajor_sw128(smem_u32(ps + st * kPBytes));
-        const uint64_t hd = sdesc_kmajor_sw128(smem_u32(qh + st * C::kQBytes));
-        const uint64_t lo = sdesc_kmajor_sw128(smem_u32(ql + st * C::kQBytes));
-        for (int kk = 0; kk < kStageR / 16; ++kk) {
-          mma_ss(tmem_base, pd + 2 * kk, hd + 2 * kk, idesc, (it | kk) != 0 ? 1u : 0u);
-          mma_ss(tmem_base, pd + 2 * kk, lo + 2 * kk, idesc, 1u);
-        }
-        tc_commit(&bars->empty[st]);
-      }
-      tc_commit(&bars->accum);
-      uint32_t dummy = 0;
-      mbar_wait_short(&bars->accum, 0, &dummy, status, kStatusTimeoutAccum);
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      h[t] = pack_bf16x2(v[2 * t], v[2 * t + 1]);
+      const float h0 = __uint_as_float(h[t] << 16), h1 = __uint_as_float(h[t] & 0xFFFF0000u);
+      l[t] = pack_bf16x2(v[2 * t] - h0, v[2 * t + 1] - h1);
     }
-  } else {
-    // Factor converters: chunk (j, 8 consecutive r) -> 16-byte hi and lo pieces
-    // at row j, chunk position c ^ (j % 8) of the 128-byte-swizzled tile.  The
-    // FP32 chunks of the next kAhead stages are loaded into registers before the
-    // current one is converted, so the global-load latency overlaps.
-    constexpr int kPer = NQ / 8;                 // chunks per thread per stage (NQ*8 chunks, 64 threads)
-    constexpr int kAhead = NQ <= 32 ? 2 : 1;
-    const int t = threadIdx.x - 64;
-    float buf[kAhead + 1][kPer][8];
-    auto fetch = [&](int it, float (&v)[kPer][8]) {
-      const int r0 = (c_begin + it) * kStageR;
-#pragma unroll
-      for (int u = 0; u < kPer; ++u) {
-        const int idx = t + 64 * u;
-        const int j = idx >> 3, c = idx & 7;
-        if (it < n_iter && j < rank) {
-          const float* src = q + j * q_sj + static_cast<int64_t>(r0 + 8 * c) * q_sr;
-          if (q_sr == 1) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(src));
-            const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
-            v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
-            v[u][4] = b.x; v[u][5] = b.y; v[u][6] = b.z; v[u][7] = b.w;
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[u][e] = __ldg(src + e * q_sr);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[u][e] = 0.f;
-        }
-      }
-    };
-#pragma unroll
-    for (int a = 0; a < kAhead; ++a) fetch(a, buf[a]);
-    for (int it = 0; it < n_iter && ok; ++it) {
-      const int st = it % C::kStages;
-      fetch(it + kAhead, buf[kAhead]);
-      if (it >= C::kStages &&
-          !mbar_wait_short_warp(&bars->empty[st], ((it / C::kStages) - 1) & 1, abort_word, status, kStatusTimeoutEmpty)) {
-        ok = false;
-        break;
-      }
-#pragma unroll
-      for (int u = 0; u < kPer; ++u) {
-        const int idx = t + 64 * u;
-        const int j = idx >> 3, c = idx & 7;
-        uint32_t h[4], l[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          h[e] = pack_bf16x2(buf[0][u][2 * e], buf[0][u][2 * e + 1]);
-          const float h0 = __uint_as_float(h[e] << 16), h1 = __uint_as_float(h[e] & 0xFFFF0000u);
-          l[e] = pack_bf16x2(buf[0][u][2 * e] - h0, buf[0][u][2 * e + 1] - h1);
-        }
-        const uint32_t off = j * 128 + ((c ^ (j & 7)) << 4);
-        *reinterpret_cast<uint4*>(qh + st * C::kQBytes + off) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(ql + st * C::kQBytes + off) = make_uint4(l[0], l[1], l[2], l[3]);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->qfull[st]);
-#pragma unroll
-      for (int a = 0; a < kAhead; ++a)
-#pragma unroll
-        for (int u = 0; u < kPer; ++u)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) buf[a][u][e] = buf[a + 1][u][e];
-    }
-  }
-
-  // ---------------------------------------------------------------- reduction
-  // All 4 warps: lane quarter w holds rows 32w..32w+31 of the CTA's 128.
-  const int row = warp * 32 + lane;
-  float acc[NQ];
-  bool have = false;
-  if (n_iter > 0 && mbar_wait_short_warp(&bars->accum, 0, abort_word, status, kStatusTimeoutAccum)) {
-    tc_fence_after();
-#pragma unroll
-    for (int c0 = 0; c0 < NQ; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
-      tmem_wait_ld();
-#pragma unroll
-      for (int e = 0; e < 16; ++e) acc[c0 + e] = __uint_as_float(v[e]);
-    }
-    have = true;
-  }
-  if (!have) {
-#pragma unroll
-    for (int e = 0; e < NQ; ++e) acc[e] = 0.f;
-  }
-  // Round 1: every CTA finished its main loop, so rank 0's stage buffers are free.
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();
-  float* red = reinterpret_cast<float*>(ps);  // [kSplit-1][kRows][NQ] in rank 0
-  if (crank != 0) {
-    const uint32_t base = mapa_shared(smem_u32(red), 0) +
-                          static_cast<uint32_t>(((crank - 1) * kRows + row) * NQ * 4);
-#pragma unroll
-    for (int e = 0; e < NQ; ++e) st_shared_cluster_u32(base + 4 * e, __float_as_uint(acc[e]));
-  }
-  cluster_sync();
-  if (crank == 0) {
-#pragma unroll 1
-    for (int p = 0; p < kSplit - 1; ++p) {
-      const float* pr = red + (p * kRows + row) * NQ;
-#pragma unroll
-      for (int e = 0; e < NQ; ++e) acc[e] += pr[e];
-    }
-    const int m = m0 + row;
-    if (m < m_end) {
-      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(m) * 64);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j0 = 8 * c + 2 * e, j1 = j0 + 1;
-          const float a = (j0 < NQ && j0 < rank) ? s * acc[j0 < NQ ? j0 : 0] : 0.f;
-          const float b = (j1 < NQ && j1 < rank) ? s * acc[j1 < NQ ? j1 : 0] : 0.f;
-          w[e] = pack_bf16x2(a, b);
-        }
-        dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    }
-  }
-  if (warp == 1) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    const int u = r0 >> 6, c = (r0 & 63) >> 4, w = r0 & 15;
+    const int64_t off = ((static_cast<int64_t>(u) * nq + j) * 4 + c) * 16 + w;
+    __nv_bfloat16* base = qc + static_cast<int64_t>(e) * 2 * plane;
+    *reinterpret_cast<uint4*>(base + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(base + plane + off) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
 
+__device__ __forceinline__ uint32_t word(const uint4& a, const uint4& b, int w) {
+  const uint4& q = w < 4 ? a : b;
+  const int k = w & 3;
+  return k == 0 ? q.x : k == 1 ? q.y : k == 2 ? q.z : q.w;
+}
+
 template <int NQ>
-static int launch_nq(const CUtensorMap& tm, const float* q, int64_t q_sj, int64_t q_sr, int rank, float s,
-                     void* out, int M, int R, cudaStream_t stream, const int4* tiles, const int* tile_count,
-                     int max_tiles, int64_t q_expert_stride) {
+__global__ void __launch_bounds__(kThreads)
+    lora_down_kernel(const __grid_constant__ CUtensorMap tm_p,  // P [M, R] bf16, box {64, 128}, 128B swizzle
+                     int M, int R, const __nv_bfloat16* __restrict__ qc, int64_t qc_es, int rank, float s,
+                     __nv_bfloat16* __restrict__ out, int split, const int4* __restrict__ tiles,
+                     const int* __restrict__ tile_count, uint32_t* status) {
   using C = Cfg<NQ>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&lora_down_tc_kernel<NQ>),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down attr: %s", cudaGetErrorString(e));
-    attr_set = true;
+  constexpr int NT = NQ / 8;  // n-tiles of 8 rank columns
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::kStage);
+  uint64_t* empty = full + kStages;
+  auto red = reinterpret_cast<float (*)[NQ + 1]>(smem + kStages * C::kStage + 2 * kStages * 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int kslice = split > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int blk = blockIdx.x / split;
+  int m0 = blk * kRows, m_end = M;
+  if (tiles != nullptr) {
+    // MoE: one <= 128-row tile of one expert's segment (every CTA of the
+    // cluster reads the same entry, so they leave together).
+    if (blk >= *tile_count) return;
+    const int4 t = tiles[blk];
+    m0 = t.y;
+    m_end = min(t.z, M);
+    qc += t.x * qc_es;
   }
+  const int64_t plane = static_cast<int64_t>(NQ) * R;
+  const int units = R / 64;
+  const int u0 = kslice * units / split;
+  const int u1 = (kslice + 1) * units / split;
+  const int n_units = u1 - u0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  uint32_t abort_local = 0;
+  volatile uint32_t* abort_word = &abort_local;
+
+  float acc[2][NT][4];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int n = 0; n < NT; ++n) acc[t][n][0] = acc[t][n][1] = acc[t][n][2] = acc[t][n][3] = 0.f;
+
+  if (warp == kWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_p);
+      int issued = 0;
+      for (int k = 0; k < n_units; ++k) {
+        const int st = k % kStages;
+        if (k >= kStages &&
+            !mbar_wait_short(&empty[st], ((k / kStages) - 1) & 1, abort_word, status, kStatusTimeoutEmpty))
+          break;
+        const int u = u0 + k;
+        uint8_t* stage = smem + st * C::kStage;
+        const __nv_bfloat16* qsrc = qc + static_cast<int64_t>(u) * NQ * 64;
+        mbar_arrive_expect_tx(&full[st], C::kStage);
+        tma_load_2d(stage, &tm_p, u * 64, m0, &full[st]);
+        bulk_load(stage + kXBytes, qsrc, C::kQPlane, &full[st]);
+        bulk_load(stage + kXBytes + C::kQPlane, qsrc + plane, C::kQPlane, &full[st]);
+        ++issued;
+      }
+      for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i) {
+        uint32_t dummy = 0;
+        mbar_wait_short(&full[i % kStages], (i / kStages) & 1, &dummy, status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    for (int k = 0; k < n_units; ++k) {
+      const int st = k % kStages;
+      if (!mbar_wait_short_warp(&full[st], (k / kStages) & 1, abort_word, status, kStatusTimeoutFull)) break;
+      const uint8_t* stage = smem + st * C::kStage;
+      // Thread (g, c) needs chunk 2c + e of rows 32w + 16t + 8h + g; under the
+      // 128-byte swizzle chunk j of row r sits at position j ^ (r % 8).
+      uint4 x[kChunks];
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int r = warp * kRowsPerWarp + 16 * t + 8 * h + g;
+            x[(t * 2 + h) * 2 + e] =
+                *reinterpret_cast<const uint4*>(stage + r * 128 + (((2 * c + e) ^ (r & 7)) << 4));
+          }
+      const uint8_t* qb = stage + kXBytes + ((g * 4 + c) * 16) * 2;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint4* hp = reinterpret_cast<const uint4*>(qb + n * 8 * 64 * 2);
+        const uint4* lp = reinterpret_cast<const uint4*>(qb + C::kQPlane + n * 8 * 64 * 2);
+        const uint4 h0 = hp[0], h1 = hp[1];
+        const uint4 l0 = lp[0], l1 = lp[1];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t bh0 = word(h0, h1, 2 * i), bh1 = word(h0, h1, 2 * i + 1);
+          const uint32_t bl0 = word(l0, l1, 2 * i), bl1 = word(l0, l1, 2 * i + 1);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            // rows g (h = 0) and g + 8 (h = 1): chunk (t*2 + h)*2 + e
+            const uint32_t a0 = word(x[(t * 2 + 0) * 2], x[(t * 2 + 0) * 2 + 1], 2 * i);
+            const uint32_t a1 = word(x[(t * 2 + 1) * 2], x[(t * 2 + 1) * 2 + 1], 2 * i);
+            const uint32_t a2 = word(x[(t * 2 + 0) * 2], x[(t * 2 + 0) * 2 + 1], 2 * i + 1);
+            const uint32_t a3 = word(x[(t * 2 + 1) * 2], x[(t * 2 + 1) * 2 + 1], 2 * i + 1);
+            mma_16816(acc[t][n], a0, a1, a2, a3, bh0, bh1);
+            mma_16816(acc[t][n], a0, a1, a2, a3, bl0, bl1);
+          }
+        }
+      }
+      // The stage's values are in registers: hand it back to the producer.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+  }
+
+  // Partial sums -> shared memory (rows of this CTA, NQ columns).
+  if (warp < kWarps) {
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int r = warp * kRowsPerWarp + 16 * t + g;
+      red[r][8 * n + 2 * c] = acc[t][n][0];
+      red[r][8 * n + 2 * c + 1] = acc[t][n][1];
+      red[r + 8][8 * n + 2 * c] = acc[t][n][2];
+      red[r + 8][8 * n + 2 * c + 1] = acc[t][n][3];
+    }
+  }
+  if (split > 1) {
+    cluster_sync();
+  } else {
+    __syncthreads();
+  }
+  // This CTA finishes rows [r_begin, r_end) of the 128: sum the split
+  // partials, scale, round, write 64 bf16 per row (zero past the rank).
+  const int r_begin = kslice * kRows / split;
+  const int r_end = (kslice + 1) * kRows / split;
+  const uint32_t red_local = smem_u32(&red[0][0]);
+  for (int idx = threadIdx.x; idx < (r_end - r_begin) * 8; idx += kThreads) {
+    const int r = r_begin + idx / 8, q8 = idx % 8;  // output columns 8*q8 .. +7
+    const int m = m0 + r;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    if (8 * q8 < NQ) {
+      if (split > 1) {
+        for (int p = 0; p < split; ++p) {
+          const uint32_t base =
+              mapa_shared(red_local, static_cast<uint32_t>(p)) + static_cast<uint32_t>((r * (NQ + 1) + 8 * q8) * 4);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] += __uint_as_float(ld_shared_cluster_u32(base + 4 * e));
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = red[r][8 * q8 + e];
+      }
+    }
+    if (m < m_end) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j0 = 8 * q8 + 2 * e;
+        w[e] = pack_bf16x2(j0 < rank ? s * v[2 * e] : 0.f, j0 + 1 < rank ? s * v[2 * e + 1] : 0.f);
+      }
+      *reinterpret_cast<uint4*>(out + static_cast<size_t>(m) * 64 + 8 * q8) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  // Peers read this CTA's partials: stay until every CTA of the cluster is done.
+  if (split > 1) cluster_sync();
+}
+
+template <int NQ>
+static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64_t qc_es, int rank, float s,
+                     void* out, cudaStream_t stream, const int4* tiles, const int* tile_count, int max_tiles) {
+  const int blocks = tiles ? max_tiles : (M + kRows - 1) / kRows;
+  if (blocks < 1) return FL_OK;
+  constexpr int kSmem = Cfg<NQ>::kSmem;
   int dev = 0;
-  cudaGetDevice(&dev);
-  uint32_t* status = status_word(dev);
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return set_error(FL_ERR_CUDA, "lora_down: no current device");
+  // Per device: the kernel's shared-memory limit and how many CTAs fit on the GPU at once.
+  static int slots[64] = {0};
+  if (!slots[dev]) {
+    int sms = 0, per_sm = 0;
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&lora_down_kernel<NQ>),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lora_down_kernel<NQ>, kThreads, kSmem);
+    if (e != cudaSuccess || per_sm < 1) return set_error(FL_ERR_CUDA, "lora_down: occupancy query failed");
+    slots[dev] = sms * per_sm;
+  }
+  // Split the reduction across a cluster while the grid still fits in one
+  // wave of resident CTAs and every slice keeps at least two 64-wide units.
+  int split = 1;
+  while (split < kMaxSplit && blocks * split * 2 <= slots[dev] && (R / 64) >= 4 * split) split *= 2;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kSplit * (tiles ? max_tiles : (M + kRows - 1) / kRows));
+  cfg.gridDim = dim3(blocks * split);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kSplit;
+  attr[0].val.clusterDim.x = split;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t le = cudaLaunchKernelEx(&cfg, lora_down_tc_kernel<NQ>, tm, q, q_sj, q_sr, rank, s,
-                                      static_cast<__nv_bfloat16*>(out), M, R, status, tiles, tile_count,
-                                      q_expert_stride);
+  CUtensorMap tm;
+  int rc = make_tensor_map_2d(&tm, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, R, M, static_cast<uint64_t>(R) * 2, 64,
+                              kRows, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  cudaError_t le = cudaLaunchKernelEx(&cfg, lora_down_kernel<NQ>, tm, M, R, qc, qc_es, rank, s,
+                                      static_cast<__nv_bfloat16*>(out), split, tiles, tile_count, status_word(dev));
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }
 
 }  // namespace ld
 
-int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
-                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+int lora_nq(int rank) { return rank <= 16 ? 16 : rank <= 32 ? 32 : 64; }
+
+size_t lora_factor_bytes(int64_t R, int rank) { return 4u * static_cast<size_t>(lora_nq(rank)) * R; }
 
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank, float s,
-                     void* out64, cudaStream_t stream, const int4* tiles, const int* tile_count, int max_tiles,
-                     int64_t q_expert_stride) {
+                     void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles, const int* tile_count,
+                     int max_tiles, int64_t q_expert_stride, int experts) {
   if (R % 128 != 0) return set_error(FL_ERR_ARG, "lora_down: reduction dim %d not a multiple of 128", R);
   if (rank < 1 || rank > 64) return set_error(FL_ERR_ARG, "lora_down: rank %d outside [1, 64]", rank);
-  if (q_sr == 1 && (reinterpret_cast<uintptr_t>(q) & 15u))
-    return set_error(FL_ERR_ARG, "lora_down: factor must be 16-byte aligned");
-  CUtensorMap tm;
-  int rc = make_tensor_map_2d(&tm, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, R, M, static_cast<uint64_t>(R) * 2, 64,
-                              ld::kRows, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  if (rank <= 16)
-    return ld::launch_nq<16>(tm, q, q_sj, q_sr, rank, s, out64, M, R, stream, tiles, tile_count, max_tiles,
-                             q_expert_stride);
-  if (rank <= 32)
-    return ld::launch_nq<32>(tm, q, q_sj, q_sr, rank, s, out64, M, R, stream, tiles, tile_count, max_tiles,
-                             q_expert_stride);
-  return ld::launch_nq<64>(tm, q, q_sj, q_sr, rank, s, out64, M, R, stream, tiles, tile_count, max_tiles,
-                           q_expert_stride);
+  if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(out64) |
+       reinterpret_cast<uintptr_t>(qc_scratch)) & 15u)
+    return set_error(FL_ERR_ARG, "lora_down: activations, output and scratch must be 16-byte aligned");
+  const int nq = lora_nq(rank);
+  auto qc = static_cast<__nv_bfloat16*>(qc_scratch);
+  {
+    const int64_t total = static_cast<int64_t>(experts) * nq * (R / 8);
+    const int threads = 256;
+    const int64_t want = (total + threads - 1) / threads;
+    const int grid = static_cast<int>(want < 4096 ? want : 4096);
+    ld::prep_kernel<<<grid, threads, 0, stream>>>(q, q_sj, q_sr, q_expert_stride, rank, R, nq, experts, qc);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down prepass: %s", cudaGetErrorString(e));
+  }
+  const int64_t qc_es = 2 * static_cast<int64_t>(nq) * R;
+  if (nq == 16) return ld::launch_nq<16>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
+  if (nq == 32) return ld::launch_nq<32>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
+  return ld::launch_nq<64>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
 }
 
 }  // namespace fl

@@ -123,7 +123,7 @@ size_t align16(size_t v) { return (v + 15) / 16 * 16; }
 
 struct GroupedPlan {
   int fwd_tiles, bwd_tiles, down_tiles, grad_tiles;
-  size_t off_fwd, off_bwd, off_down, off_grad, off_count, off_us, off_ts, total;
+  size_t off_fwd, off_bwd, off_down, off_grad, off_count, off_us, off_ts, off_qa, off_qb, total;
 };
 
 GroupedPlan grouped_plan(int64_t rows, int experts, int64_t N, int64_t K, int rank) {
@@ -148,6 +148,11 @@ GroupedPlan grouped_plan(int64_t rows, int experts, int64_t N, int64_t K, int ra
   off += rank > 0 ? static_cast<size_t>(rows) * 128 : 0;
   p.off_ts = off;
   off += rank > 0 ? static_cast<size_t>(rows) * 128 : 0;
+  // Converted factors of every expert: A (reduction K) and B^T (reduction N).
+  p.off_qa = off;
+  off += rank > 0 ? static_cast<size_t>(experts) * lora_factor_bytes(K, rank) : 0;
+  p.off_qb = off;
+  off += rank > 0 ? static_cast<size_t>(experts) * lora_factor_bytes(N, rank) : 0;
   p.total = off;
   return p;
 }
@@ -215,8 +220,8 @@ int fl_grouped_fwd(const uint16_t* X, const int32_t* seg, int64_t rows, int64_t 
   if (rank > 0) {
     if ((rc = launch_moe_plan(seg, experts, r, kDownRows, 1, t_down, p.down_tiles, counts + 1, status, st))) return rc;
     // Ts = bf16(s * X . A_e^T), A_e = A + e * rank * K
-    if ((rc = launch_lora_down(X, r, k, A, K, 1, rank, scale, ts, st, t_down, counts + 1, p.down_tiles,
-                               static_cast<int64_t>(rank) * K)))
+    if ((rc = launch_lora_down(X, r, k, A, K, 1, rank, scale, ts, ws + p.off_qa, st, t_down, counts + 1,
+                               p.down_tiles, static_cast<int64_t>(rank) * K, experts)))
       return rc;
   }
   return launch_fwd_gemm(X, rank > 0 ? ts : nullptr, payload, scales, lut16, B, rank, Y, r, n, k, status, st, t_fwd,
@@ -255,12 +260,12 @@ int fl_grouped_bwd(const uint16_t* dY, const uint16_t* X, const int32_t* seg, in
     if ((rc = launch_moe_plan(seg, experts, r, kDownRows, 1, t_down, p.down_tiles, counts + 1, status, st))) return rc;
     if ((rc = launch_moe_plan(seg, experts, r, kGradRows, 1, t_grad, p.grad_tiles, counts + 2, status, st))) return rc;
     // Us = bf16(s * dY . B_e): Q(j, n) = B_e[n * rank + j], B_e = B + e * N * rank
-    if ((rc = launch_lora_down(dY, r, n, B, 1, rank, rank, scale, us, st, t_down, counts + 1, p.down_tiles,
-                               static_cast<int64_t>(N) * rank)))
+    if ((rc = launch_lora_down(dY, r, n, B, 1, rank, rank, scale, us, ws + p.off_qb, st, t_down, counts + 1,
+                               p.down_tiles, static_cast<int64_t>(N) * rank, experts)))
       return rc;
     // Ts = bf16(s * X . A_e^T): Q(j, k) = A_e[j * K + k]
-    if ((rc = launch_lora_down(X, r, k, A, K, 1, rank, scale, ts, st, t_down, counts + 1, p.down_tiles,
-                               static_cast<int64_t>(rank) * K)))
+    if ((rc = launch_lora_down(X, r, k, A, K, 1, rank, scale, ts, ws + p.off_qa, st, t_down, counts + 1,
+                               p.down_tiles, static_cast<int64_t>(rank) * K, experts)))
       return rc;
   }
   if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, r, n, k, status, st, t_bwd, counts + 0,

@@ -2,7 +2,7 @@
 // allocate device memory when they call it.
 //
 // fl_fwd needs scratch for the scaled low-rank activations Ts = bf16(s*X.A^T)
-// (M x 64 bf16) and asks the caller for it.  Some callers have no way to
+// (M x 64 bf16) and the converted factor A, and asks the caller for it.  Some callers have no way to
 // provide it: a host binding (Go/Java/C FFI) that owns no device allocator, a
 // trainer that has committed its whole device budget up front and must not
 // grow it per call, or code that wants no allocator traffic between kernels.
@@ -10,9 +10,11 @@
 // device memory instead, so it allocates nothing at all.
 //
 // Rules of use:
-//  * Limit: M * 128 bytes must fit in kNoAllocScratchBytes (4 MiB), i.e.
-//    M <= 32768 tokens per call; larger M is rejected with FL_ERR_ARG.
-//  * Every GPU that loads the library holds the 4 MiB array until exit.
+//  * Limits: M * 128 bytes must fit in kNoAllocScratchBytes (4 MiB), i.e.
+//    M <= 32768 tokens per call, and the converted factor A (4 * rank' * K
+//    bytes, rank' = rank rounded up to 16/32/64) in kNoAllocFactorBytes
+//    (8 MiB); larger calls are rejected with FL_ERR_ARG.
+//  * Every GPU that loads the library holds the 12 MiB array until exit.
 //  * The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current.  Make that first call
 //    before any stream capture.
@@ -29,10 +31,12 @@
 namespace fl {
 
 constexpr size_t kNoAllocScratchBytes = 4u << 20;
+constexpr size_t kNoAllocFactorBytes = 8u << 20;
 
 // Host code must not use this name as a device address: on the host it is only
 // a stand-in symbol.  Device addresses come from cudaGetSymbolAddress below.
-static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+// The first kNoAllocScratchBytes hold Ts, the rest the converted factor A.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes + kNoAllocFactorBytes];
 
 static uint8_t* noalloc_scratch(int device) {
   static std::mutex mu;
@@ -62,6 +66,9 @@ extern "C" int fl_fwd_noalloc(const uint16_t* X, int64_t M, int64_t K, const uin
   if (rank > 0 && static_cast<uint64_t>(M) * 128u > kNoAllocScratchBytes)
     return set_error(FL_ERR_ARG, "fl_fwd_noalloc: M=%lld tokens exceeds the %zu-byte scratch (max %zu tokens)",
                      (long long)M, kNoAllocScratchBytes, kNoAllocScratchBytes / 128);
+  if (rank > 0 && rank <= FL_MAX_RANK && K > 0 && lora_factor_bytes(K, rank) > kNoAllocFactorBytes)
+    return set_error(FL_ERR_ARG, "fl_fwd_noalloc: K=%lld at rank %d exceeds the %zu-byte factor scratch",
+                     (long long)K, rank, kNoAllocFactorBytes);
   if (K % 128 != 0) return set_error(FL_ERR_ARG, "fl_fwd_noalloc: in_features K=%lld must be a multiple of 128", (long long)K);
   if (rank < 0 || rank > FL_MAX_RANK) return set_error(FL_ERR_UNSUPPORTED, "fl_fwd_noalloc: rank %d outside [0, %d]", rank, FL_MAX_RANK);
   if (!X || !Y || !payload || !scales || !lut16) return set_error(FL_ERR_ARG, "fl_fwd_noalloc: null pointer");
@@ -78,7 +85,7 @@ extern "C" int fl_fwd_noalloc(const uint16_t* X, int64_t M, int64_t K, const uin
   if (rank > 0) {
     ts = noalloc_scratch(dev);
     if (!ts) return FL_ERR_CUDA;
-    const int rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, st);
+    const int rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, ts + kNoAllocScratchBytes, st);
     if (rc) return rc;
   }
   if (M <= 16) return launch_smallm_fwd(X, ts, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st);

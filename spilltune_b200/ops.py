@@ -74,7 +74,7 @@ def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0):
         B = B.detach().contiguous()
     M = x2.shape[0]
     y = torch.empty((M, N), dtype=torch.bfloat16, device=x2.device)
-    ws_bytes = _lib.load().fl_fwd_workspace_bytes(M, rank)
+    ws_bytes = _lib.load().fl_fwd_workspace_bytes(M, K, rank)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device) if ws_bytes else None
     if M:
         _lib.call("fl_fwd", _ptr(x2), M, K, _ptr(weight.payload), _ptr(weight.scales), _ptr(weight.lut), N,
@@ -100,7 +100,7 @@ def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None
         if dB is None:
             dB = torch.empty((N, rank), dtype=torch.float32, device=dy2.device)
             accumulate = False
-    ws_bytes = _lib.load().fl_bwd_workspace_bytes(M, rank)
+    ws_bytes = _lib.load().fl_bwd_workspace_bytes(M, N, K, rank)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dy2.device) if ws_bytes else None
     if M:
         _lib.call("fl_bwd", _ptr(dy2), _ptr(x2), M, N, K, _ptr(weight.payload), _ptr(weight.scales),

@@ -2,6 +2,10 @@
 
     python -m spilltune_b200.probe --op fwd --M 8192 --N 14336 --K 4096 [--iters 3] [--time]
 
+With --experts E > 1, fwd/bwd run the grouped (MoE) kernels over M routed
+rows: M / top_k tokens routed uniformly at random to `top_k` of E experts of
+a stacked [E, N, K] record, and --rank gives every expert its own LoRA pair.
+
 Each call is preceded by two warm-up calls, so an `ncu -s 2 -c 1` capture
 selects the first measured launch.  --time prints CUDA-event timings instead.
 """
@@ -10,7 +14,7 @@ import json
 
 import torch
 
-from . import codec, ops
+from . import codec, moe, ops
 
 
 def main():
@@ -23,20 +27,34 @@ def main():
     p.add_argument("--codec", default="nf4-g128")
     p.add_argument("--iters", type=int, default=1)
     p.add_argument("--time", action="store_true")
+    p.add_argument("--experts", type=int, default=1)
+    p.add_argument("--top-k", type=int, default=8)
     a = p.parse_args()
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
-    w = codec.encode(torch.randn(a.N, a.K, generator=g, device=dev) * 0.02, a.codec)
+    E = a.experts
+    lead = (E,) if E > 1 else ()
+    w = codec.encode(torch.randn(*lead, a.N, a.K, generator=g, device=dev) * 0.02, a.codec)
     x = torch.randn(a.M, a.K, generator=g, device=dev).to(torch.bfloat16)
     dy = torch.randn(a.M, a.N, generator=g, device=dev).to(torch.bfloat16)
-    A = torch.randn(a.rank, a.K, generator=g, device=dev) * 0.01 if a.rank else None
-    B = torch.randn(a.N, a.rank, generator=g, device=dev) * 0.01 if a.rank else None
-    out = torch.empty(a.N, a.K, dtype=torch.bfloat16, device=dev)
-    fn = {
-        "fwd": lambda: ops.fwd(x, w, A, B, 2.0),
-        "bwd": lambda: ops.bwd(dy, x, w, A, B, 2.0),
-        "dequant": lambda: ops.dequant(w, out=out),
-    }[a.op]
+    A = torch.randn(*lead, a.rank, a.K, generator=g, device=dev) * 0.01 if a.rank else None
+    B = torch.randn(*lead, a.N, a.rank, generator=g, device=dev) * 0.01 if a.rank else None
+    if E > 1:
+        if a.op == "dequant" or a.M % a.top_k:
+            raise SystemExit("--experts needs --op fwd|bwd and M divisible by --top-k")
+        scores = torch.rand(a.M // a.top_k, E, generator=g, device=dev)
+        segs = moe.expert_segments(scores.topk(a.top_k, dim=-1)[1], E)
+        fn = {
+            "fwd": lambda: moe.grouped_fwd(x, segs, w, A, B, 2.0),
+            "bwd": lambda: moe.grouped_bwd(dy, x, segs, w, A, B, 2.0),
+        }[a.op]
+    else:
+        out = torch.empty(a.N, a.K, dtype=torch.bfloat16, device=dev)
+        fn = {
+            "fwd": lambda: ops.fwd(x, w, A, B, 2.0),
+            "bwd": lambda: ops.bwd(dy, x, w, A, B, 2.0),
+            "dequant": lambda: ops.dequant(w, out=out),
+        }[a.op]
     for _ in range(2):
         fn()
     torch.cuda.synchronize()
@@ -54,7 +72,7 @@ def main():
     torch.cuda.synchronize()
     us = s.elapsed_time(e) / iters * 1e3
     flops = 2.0 * a.M * a.N * a.K * (1 if a.op != "dequant" else 0)
-    print(json.dumps({"op": a.op, "M": a.M, "N": a.N, "K": a.K, "us": us,
+    print(json.dumps({"op": a.op, "M": a.M, "N": a.N, "K": a.K, "experts": E, "us": us,
                       "tflops": flops / us / 1e6 if flops else None}))
 
 

@@ -43,10 +43,12 @@ def test_python_binding_covers_header():
 
 
 def test_version_and_workspace_sizes(lib):
-    assert lib.fl_version() >= 100
-    assert lib.fl_fwd_workspace_bytes(8192, 16) == 8192 * 128
-    assert lib.fl_fwd_workspace_bytes(8192, 0) == 0
-    assert lib.fl_bwd_workspace_bytes(100, 8) == 100 * 256
+    assert lib.fl_version() >= 101
+    # Ts (M x 64 bf16) + the factor converted to a bf16 hi/lo pair (4 * rank' * K).
+    assert lib.fl_fwd_workspace_bytes(8192, 4096, 16) == 8192 * 128 + 4 * 16 * 4096
+    assert lib.fl_fwd_workspace_bytes(8192, 4096, 20) == 8192 * 128 + 4 * 32 * 4096
+    assert lib.fl_fwd_workspace_bytes(8192, 4096, 0) == 0
+    assert lib.fl_bwd_workspace_bytes(100, 384, 256, 8) == 100 * 256 + 4 * 16 * (384 + 256)
 
 
 def _fwd(lib, M=16, K=256, N=128, rank=0, ptr=1024, ws=0):

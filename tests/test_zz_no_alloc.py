@@ -33,7 +33,7 @@ def _fwd_with_workspace(lib, pw, x, A, B, s):
     N = pw.shape[0]
     rank = A.shape[0]
     y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-    ws_bytes = lib.fl_fwd_workspace_bytes(M, rank)
+    ws_bytes = lib.fl_fwd_workspace_bytes(M, K, rank)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
     rc = lib.fl_fwd(x.data_ptr(), M, K, pw.payload.data_ptr(), pw.scales.data_ptr(), pw.lut.data_ptr(), N,
                     A.data_ptr(), B.data_ptr(), rank, s, y.data_ptr(), ws.data_ptr(), ws_bytes,

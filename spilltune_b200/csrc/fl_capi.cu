@@ -127,8 +127,9 @@ int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, cons
     rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, workspace, qc, st);
     if (rc) return rc;
   }
-  // Decode-like steps (M <= 16) are bound by the weight bytes: dedicated kernel.
-  if (M <= 16) return launch_smallm_fwd(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st);
+  // Decode-like steps (M <= 16) are bound by the weight bytes: dedicated kernel
+  // (it streams 512-wide column chunks; other K take the tile GEMM).
+  if (M <= 16 && K % 512 == 0) return launch_smallm_fwd(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st);
   return launch_fwd_gemm(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st);
 }
 

@@ -88,6 +88,6 @@ extern "C" int fl_fwd_noalloc(const uint16_t* X, int64_t M, int64_t K, const uin
     const int rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, ts + kNoAllocScratchBytes, st);
     if (rc) return rc;
   }
-  if (M <= 16) return launch_smallm_fwd(X, ts, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st);
+  if (M <= 16 && K % 512 == 0) return launch_smallm_fwd(X, ts, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st);
   return launch_fwd_gemm(X, ts, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st);
 }

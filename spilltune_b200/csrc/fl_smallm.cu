@@ -7,32 +7,42 @@
 // stored code for int4-sym (c - 8), the bf16-rounded codebook for NF4 — and the
 // scale multiplies the fp32 partial sum of its group.
 //
-// At M <= 16 every weight byte is used once, so the kernel is bound by HBM
-// reads of the packed weights (0.53 B per weight).  Decoding must therefore be
-// cheap: a 256-entry table maps one payload byte (two codes) to a bf16 pair,
-// stored once per lane in shared memory (entry e of lane l at word e*32 + l, so
-// a warp's lookups never conflict); one prmt + one IMAD + one shared load per
-// two weights.  The MMAs are warp-level (mma.sync m16n8k16): a warp owns 32
-// weight rows as the A operand (rows g and g+8 of each 16-row tile) and the
-// tokens are the 8-wide N dimension.  The reduction dimension is split over a
-// cluster of CTAs whose partial sums meet in rank 0's shared memory
-// (distributed shared memory), which also adds the LoRA term and writes Y.
+// At M <= 16 every weight byte is used once and a whole projection is only a
+// few MB, so the kernel is bound by how fast the packed weights can be put in
+// flight: each CTA owns 16*tpc weight rows over the whole reduction (or one
+// cluster slice of it) and, before anything else, queues TMA loads of its
+// first `slots` 512-column chunks (codes with the 128-byte swizzle, plus the
+// chunk's scales) into a ring of shared-memory slots; the grid is one wave of
+// several small CTAs per SM, so decode latency is hidden by other warps.
+// Decode: the 16 operand values bf16(lut[c]) sit in registers as a low-byte
+// and a high-byte plane (the product table of fl_codebook.cuh with scale 1),
+// and prmt looks up eight codes of a payload word at a time — no table to
+// build in shared memory, no shared-memory lookups.  Four
+// warps each take one 128-wide scale group of every chunk; the MMAs are
+// warp-level (mma.sync m16n8k16) with 16 weight rows as A and the tokens as
+// the 8-wide N dimension, X fragments read from global (L2) one chunk ahead.
+// The reduction-split CTAs of a cluster add their partial sums through
+// distributed shared memory; rank 0 adds the LoRA term and writes Y.
 #include <cuda_bf16.h>
 #include <cstdint>
 
+#include "fl_codebook.cuh"
 #include "fl_host.h"
 #include "fl_ptx.cuh"
 
 namespace fl {
+
+int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+
 namespace sm {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 4;                        // one per 128-wide group of a chunk
 constexpr int kThreads = 32 * kWarps;
-constexpr int kRowsPerWarp = 32;                 // two 16-row MMA tiles
-constexpr int kRows = kWarps * kRowsPerWarp;     // 128 rows per CTA
-constexpr int kLutBytes = 256 * 32 * 4;          // per-lane byte -> bf16x2 table
-constexpr int kRing = 3;                         // groups of codes in flight per thread
-constexpr int kRingBytes = kRing * kThreads * 80;  // per thread per group: 4 x 16 B codes + 4 x 4 B scales
+constexpr int kChunkK = 512;                     // reduction columns per ring slot
+constexpr int kMaxTpc = 8;                       // 16-row tiles per CTA
+constexpr int kCtasPerSm = 3;                    // grid = one wave at this many CTAs per SM (registers allow 3)
+constexpr int kSlotBudget = 40 * 1024;           // ring bytes per CTA
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -43,226 +53,259 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// bf16 pair for the two codes of byte `pos` of `w`, from this lane's table.
-__device__ __forceinline__ uint32_t lut_pair(const uint32_t* lut_lane, uint32_t w, uint32_t pos) {
-  const uint32_t byte = prmt(w, 0u, 0x4440u | pos);
-  return lut_lane[byte * 32];
+__device__ __forceinline__ uint32_t word4(const uint4& q, int w) {
+  return w == 0 ? q.x : w == 1 ? q.y : w == 2 ? q.z : q.w;
 }
 
-template <int NT>  // 8-token tiles: 1 (M <= 8) or 2 (M <= 16)
+struct Args {
+  const __nv_bfloat16* X;   // [M, K]
+  const __nv_bfloat16* Ts;  // [M, 64] scaled low-rank activations (rank > 0)
+  const float* lut;         // [16]
+  const float* blora;       // [N, rank]
+  __nv_bfloat16* Y;         // [M, N]
+  uint32_t* status;
+  int M, N, K, rank;
+  int tpc;                  // 16-row tiles per CTA
+  int split;                // CTAs of a cluster along the reduction
+  int slots;                // ring depth
+};
+
+// Slot layout: codes box 0 (columns 0..255 of the chunk) [rows][128 B],
+// codes box 1 (256..511), scales [rows][4 fp32].
+__host__ __device__ constexpr int slot_bytes(int rows) { return rows * 128 * 2 + rows * 16; }
+
+// NT: 8-token tiles, 1 (M <= 8) or 2 (M <= 16).  TPC: 16-row tiles per CTA,
+// unrolled so the MMA chains of different tiles interleave; with few tiles
+// the k-steps alternate between two partial sums (PS = 2) for the same reason.
+template <int NT, int TPC>
 __global__ void __launch_bounds__(kThreads)
-    smallm_kernel(const __nv_bfloat16* __restrict__ X, const __nv_bfloat16* __restrict__ Ts,
-                  const uint8_t* __restrict__ codes, const float* __restrict__ scales, const float* __restrict__ lut,
-                  const float* __restrict__ blora, int rank, __nv_bfloat16* __restrict__ Y, int M, int N, int K,
-                  int split) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem);                       // kLutBytes
-  const int groups = K / 128;
-  const uint32_t crank = cluster_ctarank();
-  const int g_begin = static_cast<int>(crank) * groups / split;
-  const int g_end = (static_cast<int>(crank) + 1) * groups / split;
-  const int ks = (g_end - g_begin) * 128;                                   // this CTA's reduction slice
-  const int ks_pad = (groups + split - 1) / split * 128 + 8;                // row stride of the X slice
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + kLutBytes);  // [8*NT][ks_pad]
-  float* red = reinterpret_cast<float*>(smem + kLutBytes + 8 * NT * ks_pad * 2);  // [split-1][kRows][8*NT]
-  uint8_t* ring = smem + kLutBytes + 8 * NT * ks_pad * 2 + (split - 1) * kRows * 8 * NT * 4;
+    smallm_kernel(const __grid_constant__ CUtensorMap tm_codes,   // [N, K/2] u8, box {128, rows}, 128B swizzle
+                  const __grid_constant__ CUtensorMap tm_scales,  // [N, K/128] fp32, box {4, rows}
+                  const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int PS = TPC * NT <= 2 ? 2 : 1;
+  const int rows = 16 * TPC;
+  const int sbytes = (slot_bytes(rows) + 1023) / 1024 * 1024;
+  uint8_t* ring = smem;                                                // slots x sbytes
+  float* red = reinterpret_cast<float*>(smem + args.slots * sbytes);   // [kWarps][rows][16]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + kWarps * rows * 16);         // [slots], then the abort word
+  volatile uint32_t* abort_word = reinterpret_cast<volatile uint32_t*>(full + args.slots);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c4 = lane & 3;
-  const int n0 = (blockIdx.x / split) * kRows;
+  const int split = args.split;
+  const int kslice = split > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int n0 = (blockIdx.x / split) * rows;
+  const int chunks = args.K / kChunkK;
+  const int c_begin = kslice * chunks / split;
+  const int c_end = (kslice + 1) * chunks / split;
+  const int n_ch = c_end - c_begin;
+  // Every CTA reads the same X: start each at a different chunk so the CTAs
+  // spread over X instead of all asking the same L2 lines at once.
+  const int rot = n_ch > 0 ? static_cast<int>((blockIdx.x / split) % n_ch) : 0;
+  auto chunk_of = [&](int k) { return c_begin + (k + rot) % n_ch; };
 
-  // Per-lane table: entry e = {bf16(lut[e & 15]) (low half), bf16(lut[e >> 4])}.
-  for (int e = warp; e < 256; e += kWarps)
-    lut_s[e * 32 + lane] = pack_bf16x2(__ldg(lut + (e & 15)), __ldg(lut + (e >> 4)));
-  // X slice: tokens 0..8*NT-1 (zero past M), reduction columns of this CTA.
-  for (int idx = threadIdx.x; idx < 8 * NT * (ks / 8); idx += kThreads) {
-    const int t = idx / (ks / 8), c = idx % (ks / 8);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (t < M) v = __ldg(reinterpret_cast<const uint4*>(X + static_cast<size_t>(t) * K + g_begin * 128 + 8 * c));
-    *reinterpret_cast<uint4*>(xs + t * ks_pad + 8 * c) = v;
+  // Queue the first loads before any other work.
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < args.slots; ++i) mbar_init(&full[i], 1);
+    *abort_word = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_codes);
+    tma_prefetch_desc(&tm_scales);
   }
+  auto issue = [&](int k) {  // chunk c_begin + k into slot k % slots (thread 0)
+    const int sl = k % args.slots;
+    uint8_t* dst = ring + sl * sbytes;
+    const int c = chunk_of(k);
+    mbar_arrive_expect_tx(&full[sl], slot_bytes(rows));
+    tma_load_2d(dst, &tm_codes, c * (kChunkK / 2), n0, &full[sl]);
+    tma_load_2d(dst + rows * 128, &tm_codes, c * (kChunkK / 2) + 128, n0, &full[sl]);
+    tma_load_2d(dst + rows * 256, &tm_scales, c * 4, n0, &full[sl]);
+  };
+  int issued = 0;  // meaningful in thread 0 only
+  if (threadIdx.x == 0)
+    for (; issued < args.slots && issued < n_ch; ++issued) issue(issued);
+  // Operand table bf16(lut[c]) in registers.
+  const ProductTable table = make_table(args.lut, 1.0f);
   __syncthreads();
 
-  const uint32_t* lut_lane = lut_s + lane;
-  float acc[2][NT][4];
+  float acc[TPC][NT][4];
 #pragma unroll
-  for (int t = 0; t < 2; ++t)
+  for (int t = 0; t < TPC; ++t)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[t][nt][0] = acc[t][nt][1] = acc[t][nt][2] = acc[t][nt][3] = 0.f;
 
-  // Rows this thread feeds: tile t, half h -> n0 + 32*warp + 16*t + g + 8*h.
-  int rows[2][2];
-  bool rvalid[2][2];
+  // X fragments of chunk c for this warp's group: tokens g (+8), columns
+  // 512c + 128*warp + 32*c4 + [0, 32) — 64 contiguous bytes per token.
+  auto load_x = [&](int c, uint4 (&xv)[NT][4]) {
 #pragma unroll
-  for (int t = 0; t < 2; ++t)
+    for (int nt = 0; nt < NT; ++nt) {
+      const int tok = 8 * nt + g;
+      const uint4* src = reinterpret_cast<const uint4*>(args.X + static_cast<size_t>(tok < args.M ? tok : 0) * args.K +
+                                                        c * kChunkK + 128 * warp + 32 * c4);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      rows[t][h] = n0 + kRowsPerWarp * warp + 16 * t + g + 8 * h;
-      rvalid[t][h] = rows[t][h] < N;
+      for (int i = 0; i < 4; ++i) xv[nt][i] = tok < args.M ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
     }
-  const size_t row_bytes = static_cast<size_t>(K) / 2;
-
-  // Ring slot of group gi for this thread: 4 code segments then 4 scales.
-  auto slot = [&](int gi) { return ring + ((gi % kRing) * kThreads + threadIdx.x) * 80; };
-  auto issue = [&](int gi) {
-    if (gi < g_end) {
-      uint8_t* d = slot(gi);
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const bool v = rvalid[t][h];
-          const int r = v ? rows[t][h] : 0;
-          cp_async_16(d + (2 * t + h) * 16, codes + r * row_bytes + gi * 64 + 16 * c4, v);
-          cp_async_4(d + 64 + (2 * t + h) * 4, scales + static_cast<size_t>(r) * groups + gi, v);
-        }
-    }
-    cp_async_commit();  // one group per call, empty past the end, so wait counts stay uniform
   };
-#pragma unroll
-  for (int a = 0; a < kRing - 1; ++a) issue(g_begin + a);
 
-  uint4 q[2][2];
-  float sc[2][2];
-  for (int gi = g_begin; gi < g_end; ++gi) {
-    issue(gi + kRing - 1);
-    cp_async_wait<kRing - 1>();
-    {
-      const uint8_t* d = slot(gi);
+  // One chunk: wait for its slot, decode + MMA this warp's group for every
+  // tile, then (all warps past the slot) refill it.  Every warp passes the
+  // same __syncthreads whether or not a wait gave up.
+  bool ok = true;
+  auto chunk = [&](int k, const uint4 (&xv)[NT][4]) {
+    const int sl = k % args.slots;
+    if (ok && !mbar_wait_short_warp(&full[sl], (k / args.slots) & 1, abort_word, args.status, kStatusTimeoutFull))
+      ok = false;
+    if (ok) {
+      const uint8_t* slot = ring + sl * sbytes;
+      const uint8_t* cbox = slot + (warp >> 1) * rows * 128;  // this warp's group sits in box warp/2
+      const int j = (warp & 1) * 4 + c4;                       // 16-byte chunk of the row in that box
+      const float* scl = reinterpret_cast<const float*>(slot + rows * 256);
+      uint4 q[TPC][2];
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+      for (int t = 0; t < TPC; ++t)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          q[t][h] = *reinterpret_cast<const uint4*>(d + (2 * t + h) * 16);
-          sc[t][h] = *reinterpret_cast<const float*>(d + 64 + (2 * t + h) * 4);
+          const int r = 16 * t + g + 8 * h;
+          q[t][h] = *reinterpret_cast<const uint4*>(cbox + r * 128 + ((j ^ (r & 7)) << 4));
         }
-    }
-    float part[2][NT][4];
+      float part[PS][TPC][NT][4];
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
+      for (int p = 0; p < PS; ++p)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) part[t][nt][0] = part[t][nt][1] = part[t][nt][2] = part[t][nt][3] = 0.f;
-    // MMA k-step kk uses bytes 2kk (k = 32c4+4kk+{0,1}) and 2kk+1 (+{2,3}) of the thread's 16 bytes.
+        for (int t = 0; t < TPC; ++t)
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int col = (gi - g_begin) * 128 + 32 * c4 + 4 * kk;
-      uint32_t b[NT][2];
+          for (int nt = 0; nt < NT; ++nt) part[p][t][nt][0] = part[p][t][nt][1] = part[p][t][nt][2] = part[p][t][nt][3] = 0.f;
+      // Payload word w of the thread's 16 bytes holds columns 32c4 + 8w + [0, 8);
+      // MMA k-step kk = 2w + s uses its pairs 2s (columns +4s+{0,1}) and 2s+1 (+{2,3}).
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const uint2 bv = *reinterpret_cast<const uint2*>(xs + (8 * nt + g) * ks_pad + col);
-        b[nt][0] = bv.x;
-        b[nt][1] = bv.y;
-      }
-      const uint32_t wsel = kk >> 1;             // word of the 16-byte chunk
-      const uint32_t p0 = 2 * (kk & 1), p1 = p0 + 1;
+      for (int w = 0; w < 4; ++w) {
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const uint32_t w0 = wsel == 0 ? q[t][0].x : wsel == 1 ? q[t][0].y : wsel == 2 ? q[t][0].z : q[t][0].w;
-        const uint32_t w1 = wsel == 0 ? q[t][1].x : wsel == 1 ? q[t][1].y : wsel == 2 ? q[t][1].z : q[t][1].w;
-        const uint32_t a0 = lut_pair(lut_lane, w0, p0), a1 = lut_pair(lut_lane, w1, p0);
-        const uint32_t a2 = lut_pair(lut_lane, w0, p1), a3 = lut_pair(lut_lane, w1, p1);
+        for (int t = 0; t < TPC; ++t) {
+          uint32_t e0[4], e1[4];  // rows g and g + 8
+          lookup8(table, word4(q[t][0], w), e0);
+          lookup8(table, word4(q[t][1], w), e1);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma16816(part[t][nt], a0, a1, a2, a3, b[nt][0], b[nt][1]);
-      }
-    }
+          for (int sub = 0; sub < 2; ++sub) {
+            const int kk = 2 * w + sub;
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        acc[t][nt][0] = fmaf(sc[t][0], part[t][nt][0], acc[t][nt][0]);
-        acc[t][nt][1] = fmaf(sc[t][0], part[t][nt][1], acc[t][nt][1]);
-        acc[t][nt][2] = fmaf(sc[t][1], part[t][nt][2], acc[t][nt][2]);
-        acc[t][nt][3] = fmaf(sc[t][1], part[t][nt][3], acc[t][nt][3]);
-      }
-  }
-  cp_async_wait<0>();
-
-  // ------------------------------------------------------------ cluster reduction
-  // Accumulator element i of tile t / token tile nt: row rows[t][i / 2],
-  // token 8*nt + 2*c4 + (i & 1).  Slot within the CTA: (local row, token).
-  cluster_sync();  // every CTA is past its reads of X / the table; rank 0's `red` is free
-  if (crank != 0) {
-    const uint32_t base = mapa_shared(smem_u32(red), 0) + static_cast<uint32_t>((crank - 1) * kRows * 8 * NT * 4);
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int lr = kRowsPerWarp * warp + 16 * t + g + 8 * (i >> 1);
-          const int tok = 8 * nt + 2 * c4 + (i & 1);
-          st_shared_cluster_u32(base + (lr * 8 * NT + tok) * 4, __float_as_uint(acc[t][nt][i]));
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint4& xq = xv[nt][w];
+              const uint32_t b0 = sub ? xq.z : xq.x, b1 = sub ? xq.w : xq.y;
+              mma16816(part[kk % PS][t][nt], e0[2 * sub], e1[2 * sub], e0[2 * sub + 1], e1[2 * sub + 1], b0, b1);
+            }
+          }
         }
-  }
-  cluster_sync();
-  if (crank == 0) {
-    // LoRA operands for the epilogue, staged once in areas the main loop is
-    // done with: Ts rows of the tokens in the X slice (>= 8*NT*136 bf16), the
-    // CTA's Blora rows in the 32 KiB byte table (kRows x rank <= 64 floats).
-    float* ts_s = reinterpret_cast<float*>(xs);                   // [8*NT][64]
-    float* b_s = reinterpret_cast<float*>(lut_s);                 // [kRows][rank]
-    if (rank > 0) {
-      for (int idx = threadIdx.x; idx < 8 * NT * 64; idx += kThreads) {
-        const int tok = idx >> 6, j = idx & 63;
-        ts_s[idx] = (tok < M && j < rank) ? __bfloat162float(Ts[static_cast<size_t>(tok) * 64 + j]) : 0.f;
       }
-      for (int idx = threadIdx.x; idx < kRows * rank; idx += kThreads) {
-        const int lr = idx / rank;
-        b_s[idx] = (n0 + lr < N) ? __ldg(blora + static_cast<size_t>(n0) * rank + idx) : 0.f;
+#pragma unroll
+      for (int t = 0; t < TPC; ++t) {
+        const int r0 = 16 * t + g, r1 = r0 + 8;
+        const float s0 = scl[r0 * 4 + warp], s1 = scl[r1 * 4 + warp];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float v[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[i] = PS == 2 ? part[0][t][nt][i] + part[PS - 1][t][nt][i] : part[0][t][nt][i];
+          acc[t][nt][0] = fmaf(s0, v[0], acc[t][nt][0]);
+          acc[t][nt][1] = fmaf(s0, v[1], acc[t][nt][1]);
+          acc[t][nt][2] = fmaf(s1, v[2], acc[t][nt][2]);
+          acc[t][nt][3] = fmaf(s1, v[3], acc[t][nt][3]);
+        }
       }
     }
     __syncthreads();
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int lr = kRowsPerWarp * warp + 16 * t + g + 8 * (i >> 1);
-          const int tok = 8 * nt + 2 * c4 + (i & 1);
-          float v = acc[t][nt][i];
-          for (int p = 0; p < split - 1; ++p) v += red[(p * kRows + lr) * 8 * NT + tok];
-          const int n = n0 + lr;
-          if (n < N && tok < M) {
-            const float* tr = ts_s + tok * 64;
-            const float* br = b_s + lr * rank;
-            for (int j = 0; j < rank; ++j) v = fmaf(tr[j], br[j], v);
-            Y[static_cast<size_t>(tok) * N + n] = __float2bfloat16_rn(v);
-          }
-        }
+    if (threadIdx.x == 0 && issued < n_ch && !*abort_word) {
+      fence_proxy_async_smem();  // the slot's generic reads before the async-proxy refill
+      issue(issued);
+      ++issued;
+    }
+  };
+  uint4 xa[NT][4], xb[NT][4];
+  if (n_ch > 0) load_x(chunk_of(0), xa);
+  for (int k = 0; k < n_ch; k += 2) {
+    if (k + 1 < n_ch) load_x(chunk_of(k + 1), xb);
+    chunk(k, xa);
+    if (k + 1 < n_ch) {
+      if (k + 2 < n_ch) load_x(chunk_of(k + 2), xa);
+      chunk(k + 1, xb);
+    }
   }
+  // After an abort, loads already queued may still land: wait for them
+  // (bounded) before the shared memory is released.
+  if (threadIdx.x == 0 && *abort_word) {
+    for (int k = issued > args.slots ? issued - args.slots : 0; k < issued; ++k) {
+      uint32_t dummy = 0;
+      mbar_wait_short(&full[k % args.slots], (k / args.slots) & 1, &dummy, args.status, kStatusTimeoutDrain);
+    }
+  }
+
+  // ------------------------------------------------------------ reductions
+  // Warp partials -> red[warp][row][token]; accumulator element i of tile t:
+  // row 16t + g + 8*(i >> 1), token 8*nt + 2*c4 + (i & 1).
+#pragma unroll
+  for (int t = 0; t < TPC; ++t) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        red[(warp * rows + 16 * t + g + 8 * (i >> 1)) * 16 + 8 * nt + 2 * c4 + (i & 1)] = acc[t][nt][i];
+  }
+  __syncthreads();
+  // Sum the four group warps into red[0] (tokens past 8*NT stay unused).
+  for (int idx = threadIdx.x; idx < rows * 16; idx += kThreads)
+    red[idx] = red[idx] + red[rows * 16 + idx] + red[2 * rows * 16 + idx] + red[3 * rows * 16 + idx];
+  if (split > 1) {
+    cluster_sync();
+  } else {
+    __syncthreads();
+  }
+  if (kslice == 0) {
+    const uint32_t red_local = smem_u32(red);
+    for (int idx = threadIdx.x; idx < rows * 16; idx += kThreads) {
+      const int lr = idx >> 4, tok = idx & 15;
+      const int n = n0 + lr;
+      if (n < args.N && tok < args.M) {
+        float v = red[idx];
+        for (int p = 1; p < split; ++p)
+          v += __uint_as_float(ld_shared_cluster_u32(mapa_shared(red_local, static_cast<uint32_t>(p)) + idx * 4));
+        if (args.rank > 0) {
+          const __nv_bfloat16* tr = args.Ts + static_cast<size_t>(tok) * 64;
+          const float* br = args.blora + static_cast<size_t>(n) * args.rank;
+          for (int jj = 0; jj < args.rank; ++jj) v = fmaf(__bfloat162float(tr[jj]), __ldg(br + jj), v);
+        }
+        args.Y[static_cast<size_t>(tok) * args.N + n] = __float2bfloat16_rn(v);
+      }
+    }
+  }
+  if (split > 1) cluster_sync();  // peers' partials stay valid until rank 0 has read them
 }
 
-template <int NT>
-static int launch_nt(const void* X, const void* Ts, const uint8_t* codes, const float* scales, const float* lut,
-                     const float* blora, int rank, void* Y, int M, int N, int K, int split, cudaStream_t stream) {
-  const int groups = K / 128;
-  const int ks_pad = (groups + split - 1) / split * 128 + 8;
-  const size_t smem = kLutBytes + static_cast<size_t>(8 * NT) * ks_pad * 2 +
-                      static_cast<size_t>(split - 1) * kRows * 8 * NT * 4 + kRingBytes;
-  if (smem > 227 * 1024) return set_error(FL_ERR_UNSUPPORTED, "small-M path: K=%d too large", K);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&smallm_kernel<NT>),
+template <int NT, int TPC>
+static int launch_nt(const Args& a, const CUtensorMap& tc, const CUtensorMap& ts, int blocks, int smem,
+                     cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&smallm_kernel<NT, TPC>),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "small-M attr: %s", cudaGetErrorString(e));
-    attr_set = true;
+    attr_set[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(split * ((N + kRows - 1) / kRows));
+  cfg.gridDim = dim3(blocks * a.split);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = split;
+  attr[0].val.clusterDim.x = a.split;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t le = cudaLaunchKernelEx(&cfg, smallm_kernel<NT>, static_cast<const __nv_bfloat16*>(X),
-                                      static_cast<const __nv_bfloat16*>(Ts), codes, scales, lut, blora, rank,
-                                      static_cast<__nv_bfloat16*>(Y), M, N, K, split);
+  cudaError_t le = cudaLaunchKernelEx(&cfg, smallm_kernel<NT, TPC>, tc, ts, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "small-M launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }
@@ -271,23 +314,61 @@ static int launch_nt(const void* X, const void* Ts, const uint8_t* codes, const 
 
 int launch_smallm_fwd(const void* X, const void* Ts, const uint8_t* codes, const float* scales, const float* lut,
                       const float* lora, int rank, void* Y, int M, int N, int K, cudaStream_t stream) {
+  using namespace sm;
   if (M < 1 || M > 16) return set_error(FL_ERR_ARG, "small-M path needs 1 <= M <= 16");
-  if (K % 128 != 0) return set_error(FL_ERR_ARG, "small-M path needs K %% 128 == 0");
-  // Enough CTAs to cover the SMs twice; a cluster holds at most 8.
-  const int row_tiles = (N + sm::kRows - 1) / sm::kRows;
-  int split = (2 * 148 + row_tiles - 1) / row_tiles;
-  if (split > 4) split = 4;  // clusters of <= 4 keep several clusters resident per GPC
-  if (split > K / 128) split = K / 128;
-  if (split < 1) split = 1;
-  // Keep the X slice + partials within shared memory.
-  auto bytes = [&](int sp) {
-    return sm::kLutBytes + 16LL * ((K / 128 + sp - 1) / sp * 128 + 8) * 2 + (sp - 1) * sm::kRows * 16LL * 4 +
-           sm::kRingBytes;
-  };
-  while (split > 1 && bytes(split) > 220 * 1024) --split;
-  while (split < 8 && bytes(split) > 220 * 1024) ++split;
-  if (M <= 8) return sm::launch_nt<1>(X, Ts, codes, scales, lut, lora, rank, Y, M, N, K, split, stream);
-  return sm::launch_nt<2>(X, Ts, codes, scales, lut, lora, rank, Y, M, N, K, split, stream);
+  if (K % kChunkK != 0) return set_error(FL_ERR_ARG, "small-M path needs K %% 512 == 0");
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    sms = 148;
+  // One wave at kCtasPerSm CTAs per SM: the fewest 16-row tiles per CTA that
+  // fit (1, 2, 4 or 8).
+  const int tiles = (N + 15) / 16;
+  const int want = (tiles + kCtasPerSm * sms - 1) / (kCtasPerSm * sms);
+  int tpc = 1;
+  const int max_tpc = M <= 8 ? kMaxTpc : kMaxTpc / 2;  // 16 tokens x 8 tiles would spill registers
+  while (tpc < want && tpc < max_tpc) tpc *= 2;
+  const int rows = 16 * tpc;
+  const int blocks = (N + rows - 1) / rows;
+  // Too few row blocks: split the reduction across a cluster.
+  const int chunks = K / kChunkK;
+  int split = 1;
+  while (split < 8 && blocks * split * 2 <= kCtasPerSm * sms && chunks >= 2 * split) split *= 2;
+  const int sbytes = (slot_bytes(rows) + 1023) / 1024 * 1024;
+  int slots = kSlotBudget / sbytes;
+  if (slots > 8) slots = 8;
+  if (slots < 2) slots = 2;
+  const int smem = 1024 + slots * sbytes + kWarps * rows * 16 * 4 + slots * 8 + 16;
+  Args a;
+  a.X = static_cast<const __nv_bfloat16*>(X);
+  a.Ts = static_cast<const __nv_bfloat16*>(Ts);
+  a.lut = lut;
+  a.blora = lora;
+  a.Y = static_cast<__nv_bfloat16*>(Y);
+  a.status = status_word(dev);
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.rank = rank;
+  a.tpc = tpc;
+  a.split = split;
+  a.slots = slots;
+  CUtensorMap tc, ts;
+  int rc = make_tensor_map_2d(&tc, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, 128, rows,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tensor_map_2d(&ts, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, K / 128, N, static_cast<uint64_t>(K / 128) * 4,
+                          4, rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (M <= 8) {
+    if (tpc == 1) return launch_nt<1, 1>(a, tc, ts, blocks, smem, stream);
+    if (tpc == 2) return launch_nt<1, 2>(a, tc, ts, blocks, smem, stream);
+    if (tpc == 4) return launch_nt<1, 4>(a, tc, ts, blocks, smem, stream);
+    return launch_nt<1, 8>(a, tc, ts, blocks, smem, stream);
+  }
+  if (tpc == 1) return launch_nt<2, 1>(a, tc, ts, blocks, smem, stream);
+  if (tpc == 2) return launch_nt<2, 2>(a, tc, ts, blocks, smem, stream);
+  return launch_nt<2, 4>(a, tc, ts, blocks, smem, stream);
 }
 
 }  // namespace fl

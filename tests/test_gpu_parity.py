@@ -216,13 +216,18 @@ SMALLM_CASES = [
     (16, 14336, 4096, 16),
     (16, 4096, 14336, 16),
     (13, 200, 512, 64),      # ragged rows and tokens
+    (16, 1024, 1024, 8),     # reduction split over a 2-CTA cluster
+    (3, 1000, 2048, 32),     # row count not a multiple of 16
+    (16, 8192, 512, 16),     # one 512-wide chunk per CTA
+    (9, 4096, 14336, 64),    # 28 chunks through the slot ring, rank 64
 ]
 
 
 @pytest.mark.parametrize("codec_name", ["int4-sym-g128", "nf4-g128"])
 @pytest.mark.parametrize("M,N,K,rank", SMALLM_CASES)
 def test_small_m_fwd_parity(cuda_lib, codec_name, M, N, K, rank):
-    """M <= 16 runs the decode-step kernel (operand bf16(lut), scale on the partial sums)."""
+    """M <= 16 with K % 512 == 0 runs the decode-step kernel (operand bf16(lut), scale on the partial
+    sums); other K take the tile GEMM."""
     from spilltune_b200 import ops
     pw, x, A, B, _ = _problem(M, N, K, rank, codec_name, seed=M * 11 + N + K)
     s = 2.0

@@ -151,6 +151,39 @@ int fl_grouped_bwd(const uint16_t* dY, const uint16_t* X, const int32_t* seg, in
                    const float* B, int rank, float scale, uint16_t* dX, float* dA, float* dB, int accumulate,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * bitsandbytes NF4 with double quantization, block 64 ("NF4-DQ64") — the
+ * record the reference's Qwen3.5 NF4 path stages (CUDARecord,
+ * ram_vram_finetune/quantization/nf4_backend_cuda.py:522-644, layout checked
+ * at nf4_backend.py:184-278) and multiplies with bnb.matmul_4bit in
+ * linear_cuda (nf4_backend_cuda.py:888-917).  Layout: packed uint8
+ * [(N*K+1)/2], element 2i in the HIGH nibble of byte i and 2i+1 in the low
+ * nibble; absmax uint8 [ceil(N*K/64)]; nested_absmax fp32 [ceil(blocks/256)];
+ * nested_map fp32[256]; quant_map fp32[16]; nested_offset >= 0.
+ * bitsandbytes is not available to pin these numerics (the decode below is a
+ * restatement of its published format).
+ *
+ * fl_nf4dq_scales: the double-quantization prologue, FP32 block scales
+ *   scales[b] = fp32(nested_map[absmax[b]] * nested_absmax[b / 256]) + offset.
+ * fl_dequant_nf4dq: w[i] = bf16_rne(fp32(quant_map[code_i] * scales[i / 64])).
+ * fl_fwd_nf4dq / fl_bwd_nf4dq: fl_fwd / fl_bwd on such a record (block_scales
+ * from fl_nf4dq_scales, computed once per staged record), same workspace
+ * sizes, same LoRA branch; every M takes the tile GEMM.
+ * Requires K % 128 == 0 (and N % 64 == 0 for the backward), packed 16-byte
+ * aligned.
+ */
+int fl_nf4dq_scales(const uint8_t* absmax_q, const float* nested_absmax, const float* nested_map, float offset,
+                    int64_t blocks, float* scales_out, void* stream);
+int fl_dequant_nf4dq(const uint8_t* packed, const float* block_scales, const float* quant_map, int64_t numel,
+                     uint16_t* out_bf16, void* stream);
+int fl_fwd_nf4dq(const uint16_t* X, int64_t M, int64_t K, const uint8_t* packed, const float* block_scales,
+                 const float* quant_map, int64_t N, const float* A, const float* B, int rank, float scale, uint16_t* Y,
+                 void* workspace, size_t workspace_bytes, void* stream);
+int fl_bwd_nf4dq(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* packed,
+                 const float* block_scales, const float* quant_map, const float* A, const float* B, int rank,
+                 float scale, uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -2,7 +2,10 @@
 
 Restates ``ram_vram_finetune/quantization/codecs.py`` (encode :66-116,
 unpack_codes :55-64, decode_into :158-170, validate_spec :119-155) for the
-int4-sym-g128 format, plus the NF4 group-128 codebook variant.
+int4-sym-g128 format, plus the NF4 group-128 codebook variant, plus the
+bitsandbytes NF4 double-quantized block-64 record the reference's NF4 path
+uses (layout validated at quantization/nf4_backend.py:184-278; bitsandbytes
+itself is absent, so that decode is a restatement with parity unpinned).
 """
 import ctypes
 import os
@@ -59,6 +62,10 @@ def lib():
         L.oracle_encode_nf4.restype = ctypes.c_int
         L.oracle_validate_int4_sym.argtypes = [p, p, i64]
         L.oracle_validate_int4_sym.restype = ctypes.c_int
+        L.oracle_nf4dq_absmax.argtypes = [p, p, p, ctypes.c_float, i64, p]
+        L.oracle_nf4dq_decode.argtypes = [p, p, p, i64, p]
+        L.oracle_nf4dq_encode.argtypes = [p, i64, p, p, p, p, p, p]
+        L.oracle_nf4dq_encode.restype = ctypes.c_float
         L.oracle_f32_to_bf16.argtypes = [ctypes.c_float]
         L.oracle_f32_to_bf16.restype = ctypes.c_uint16
         _lib = L
@@ -116,3 +123,61 @@ def validate_int4_sym(payload, scales, numel):
 
 def bf16_bits_to_f32(bits):
     return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ---------------------------------------------------------------- NF4-DQ64
+DQ_BLOCK = 64
+DQ_NESTED = 256
+
+
+def dynamic_map():
+    """The 256-entry signed dynamic ("dynamic tree") map that bitsandbytes uses
+    as the nested_quant_map of double quantization, rebuilt from its published
+    construction (Dettmers et al., 8-bit optimizers via block-wise
+    quantization): for each exponent level i = 0..6, the 2**i midpoints of
+    2**i + 1 evenly spaced points on [0.1, 1], scaled by 10**(i - 6), with
+    both signs; plus 0 and 1; sorted.  Parity with the package is unpinned."""
+    vals = [0.0, 1.0]
+    for i in range(7):
+        pts = np.linspace(0.1, 1.0, 2 ** i + 1, dtype=np.float64)
+        mids = (pts[:-1] + pts[1:]) / 2.0 * 10.0 ** (i - 6)
+        vals += list(mids) + list(-mids)
+    assert len(vals) == 256
+    return np.sort(np.array(vals, dtype=np.float32))
+
+
+def nf4dq_encode(x, quant_map=NF4_LUT, nested_map=None):
+    """Test-fixture NF4-DQ64 record of a float array (flattened): returns
+    (packed uint8[(n+1)/2], absmax uint8[blocks], nested_absmax fp32, offset)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    quant_map = np.ascontiguousarray(quant_map, dtype=np.float32)
+    nested_map = dynamic_map() if nested_map is None else np.ascontiguousarray(nested_map, dtype=np.float32)
+    blocks = (x.size + DQ_BLOCK - 1) // DQ_BLOCK
+    packed = np.zeros((x.size + 1) // 2, np.uint8)
+    absmax_q = np.zeros(blocks, np.uint8)
+    nested = np.zeros((blocks + DQ_NESTED - 1) // DQ_NESTED, np.float32)
+    tmp = np.zeros(blocks, np.float32)
+    offset = lib().oracle_nf4dq_encode(_ptr(x), x.size, _ptr(quant_map), _ptr(nested_map), _ptr(packed),
+                                       _ptr(absmax_q), _ptr(nested), _ptr(tmp))
+    return packed, absmax_q, nested, float(offset)
+
+
+def nf4dq_absmax(absmax_q, nested_absmax, nested_map, offset):
+    """FP32 block scales of a DQ64 record (the double-quantization prologue)."""
+    absmax_q = np.ascontiguousarray(absmax_q, dtype=np.uint8)
+    nested_absmax = np.ascontiguousarray(nested_absmax, dtype=np.float32)
+    nested_map = np.ascontiguousarray(nested_map, dtype=np.float32)
+    out = np.empty(absmax_q.size, np.float32)
+    lib().oracle_nf4dq_absmax(_ptr(absmax_q), _ptr(nested_absmax), _ptr(nested_map), float(offset), absmax_q.size,
+                              _ptr(out))
+    return out
+
+
+def nf4dq_decode(packed, absmax_f32, numel, quant_map=NF4_LUT):
+    """BF16 bit patterns of a DQ64 record given its FP32 block scales."""
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    absmax_f32 = np.ascontiguousarray(absmax_f32, dtype=np.float32)
+    quant_map = np.ascontiguousarray(quant_map, dtype=np.float32)
+    out = np.empty(numel, np.uint16)
+    lib().oracle_nf4dq_decode(_ptr(packed), _ptr(absmax_f32), _ptr(quant_map), numel, _ptr(out))
+    return out

@@ -193,3 +193,89 @@ int oracle_validate_int4_sym(const uint8_t *payload, const float *scales, int64_
     }
     return 0;
 }
+
+/* ------------------------------------------------------------------------
+ * bitsandbytes NF4 with double quantization, block 64 ("NF4-DQ64"), the
+ * record the reference's Qwen3.5 NF4 path stages and multiplies
+ * (ram_vram_finetune/quantization/nf4_backend.py:184-278 validates its
+ * layout: packed uint8 [(numel+1)/2], absmax uint8 [ceil(numel/64)],
+ * nested_absmax fp32 [ceil(blocks/256)], nested_quant_map fp32[256],
+ * quant_map fp32[16], nested_offset >= 0).  bitsandbytes 0.50.2 is absent
+ * here, so this is a restatement of its published format, PARITY UNPINNED:
+ *   block absmax  a[b] = fp32(nested_map[absmax[b]] * nested_absmax[b / 256]) + offset
+ *   element i     w[i] = bf16_rne(fp32(quant_map[code_i] * a[i / 64]))
+ *   code_i        high nibble of packed[i / 2] for even i, low nibble for odd i.
+ * ------------------------------------------------------------------------ */
+#define DQ_BLOCK 64
+#define DQ_NESTED 256
+
+void oracle_nf4dq_absmax(const uint8_t *absmax_q, const float *nested_absmax, const float *nested_map,
+                         float offset, int64_t blocks, float *out) {
+    for (int64_t b = 0; b < blocks; ++b) {
+        float v = nested_map[absmax_q[b]] * nested_absmax[b / DQ_NESTED];
+        out[b] = v + offset;
+    }
+}
+
+void oracle_nf4dq_decode(const uint8_t *packed, const float *absmax, const float *quant_map, int64_t numel,
+                         uint16_t *out) {
+    for (int64_t i = 0; i < numel; ++i) {
+        uint8_t byte = packed[i >> 1];
+        int code = (i & 1) ? (byte & 15) : (byte >> 4);
+        out[i] = oracle_f32_to_bf16(quant_map[code] * absmax[i / DQ_BLOCK]);
+    }
+}
+
+/* Nearest entry of a sorted-or-not table (ties to the lower index). */
+static int nearest(const float *table, int n, float x) {
+    int best = 0;
+    float bd = fabsf(x - table[0]);
+    for (int c = 1; c < n; ++c) {
+        float d = fabsf(x - table[c]);
+        if (d < bd) { bd = d; best = c; }
+    }
+    return best;
+}
+
+/* Test-fixture encoder of the same layout (no bitsandbytes available): block
+ * absmax (1.0 for an all-zero block), NF4 code nearest to x/absmax; offset =
+ * mean of the block absmaxes; (absmax - offset) quantized per 256 blocks to
+ * the nearest nested_map entry of (absmax - offset) / max|absmax - offset|
+ * (nested_absmax = that max, 1.0 when it is 0).  Returns the offset. */
+float oracle_nf4dq_encode(const float *x, int64_t numel, const float *quant_map, const float *nested_map,
+                          uint8_t *packed, uint8_t *absmax_q, float *nested_absmax, float *absmax_tmp) {
+    int64_t blocks = (numel + DQ_BLOCK - 1) / DQ_BLOCK;
+    double sum = 0.0;
+    for (int64_t b = 0; b < blocks; ++b) {
+        float amax = 0.0f;
+        for (int i = 0; i < DQ_BLOCK; ++i) {
+            int64_t idx = b * DQ_BLOCK + i;
+            if (idx < numel && fabsf(x[idx]) > amax) amax = fabsf(x[idx]);
+        }
+        absmax_tmp[b] = amax == 0.0f ? 1.0f : amax;
+        sum += absmax_tmp[b];
+    }
+    float offset = (float)(sum / (double)blocks);
+    int64_t nb = (blocks + DQ_NESTED - 1) / DQ_NESTED;
+    for (int64_t s = 0; s < nb; ++s) {
+        float m = 0.0f;
+        for (int64_t b = s * DQ_NESTED; b < blocks && b < (s + 1) * DQ_NESTED; ++b) {
+            float d = fabsf(absmax_tmp[b] - offset);
+            if (d > m) m = d;
+        }
+        nested_absmax[s] = m == 0.0f ? 1.0f : m;
+        for (int64_t b = s * DQ_NESTED; b < blocks && b < (s + 1) * DQ_NESTED; ++b)
+            absmax_q[b] = (uint8_t)nearest(nested_map, 256, (absmax_tmp[b] - offset) / nested_absmax[s]);
+    }
+    /* Codes against the absmax the decoder will reconstruct. */
+    for (int64_t b = 0; b < blocks; ++b)
+        absmax_tmp[b] = nested_map[absmax_q[b]] * nested_absmax[b / DQ_NESTED] + offset;
+    if (numel > 0) memset(packed, 0, (size_t)((numel + 1) / 2));
+    for (int64_t i = 0; i < numel; ++i) {
+        float a = absmax_tmp[i / DQ_BLOCK];
+        int code = nearest(quant_map, 16, a != 0.0f ? x[i] / a : 0.0f);
+        if (i & 1) packed[i >> 1] |= (uint8_t)code;
+        else packed[i >> 1] |= (uint8_t)(code << 4);
+    }
+    return offset;
+}

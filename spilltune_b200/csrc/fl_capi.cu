@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <mutex>
 
+#include "fl_codebook.cuh"
 #include "fl_host.h"
 
 namespace fl {
@@ -107,17 +108,20 @@ static int check_common(const char* who, int64_t M, int64_t N, int64_t K, int ra
   return FL_OK;
 }
 
-int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, const float* scales, const float* lut16,
-           int64_t N, const float* A, const float* B, int rank, float scale, uint16_t* Y, void* workspace,
-           size_t workspace_bytes, void* stream) {
-  int rc = check_common("fl_fwd", M, N, K, rank, payload, scales, lut16);
+}  // extern "C"
+
+// Forward / backward bodies shared by the two record layouts.
+static int fwd_impl(const char* who, int layout, const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload,
+                    const float* scales, const float* lut16, int64_t N, const float* A, const float* B, int rank,
+                    float scale, uint16_t* Y, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_common(who, M, N, K, rank, payload, scales, lut16);
   if (rc) return rc;
-  if (!X || !Y) return set_error(FL_ERR_ARG, "fl_fwd: null X/Y");
-  if (!aligned16(X)) return set_error(FL_ERR_ARG, "fl_fwd: X must be 16-byte aligned");
+  if (!X || !Y) return set_error(FL_ERR_ARG, "%s: null X/Y", who);
+  if (!aligned16(X)) return set_error(FL_ERR_ARG, "%s: X must be 16-byte aligned", who);
   if (rank > 0) {
-    if (!A || !B) return set_error(FL_ERR_ARG, "fl_fwd: null LoRA factor");
+    if (!A || !B) return set_error(FL_ERR_ARG, "%s: null LoRA factor", who);
     if (!workspace || workspace_bytes < fl_fwd_workspace_bytes(M, K, rank) || !aligned16(workspace))
-      return set_error(FL_ERR_ARG, "fl_fwd: workspace missing, short or misaligned");
+      return set_error(FL_ERR_ARG, "%s: workspace missing, short or misaligned", who);
   }
   uint32_t* status = nullptr;
   if ((rc = current_status(&status))) return rc;
@@ -129,24 +133,26 @@ int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, cons
   }
   // Decode-like steps (M <= 16) are bound by the weight bytes: dedicated kernel
   // (it streams 512-wide column chunks; other K take the tile GEMM).
-  if (M <= 16 && K % 512 == 0) return launch_smallm_fwd(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st);
-  return launch_fwd_gemm(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st);
+  if (layout == kLayoutG128 && M <= 16 && K % 512 == 0)
+    return launch_smallm_fwd(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st);
+  return launch_fwd_gemm(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st,
+                         nullptr, nullptr, 1, 0, layout);
 }
 
-int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* payload,
-           const float* scales, const float* lut16, const float* A, const float* B, int rank, float scale,
-           uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace, size_t workspace_bytes,
-           void* stream) {
-  int rc = check_common("fl_bwd", M, N, K, rank, payload, scales, lut16);
+static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N,
+                    int64_t K, const uint8_t* payload, const float* scales, const float* lut16, const float* A,
+                    const float* B, int rank, float scale, uint16_t* dX, float* dA, float* dB, int accumulate,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_common(who, M, N, K, rank, payload, scales, lut16);
   if (rc) return rc;
-  if (N % 64 != 0) return set_error(FL_ERR_ARG, "fl_bwd: out_features N=%lld must be a multiple of 64", (long long)N);
-  if (!dY || !dX) return set_error(FL_ERR_ARG, "fl_bwd: null dY/dX");
-  if (!aligned16(dY)) return set_error(FL_ERR_ARG, "fl_bwd: dY must be 16-byte aligned");
+  if (N % 64 != 0) return set_error(FL_ERR_ARG, "%s: out_features N=%lld must be a multiple of 64", who, (long long)N);
+  if (!dY || !dX) return set_error(FL_ERR_ARG, "%s: null dY/dX", who);
+  if (!aligned16(dY)) return set_error(FL_ERR_ARG, "%s: dY must be 16-byte aligned", who);
   if (rank > 0) {
-    if (!X || !A || !B || !dA || !dB) return set_error(FL_ERR_ARG, "fl_bwd: null X or LoRA factor/gradient");
-    if (!aligned16(X)) return set_error(FL_ERR_ARG, "fl_bwd: X must be 16-byte aligned");
+    if (!X || !A || !B || !dA || !dB) return set_error(FL_ERR_ARG, "%s: null X or LoRA factor/gradient", who);
+    if (!aligned16(X)) return set_error(FL_ERR_ARG, "%s: X must be 16-byte aligned", who);
     if (!workspace || workspace_bytes < fl_bwd_workspace_bytes(M, N, K, rank) || !aligned16(workspace))
-      return set_error(FL_ERR_ARG, "fl_bwd: workspace missing, short or misaligned");
+      return set_error(FL_ERR_ARG, "%s: workspace missing, short or misaligned", who);
   }
   uint32_t* status = nullptr;
   if ((rc = current_status(&status))) return rc;
@@ -161,7 +167,8 @@ int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t 
     // Ts = bf16(s * X . A^T): Q(j, k) = A[j * K + k]
     if ((rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, qc_a, st))) return rc;
   }
-  if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, (int)M, (int)N, (int)K, status, st)))
+  if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, (int)M, (int)N, (int)K, status, st,
+                            nullptr, nullptr, 1, 0, layout)))
     return rc;
   if (rank > 0) {
     // dA[j, k] = sum_m Us[m, j] X[m, k]
@@ -170,6 +177,59 @@ int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t 
     if ((rc = launch_lora_grad(dY, (int)M, (int)N, ts, rank, dB, rank, 1, accumulate, st))) return rc;
   }
   return FL_OK;
+}
+
+extern "C" {
+
+int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, const float* scales, const float* lut16,
+           int64_t N, const float* A, const float* B, int rank, float scale, uint16_t* Y, void* workspace,
+           size_t workspace_bytes, void* stream) {
+  return fwd_impl("fl_fwd", kLayoutG128, X, M, K, payload, scales, lut16, N, A, B, rank, scale, Y, workspace,
+                  workspace_bytes, stream);
+}
+
+int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* payload,
+           const float* scales, const float* lut16, const float* A, const float* B, int rank, float scale,
+           uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace, size_t workspace_bytes,
+           void* stream) {
+  return bwd_impl("fl_bwd", kLayoutG128, dY, X, M, N, K, payload, scales, lut16, A, B, rank, scale, dX, dA, dB,
+                  accumulate, workspace, workspace_bytes, stream);
+}
+
+// ---------------------------------------------------------------- NF4-DQ64
+int fl_nf4dq_scales(const uint8_t* absmax_q, const float* nested_absmax, const float* nested_map, float offset,
+                    int64_t blocks, float* scales_out, void* stream) {
+  if (blocks < 0) return set_error(FL_ERR_ARG, "fl_nf4dq_scales: negative block count");
+  if (blocks == 0) return FL_OK;
+  if (!absmax_q || !nested_absmax || !nested_map || !scales_out)
+    return set_error(FL_ERR_ARG, "fl_nf4dq_scales: null pointer");
+  if (!(offset >= 0.0f) || offset != offset) return set_error(FL_ERR_ARG, "fl_nf4dq_scales: offset must be >= 0");
+  return launch_nf4dq_prologue(absmax_q, nested_absmax, nested_map, offset, blocks, scales_out,
+                               static_cast<cudaStream_t>(stream));
+}
+
+int fl_dequant_nf4dq(const uint8_t* packed, const float* block_scales, const float* quant_map, int64_t numel,
+                     uint16_t* out_bf16, void* stream) {
+  if (numel < 0) return set_error(FL_ERR_ARG, "fl_dequant_nf4dq: negative numel");
+  if (numel == 0) return FL_OK;
+  if (!packed || !block_scales || !quant_map || !out_bf16) return set_error(FL_ERR_ARG, "fl_dequant_nf4dq: null pointer");
+  return launch_dequant(packed, block_scales, quant_map, numel, out_bf16, static_cast<cudaStream_t>(stream),
+                        kLayoutNf4Dq64);
+}
+
+int fl_fwd_nf4dq(const uint16_t* X, int64_t M, int64_t K, const uint8_t* packed, const float* block_scales,
+                 const float* quant_map, int64_t N, const float* A, const float* B, int rank, float scale, uint16_t* Y,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  return fwd_impl("fl_fwd_nf4dq", kLayoutNf4Dq64, X, M, K, packed, block_scales, quant_map, N, A, B, rank, scale, Y,
+                  workspace, workspace_bytes, stream);
+}
+
+int fl_bwd_nf4dq(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* packed,
+                 const float* block_scales, const float* quant_map, const float* A, const float* B, int rank,
+                 float scale, uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  return bwd_impl("fl_bwd_nf4dq", kLayoutNf4Dq64, dY, X, M, N, K, packed, block_scales, quant_map, A, B, rank, scale,
+                  dX, dA, dB, accumulate, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -44,6 +44,25 @@ __device__ __forceinline__ void lookup4(const ProductTable& t, uint32_t sel, uin
   out1 = prmt(lo, hi, 0x7362);
 }
 
+// Record layouts the kernels decode (FL_LAYOUT_* in the C header):
+//   0  the reference's group-128 record: even element in the low nibble,
+//      one FP32 scale per 128 elements;
+//   1  bitsandbytes NF4 double-quantized, block 64: even element in the HIGH
+//      nibble, one FP32 scale per 64 elements (from the DQ prologue).
+constexpr int kLayoutG128 = 0;
+constexpr int kLayoutNf4Dq64 = 1;
+
+// As lookup4, for a word whose codes are paired high nibble first: returns
+// out0 = {e1 (low half), e0}, out1 = {e3, e2} — the element order of a
+// high-nibble-first byte stream.
+__device__ __forceinline__ void lookup4_hf(const ProductTable& t, uint32_t sel, uint32_t mask, uint32_t& out0,
+                                           uint32_t& out1) {
+  const uint32_t lo = (prmt(t.lo[0], t.lo[1], sel) & ~mask) | (prmt(t.lo[2], t.lo[3], sel) & mask);
+  const uint32_t hi = (prmt(t.hi[0], t.hi[1], sel) & ~mask) | (prmt(t.hi[2], t.hi[3], sel) & mask);
+  out0 = prmt(lo, hi, 0x4051);
+  out1 = prmt(lo, hi, 0x6273);
+}
+
 // Eight codes of one 32-bit payload word (element i in nibble i) -> four bf16x2
 // words in element order.  The selector and bit-3 masks of both halves come
 // from one AND, one shift and two prmt (sign-replicate mode): byte i of a mask
@@ -55,6 +74,25 @@ __device__ __forceinline__ void lookup8(const ProductTable& t, uint32_t w, uint3
   const uint32_t mask_hi = prmt(w4, w, 0xFBEA);  // codes 4..7
   lookup4(t, sel, mask_lo, out[0], out[1]);
   lookup4(t, sel >> 16, mask_hi, out[2], out[3]);
+}
+
+}  // namespace fl
+
+namespace fl {
+
+// Layout-generic form: four bf16x2 words in element order for either layout.
+template <int kLayout>
+__device__ __forceinline__ void lookup8_l(const ProductTable& t, uint32_t w, uint32_t* out) {
+  if constexpr (kLayout == kLayoutG128) {
+    lookup8(t, w, out);
+  } else {
+    const uint32_t sel = w & 0x77777777u;
+    const uint32_t w4 = w << 4;
+    const uint32_t mask_lo = prmt(w4, w, 0xD9C8);
+    const uint32_t mask_hi = prmt(w4, w, 0xFBEA);
+    lookup4_hf(t, sel, mask_lo, out[0], out[1]);
+    lookup4_hf(t, sel >> 16, mask_hi, out[2], out[3]);
+  }
 }
 
 }  // namespace fl

@@ -131,6 +131,8 @@ __device__ __forceinline__ Tile tile_at(const GemmArgs& args, int t, int num_w, 
 // producer prefetches the next tile while the current one finishes; the
 // accumulator is drained into a shared-memory staging tile (released to the
 // MMA issuer as soon as it is read) and leaves by an asynchronous TMA store.
+// kLayout selects the record layout the dequant warps decode (fl_codebook.cuh).
+template <int kLayout>
 __global__ void __launch_bounds__(kThreads, 1)
     fl_tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,   // X, [M, K] bf16, box {64, 128}
                       const __grid_constant__ CUtensorMap tm_low,   // Ts, [M, 64] bf16, box {64, 128}
@@ -357,15 +359,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (32 TMEM columns).
       const int n = l0 + row;
       const bool valid = n < N;
-      const float* srow = args.scales + static_cast<size_t>(wrow0 + (valid ? n : 0)) * groups_per_row;
-      float next_scale = (valid && grp < groups_per_row) ? __ldg(srow + grp) : 0.0f;
+      // Scales per row: one per 128-group (layout 0) or per 64-block = per stage
+      // (layout 1).  A stage pair is one group, or two blocks.
+      constexpr bool kBlock64 = kLayout == kLayoutNf4Dq64;
+      const int spr = kBlock64 ? 2 * groups_per_row : groups_per_row;
+      const float* srow = args.scales + static_cast<size_t>(wrow0 + (valid ? n : 0)) * spr;
+      float next_scale = (valid && grp < groups_per_row) ? __ldg(srow + (kBlock64 ? 2 * grp : grp)) : 0.0f;
+      float next_scale2 = (kBlock64 && valid && grp < groups_per_row) ? __ldg(srow + 2 * grp + 1) : 0.0f;
       for (int pit = 2 * grp; pit < n_iter || (pit == 2 * grp && tl > 0); pit += 2 * kGroups) {
         if (pit < n_iter && ok) {
           ProductTable table;
+          float sc_a = 0.f, sc_b = 0.f;  // layout 1: the pair's two block scales
           if (pit < n_main) {
-            table = make_table(lut_s, next_scale);
             const int g_next = pit / 2 + kGroups;
-            next_scale = (valid && g_next < groups_per_row) ? __ldg(srow + g_next) : 0.0f;
+            if constexpr (kBlock64) {
+              sc_a = next_scale;
+              sc_b = next_scale2;
+              next_scale = (valid && g_next < groups_per_row) ? __ldg(srow + 2 * g_next) : 0.0f;
+              next_scale2 = (valid && g_next < groups_per_row) ? __ldg(srow + 2 * g_next + 1) : 0.0f;
+            } else {
+              table = make_table(lut_s, next_scale);
+              next_scale = (valid && g_next < groups_per_row) ? __ldg(srow + g_next) : 0.0f;
+            }
           }
           for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
             const int gi = g0 + it;
@@ -383,16 +398,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             uint32_t v[32];
             if (it < n_main) {
+              if constexpr (kBlock64) table = make_table(lut_s, it == pit ? sc_a : sc_b);
               const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + row * 32);
               const uint4 q0 = q[0], q1 = q[1];
-              lookup8(table, q0.x, v + 0);
-              lookup8(table, q0.y, v + 4);
-              lookup8(table, q0.z, v + 8);
-              lookup8(table, q0.w, v + 12);
-              lookup8(table, q1.x, v + 16);
-              lookup8(table, q1.y, v + 20);
-              lookup8(table, q1.z, v + 24);
-              lookup8(table, q1.w, v + 28);
+              lookup8_l<kLayout>(table, q0.x, v + 0);
+              lookup8_l<kLayout>(table, q0.y, v + 4);
+              lookup8_l<kLayout>(table, q0.z, v + 8);
+              lookup8_l<kLayout>(table, q0.w, v + 12);
+              lookup8_l<kLayout>(table, q1.x, v + 16);
+              lookup8_l<kLayout>(table, q1.y, v + 20);
+              lookup8_l<kLayout>(table, q1.z, v + 24);
+              lookup8_l<kLayout>(table, q1.w, v + 28);
             } else {
               // LoRA stage: A row = bf16(Blora[n, 0:64]) zero padded past the rank.
 #pragma unroll
@@ -520,7 +536,10 @@ int resident_pairs(const void* kernel, int threads, int smem, int* pairs) {
 // blora: [N, rank] fp32; y: [M, N] bf16.
 int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
                     const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
-                    cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles) {
+                    cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles,
+                    int layout) {
+  if (layout != kLayoutG128 && layout != kLayoutNf4Dq64) return set_error(FL_ERR_ARG, "fwd gemm: unknown layout");
+  if (layout != kLayoutG128 && tiles) return set_error(FL_ERR_UNSUPPORTED, "grouped launches use layout 0");
   CUtensorMap tm_act, tm_low, tm_code;
   int rc = make_tensor_map_2d(&tm_act, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, static_cast<uint64_t>(K) * 2, 64,
                               kTokHalf, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -560,8 +579,9 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
   // can be resident at once.
   const int tiles_max = tiles ? max_tiles : ((N + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok);
   int pairs = 0;
-  if ((rc = resident_pairs(reinterpret_cast<const void*>(&fl_tc_gemm_kernel), kThreads, kSmemBytes, &pairs)))
-    return rc;
+  const void* kfn = layout == kLayoutG128 ? reinterpret_cast<const void*>(&fl_tc_gemm_kernel<kLayoutG128>)
+                                          : reinterpret_cast<const void*>(&fl_tc_gemm_kernel<kLayoutNf4Dq64>);
+  if ((rc = resident_pairs(kfn, kThreads, kSmemBytes, &pairs))) return rc;
   if (pairs > tiles_max) pairs = tiles_max;
   if (pairs < 1) return FL_OK;
   cudaLaunchConfig_t cfg = {};
@@ -576,7 +596,9 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t le = cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel, tm_act, tm_low, tm_code, tm_out, a);
+  cudaError_t le = layout == kLayoutG128
+                       ? cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<kLayoutG128>, tm_act, tm_low, tm_code, tm_out, a)
+                       : cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<kLayoutNf4Dq64>, tm_act, tm_low, tm_code, tm_out, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "fwd gemm launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }

@@ -111,6 +111,7 @@ __device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int 
 // Persistent: each CTA pair walks tiles pair, pair + P, ...; stage counters
 // run on across tiles and the two TMEM accumulators alternate, so the MMAs of
 // the next tile overlap the drain of the previous one.
+template <int kLayout>
 __global__ void __launch_bounds__(kThreads, 1)
     fl_bwd_ss_kernel(const __grid_constant__ CUtensorMap tm_dy,    // dY [M, N] bf16, box {64, 128}
                      const __grid_constant__ CUtensorMap tm_us,    // Us [M, 64] bf16, box {64, 128}
@@ -297,12 +298,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int wrow0 = tile.expert * N;
       const float* alora = args.alora + static_cast<size_t>(tile.expert) * args.rank * K;
       const bool tile_valid = kb < K;
-      const int gsc = tile_valid ? kb / 128 : 0;  // the CTA's 128 columns share one scale group
+      // Layout 0: the CTA's 128 columns share one 128-group scale; layout 1:
+      // each thread's 64 columns are one 64-block.
+      constexpr bool kBlock64 = kLayout == kLayoutNf4Dq64;
+      const int spr = kBlock64 ? 2 * groups_per_row : groups_per_row;
+      const int gsc = tile_valid ? (kBlock64 ? kb / 64 + khalf : kb / 128) : 0;
       // The row's scale for the next stage this group owns is loaded one owned
       // stage ahead (stages 2g, 2g+1, 2g+2*kGroups, ...).
       auto load_scale = [&](int it) {
         return (tile_valid && it < n_main)
-                   ? __ldg(args.scales + static_cast<size_t>(wrow0 + it * kStageN + r) * groups_per_row + gsc)
+                   ? __ldg(args.scales + static_cast<size_t>(wrow0 + it * kStageN + r) * spr + gsc)
                    : 0.0f;
       };
       float next_scale = load_scale(2 * grp);
@@ -329,14 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + r * 64 + khalf * 32);
               const uint4 q0 = q[0], q1 = q[1];
-              lookup8(table, q0.x, v + 0);
-              lookup8(table, q0.y, v + 4);
-              lookup8(table, q0.z, v + 8);
-              lookup8(table, q0.w, v + 12);
-              lookup8(table, q1.x, v + 16);
-              lookup8(table, q1.y, v + 20);
-              lookup8(table, q1.z, v + 24);
-              lookup8(table, q1.w, v + 28);
+              lookup8_l<kLayout>(table, q0.x, v + 0);
+              lookup8_l<kLayout>(table, q0.y, v + 4);
+              lookup8_l<kLayout>(table, q0.z, v + 8);
+              lookup8_l<kLayout>(table, q0.w, v + 12);
+              lookup8_l<kLayout>(table, q1.x, v + 16);
+              lookup8_l<kLayout>(table, q1.y, v + 20);
+              lookup8_l<kLayout>(table, q1.z, v + 24);
+              lookup8_l<kLayout>(table, q1.w, v + 28);
             } else {
               // LoRA stage: row r of B is bf16(Alora[r, kb + 64*khalf .. +64]), zero past the rank.
               if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {
@@ -397,8 +402,11 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 // 256 tokens x 256 columns of dX).
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
-                    cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles) {
+                    cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles,
+                    int layout) {
   using namespace bwd;
+  if (layout != kLayoutG128 && layout != kLayoutNf4Dq64) return set_error(FL_ERR_ARG, "bwd gemm: unknown layout");
+  if (layout != kLayoutG128 && tiles) return set_error(FL_ERR_UNSUPPORTED, "grouped launches use layout 0");
   if ((K * 2) % 16 != 0 || N % kStageN != 0 || K % 128 != 0)
     return set_error(FL_ERR_ARG, "bwd gemm: needs N %% 64 == 0 and K %% 128 == 0");
   CUtensorMap tm_dy, tm_us, tm_code;
@@ -430,8 +438,9 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   const int tiles_max = tiles ? max_tiles
                               : ((K + 2 * kColHalf - 1) / (2 * kColHalf)) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf));
   int pairs = 0;
-  if ((rc = resident_pairs(reinterpret_cast<const void*>(&fl_bwd_ss_kernel), kThreads, kSmemBytes, &pairs)))
-    return rc;
+  const void* kfn = layout == kLayoutG128 ? reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutG128>)
+                                          : reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutNf4Dq64>);
+  if ((rc = resident_pairs(kfn, kThreads, kSmemBytes, &pairs))) return rc;
   if (pairs > tiles_max) pairs = tiles_max;
   if (pairs < 1) return FL_OK;
   cudaLaunchConfig_t cfg = {};
@@ -446,7 +455,9 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t le = cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel, tm_dy, tm_us, tm_code, a);
+  cudaError_t le = layout == kLayoutG128
+                       ? cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutG128>, tm_dy, tm_us, tm_code, a)
+                       : cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutNf4Dq64>, tm_dy, tm_us, tm_code, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "bwd gemm launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }

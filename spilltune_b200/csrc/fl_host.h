@@ -19,7 +19,7 @@ uint32_t* status_word(int device);  // device status word of the calling device
 int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
                     const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
-                    int experts = 1, int max_tiles = 0);
+                    int experts = 1, int max_tiles = 0, int layout = 0);
 
 // 2-CTA clusters of `kernel` that can be resident at once on the current
 // device (also raises the kernel's dynamic shared-memory limit to `smem`).
@@ -38,10 +38,13 @@ int moe_max_tiles(int total_rows, int experts, int rows, int col_tiles);
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
-                    int experts = 1, int max_tiles = 0);
+                    int experts = 1, int max_tiles = 0, int layout = 0);
 
 int launch_dequant(const uint8_t* payload, const float* scales, const float* lut, int64_t numel, void* out,
-                   cudaStream_t stream);
+                   cudaStream_t stream, int layout = 0);
+// FP32 block scales of an NF4-DQ64 record (the double-quantization prologue).
+int launch_nf4dq_prologue(const uint8_t* absmax_q, const float* nested_absmax, const float* nested_map, float offset,
+                          int64_t blocks, float* out, cudaStream_t stream);
 
 // out[m, j] = bf16(s * sum_r P[m, r] * Q(j, r)), j < rank, zero for rank <= j < 64.
 // Q(j, r) = q[j * q_sj + r * q_sr] (fp32).  qc_scratch: lora_factor_bytes(R,

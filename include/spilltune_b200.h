@@ -184,6 +184,23 @@ int fl_bwd_nf4dq(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, in
                  float scale, uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace,
                  size_t workspace_bytes, void* stream);
 
+/*
+ * Chunked LM head + shifted cross-entropy, one token chunk per call: the body
+ * of the reference's _ChunkedCE.forward loop (ram_vram_finetune/quantization/
+ * native_terminal.py:20-28; the same loop inline in training/engine.py:58-78).
+ *   h       bf16 [T, H]   normalized hidden states of the chunk's tokens;
+ *   head    bf16 [V, H]   frozen LM head;
+ *   targets int64 [T]     next-token labels, -100 = no loss for that token;
+ *   loss_sum fp32 scalar (device) += sum over targeted tokens of
+ *            logsumexp(logits) - logits[target], logits = bf16(h . head^T);
+ *   dh      bf16 [T, H]   = d(loss / normalization) / dh, inv_norm = 1/normalization.
+ * workspace: >= fl_ce_workspace_bytes(T, V) bytes, 256-byte aligned (holds the
+ * chunk's bf16 logits).  Requires H % 8 == 0, V % 8 == 0.
+ */
+size_t fl_ce_workspace_bytes(int64_t T, int64_t V);
+int fl_ce_chunk(const uint16_t* h, int64_t T, int64_t H, const uint16_t* head, int64_t V, const int64_t* targets,
+                float inv_norm, float* loss_sum, uint16_t* dh, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

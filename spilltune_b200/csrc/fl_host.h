@@ -72,4 +72,9 @@ int launch_smallm_fwd(const void* X, const void* Ts, const uint8_t* codes, const
                       const float* lut, const float* lora, int rank, void* Y, int M, int N, int K,
                       cudaStream_t stream);
 
+// Chunked LM head + cross-entropy (fl_head.cu).
+size_t ce_workspace_bytes(int64_t T, int64_t V);
+int launch_ce_chunk(const void* h, int T, int H, const void* head, int V, const int64_t* targets, float inv_norm,
+                    float* loss_sum, void* dh, void* ws, cudaStream_t stream);
+
 }  // namespace fl

@@ -1,0 +1,76 @@
+"""Chunked LM head + cross-entropy (the reference's terminal, native_terminal.py:11-47).
+
+GPU: loss and hidden-state VJP of ``spilltune_b200.head.chunked_causal_loss``
+against the oracle restatement of ``_ChunkedCE`` (CPU, same bf16 logits, FP32
+CE): loss within 1e-3 relative, VJP within rel-L2 1e-2.  CPU: argument checks.
+"""
+import pytest
+import torch
+
+import oracle.head as oh
+import oracle.linear as ol
+
+
+def _case(Bsz, S, H, V, seed, ignore_frac=0.2):
+    g = torch.Generator().manual_seed(seed)
+    normalized = torch.randn(Bsz, S, H, generator=g).to(torch.bfloat16)
+    head = (torch.randn(V, H, generator=g) * 0.05).to(torch.bfloat16)
+    labels = torch.randint(0, V, (Bsz, S), generator=g)
+    labels[torch.rand(Bsz, S, generator=g) < ignore_frac] = -100
+    return normalized, head, labels
+
+
+def test_argument_checks():
+    from spilltune_b200 import head as hd
+    n, h, l = _case(1, 8, 16, 32, 0)
+    with pytest.raises(ValueError, match="token chunk/normalization"):
+        hd._ChunkedCE.forward(None, n, h, l, 0.0, 4, ((0, 4),))
+    with pytest.raises(ValueError, match="labels/trainable"):
+        hd._ChunkedCE.forward(None, n, h, l[:, :4], 1.0, 4, ((0, 4),))
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        hd.chunked_causal_loss(n, h, l, normalization=1.0, token_chunk=4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("Bsz,S,H,V,chunk", [(2, 64, 256, 1000, 32), (1, 300, 512, 4096, 128),
+                                             (2, 129, 128, 2048, 64)])
+def test_matches_reference_chunked_ce(cuda_lib, Bsz, S, H, V, chunk):
+    from spilltune_b200 import head as hd
+    normalized, head, labels = _case(Bsz, S, H, V, S + V)
+    norm = float((labels[:, 1:] != -100).sum())
+    chunks = tuple((s, min(s + chunk, S - 1)) for s in range(0, S - 1, chunk)
+                   if bool((labels[:, s + 1:min(s + chunk, S - 1) + 1] != -100).any()))
+    ref_loss, ref_vjp = oh.chunked_ce(normalized, head, labels, norm, chunks)
+    x = normalized.cuda().requires_grad_(True)
+    loss = hd.chunked_causal_loss(x, head.cuda(), labels.cuda(), normalization=norm, token_chunk=chunk,
+                                  supervised_chunks=chunks)
+    (vjp,) = torch.autograd.grad(loss, (x,))
+    assert abs(float(loss) - float(ref_loss)) <= 1e-3 * abs(float(ref_loss))
+    assert ol.rel_l2(vjp.cpu(), ref_vjp) <= 1e-2
+
+
+@pytest.mark.gpu
+def test_llama3_head_shape_chunk(cuda_lib):
+    """One 256-token chunk at the Llama-3-8B head shape (V=128256, H=4096):
+    loss and sampled gradient rows against an FP32 evaluation of the same
+    bf16 logits (computed with torch on the GPU as the checker)."""
+    from spilltune_b200 import head as hd
+    T, H, V = 256, 4096, 128256
+    g = torch.Generator().manual_seed(7)
+    h = torch.randn(T, H, generator=g).to(torch.bfloat16).cuda()
+    head = (torch.randn(V, H, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    tg = torch.randint(0, V, (T,), generator=g)
+    tg[::7] = -100
+    tg = tg.cuda()
+    loss = torch.zeros((), dtype=torch.float32, device="cuda")
+    dh = hd.ce_chunk(h, head, tg, 1.0, loss)
+    logits = (h.float() @ head.float().t()).to(torch.bfloat16).float()
+    keep = tg != -100
+    ref_loss = float((torch.logsumexp(logits[keep], -1) - logits[keep, tg[keep]]).sum())
+    assert abs(float(loss) - ref_loss) <= 1e-3 * abs(ref_loss)
+    rows = torch.tensor([0, 1, 100, 255], device="cuda")
+    p = torch.softmax(logits[rows], dim=-1)
+    p[torch.arange(4, device="cuda"), tg[rows].clamp_min(0)] -= 1.0
+    p[~keep[rows]] = 0
+    ref_dh = p.to(torch.bfloat16).float() @ head.float()
+    assert ol.rel_l2(dh[rows].cpu(), ref_dh.cpu()) <= 1e-2

@@ -74,9 +74,10 @@ size_t fl_fwd_workspace_bytes(int64_t M, int64_t K, int rank);
  * (ram_vram_finetune/quantization/nf4_backend_cuda.py:888-917).
  * rank = 0 computes the plain frozen F.linear (dense.py:122-124 without LoRA).
  * M <= 16 with K % 512 == 0 runs a decode-step kernel bound by the weight bytes; it factors each
- * 128-wide scale group out of its dot product, so its operand is bf16(lut16[c])
- * (exact for int4-sym, the bf16-rounded codebook for NF4) and the scale
- * multiplies the FP32 partial sum.
+ * scale group out of its dot product, so its operand is bf16(lut16[c]) (exact
+ * for int4-sym, the bf16-rounded codebook for NF4) and the scale multiplies
+ * the FP32 partial sum; the LoRA term is added in FP32 from the bf16
+ * Ts = bf16(scale * X . A^T).
  * Requires K % 128 == 0, rank <= 64, 16-byte aligned pointers, bias-free
  * projections.  workspace: >= fl_fwd_workspace_bytes(M, K, rank) bytes,
  * 16-byte aligned (may be NULL when rank == 0).

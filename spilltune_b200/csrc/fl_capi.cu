@@ -126,15 +126,19 @@ static int fwd_impl(const char* who, int layout, const uint16_t* X, int64_t M, i
   uint32_t* status = nullptr;
   if ((rc = current_status(&status))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* qc = rank > 0 ? static_cast<uint8_t*>(workspace) + static_cast<size_t>(M) * 128 : nullptr;
+  // Decode-like steps (M <= 16) are bound by the weight bytes: dedicated kernel
+  // (it streams 512-wide column chunks; other K take the tile GEMM).  Its LoRA
+  // partial sums use the converted-factor scratch (M * 64 * K/128 floats fit).
+  if (layout == kLayoutG128 && M <= 16 && K % 512 == 0) {
+    float* parts = static_cast<float*>(qc);
+    if (rank > 0 && (rc = launch_lora_parts(X, (int)M, (int)K, A, K, rank, parts, st))) return rc;
+    return launch_smallm_fwd(X, parts, scale, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st, layout);
+  }
   if (rank > 0) {
-    void* qc = static_cast<uint8_t*>(workspace) + static_cast<size_t>(M) * 128;
     rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, workspace, qc, st);
     if (rc) return rc;
   }
-  // Decode-like steps (M <= 16) are bound by the weight bytes: dedicated kernel
-  // (it streams 512-wide column chunks; other K take the tile GEMM).
-  if (layout == kLayoutG128 && M <= 16 && K % 512 == 0)
-    return launch_smallm_fwd(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st);
   return launch_fwd_gemm(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st,
                          nullptr, nullptr, 1, 0, layout);
 }

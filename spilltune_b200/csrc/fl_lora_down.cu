@@ -342,6 +342,197 @@ static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64
 
 }  // namespace ld
 
+// Small-M form (at most 16 rows of P, rows of Q contiguous along r): the work
+// is a few MFLOP, so the kernel is built for latency.  Block y takes the ranks
+// j = 8y + w (one per warp w); a warp's lanes take four consecutive r of
+// every 128-wide piece of the CTA's slice of the reduction and keep one exact
+// FP32 sum per row of P.  The CTAs of a cluster split the reduction; CTA 0
+// adds their sums in rank order.  The kernel first lets the next launch of the
+// stream start (programmatic dependent launch): the small-M frozen projection
+// streams its weights meanwhile and reads Lo only once this grid completed.
+namespace lds {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxRows = 16;
+constexpr int kMaxSplit = 8;
+
+__global__ void __launch_bounds__(kThreads)
+    lora_down_small_kernel(const __nv_bfloat16* __restrict__ P, int M, int R, const float* __restrict__ q,
+                           int64_t q_sj, int rank, float s, __nv_bfloat16* __restrict__ out, int split) {
+  griddep_launch_dependents();
+  __shared__ float part[kWarps * kMaxRows];  // [warp][m]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cr = split > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int pieces = R / 128;
+  const int p0 = cr * pieces / split, p1 = (cr + 1) * pieces / split;
+  const int j = blockIdx.y * kWarps + warp;
+  float acc[kMaxRows];
+#pragma unroll
+  for (int m = 0; m < kMaxRows; ++m) acc[m] = 0.f;
+  if (j < rank) {
+    const float* qrow = q + j * q_sj;
+    for (int p = p0; p < p1; ++p) {
+      const int r = p * 128 + lane * 4;
+      const float4 qv = __ldg(reinterpret_cast<const float4*>(qrow + r));
+#pragma unroll
+      for (int m = 0; m < kMaxRows; ++m) {
+        if (m < M) {
+          const uint2 xv = __ldg(reinterpret_cast<const uint2*>(P + static_cast<size_t>(m) * R + r));
+          acc[m] = fmaf(__uint_as_float(xv.x << 16), qv.x, acc[m]);
+          acc[m] = fmaf(__uint_as_float(xv.x & 0xFFFF0000u), qv.y, acc[m]);
+          acc[m] = fmaf(__uint_as_float(xv.y << 16), qv.z, acc[m]);
+          acc[m] = fmaf(__uint_as_float(xv.y & 0xFFFF0000u), qv.w, acc[m]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kMaxRows; ++m)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+  if (lane < kMaxRows) {
+    float v = 0.f;
+#pragma unroll
+    for (int m = 0; m < kMaxRows; ++m) v = lane == m ? acc[m] : v;
+    part[warp * kMaxRows + lane] = v;
+  }
+  __syncthreads();
+  if (split > 1) cluster_sync();
+  if (cr == 0) {
+    const uint32_t local = smem_u32(part);
+    // This block's ranks; block 0 also writes the zero columns [rank, 64).
+    const int j0 = blockIdx.y * kWarps;
+    const int j_end = blockIdx.y == 0 ? 64 : min(j0 + kWarps, rank);
+    const int width = j_end - j0;
+    for (int idx = threadIdx.x; idx < M * width; idx += kThreads) {
+      const int m = idx / width, jj = j0 + idx % width;
+      float v = 0.f;
+      if (jj < rank && jj < j0 + kWarps) {
+        const int off = (jj - j0) * kMaxRows + m;
+        for (int c = 0; c < split; ++c)
+          v += c == 0 ? part[off]
+                      : __uint_as_float(ld_shared_cluster_u32(mapa_shared(local, static_cast<uint32_t>(c)) +
+                                                              static_cast<uint32_t>(off) * 4));
+        v *= s;
+      }
+      if (jj >= rank || jj < j0 + kWarps) out[static_cast<size_t>(m) * 64 + jj] = __float2bfloat16_rn(v);
+    }
+  }
+  if (split > 1) cluster_sync();  // peers' sums stay valid until CTA 0 has read them
+}
+
+static int launch(const void* P, int M, int R, const float* q, int64_t q_sj, int rank, float s, void* out,
+                  cudaStream_t stream) {
+  int split = 1;
+  while (split < kMaxSplit && (R / 128) >= 2 * split) split *= 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(split, (rank + kWarps - 1) / kWarps);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t le = cudaLaunchKernelEx(&cfg, lora_down_small_kernel, static_cast<const __nv_bfloat16*>(P), M, R, q,
+                                      q_sj, rank, s, static_cast<__nv_bfloat16*>(out), split);
+  if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down (small M) launch: %s", cudaGetErrorString(le));
+  return FL_OK;
+}
+
+
+// Partial form for the small-M forward: CTA p takes the 128-wide piece p of the
+// reduction (exact FP32 sums in shared memory); the clusters of lora_parts_per_cluster(R)
+// CTAs add their pieces in rank order through distributed shared memory, and
+// cluster c writes parts[m][j][c] (j < rank; the partials of one output
+// contiguous) for the consumer to add in order.  One piece per CTA keeps every
+// CTA to a single round of loads, so the kernel finishes early even while the
+// frozen projection that follows (programmatic dependent launch) streams its
+// weights on the same SMs.
+__global__ void __launch_bounds__(kThreads)
+    lora_parts_kernel(const __nv_bfloat16* __restrict__ P, int M, int R, const float* __restrict__ q,
+                      int64_t q_sj, int rank, float* __restrict__ parts, int csize) {
+  griddep_launch_dependents();
+  __shared__ float mine[kMaxRows * 64];  // [m][j] of this CTA's piece
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 128 + lane * 4;
+  uint2 xv[kMaxRows];
+#pragma unroll
+  for (int m = 0; m < kMaxRows; ++m)
+    xv[m] = m < M ? __ldg(reinterpret_cast<const uint2*>(P + static_cast<size_t>(m) * R + r)) : make_uint2(0, 0);
+  for (int j = warp; j < rank; j += kWarps) {
+    const float4 qv = __ldg(reinterpret_cast<const float4*>(q + j * q_sj + r));
+    float acc[kMaxRows];
+#pragma unroll
+    for (int m = 0; m < kMaxRows; ++m) {
+      float a = __uint_as_float(xv[m].x << 16) * qv.x;
+      a = fmaf(__uint_as_float(xv[m].x & 0xFFFF0000u), qv.y, a);
+      a = fmaf(__uint_as_float(xv[m].y << 16), qv.z, a);
+      acc[m] = fmaf(__uint_as_float(xv[m].y & 0xFFFF0000u), qv.w, a);
+    }
+#pragma unroll
+    for (int m = 0; m < kMaxRows; ++m)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+    float v = 0.f;
+#pragma unroll
+    for (int m = 0; m < kMaxRows; ++m) v = lane == m ? acc[m] : v;
+    if (lane < kMaxRows) mine[lane * 64 + j] = v;
+  }
+  cluster_sync();
+  const int crank = static_cast<int>(cluster_ctarank());
+  if (crank == 0) {
+    const int n_cl = gridDim.x / csize;
+    const int cl = blockIdx.x / csize;
+    const uint32_t local = smem_u32(mine);
+    for (int idx = threadIdx.x; idx < M * rank; idx += kThreads) {
+      const int m = idx / rank, j = idx % rank;
+      const uint32_t off = static_cast<uint32_t>(m * 64 + j) * 4;
+      float v = mine[m * 64 + j];
+      for (int c = 1; c < csize; ++c)
+        v += __uint_as_float(ld_shared_cluster_u32(mapa_shared(local, static_cast<uint32_t>(c)) + off));
+      parts[(static_cast<size_t>(m) * 64 + j) * n_cl + cl] = v;
+    }
+  }
+  cluster_sync();  // peers' sums stay valid until rank 0 has read them
+}
+
+}  // namespace lds
+
+int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj, int rank, float* parts,
+                      cudaStream_t stream) {
+  if (R % 128 != 0 || M < 1 || M > lds::kMaxRows || rank < 1 || rank > 64)
+    return set_error(FL_ERR_ARG, "lora_parts: needs R %% 128 == 0, 1 <= M <= 16, 1 <= rank <= 64");
+  if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(parts)) & 15u ||
+      q_sj % 4 != 0)
+    return set_error(FL_ERR_ARG, "lora_parts: activations, factor and partials must be 16-byte aligned");
+  const int csize = lora_parts_per_cluster(R);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(R / 128);
+  cfg.blockDim = dim3(lds::kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lds::lora_parts_kernel, static_cast<const __nv_bfloat16*>(P), M, R, q, q_sj,
+                                     rank, parts, csize);
+  if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_parts launch: %s", cudaGetErrorString(e));
+  return FL_OK;
+}
+
+int lora_parts_per_cluster(int R) {
+  const int pieces = R / 128;
+  return pieces % 8 == 0 ? 8 : pieces % 4 == 0 ? 4 : pieces % 2 == 0 ? 2 : 1;
+}
+
 int lora_nq(int rank) { return rank <= 16 ? 16 : rank <= 32 ? 32 : 64; }
 
 size_t lora_factor_bytes(int64_t R, int rank) { return 4u * static_cast<size_t>(lora_nq(rank)) * R; }
@@ -354,6 +545,9 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
   if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(out64) |
        reinterpret_cast<uintptr_t>(qc_scratch)) & 15u)
     return set_error(FL_ERR_ARG, "lora_down: activations, output and scratch must be 16-byte aligned");
+  if (tiles == nullptr && M <= lds::kMaxRows && q_sr == 1 && q_sj % 4 == 0 &&
+      (reinterpret_cast<uintptr_t>(q) & 15u) == 0)
+    return lds::launch(P, M, R, q, q_sj, rank, s, out64, stream);
   const int nq = lora_nq(rank);
   auto qc = static_cast<__nv_bfloat16*>(qc_scratch);
   {

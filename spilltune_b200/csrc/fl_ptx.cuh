@@ -437,6 +437,13 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// 32-bit load from this CTA's shared memory at a shared-window address.
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
 // Instruction descriptor, kind::f16 with bf16 A/B, fp32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
   return (1u << 4)                                   // D format f32
@@ -481,6 +488,15 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
   return d;
 }
+
+// Programmatic dependent launch: the next kernel of the stream, launched with
+// programmatic stream serialization, may start before this grid completes.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Wait until the grids this one depends on programmatically have completed and
+// their memory operations are visible (returns at once when there is none).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31) == 0; }
 

@@ -7,26 +7,33 @@
 // stored code for int4-sym (c - 8), the bf16-rounded codebook for NF4 — and the
 // scale multiplies the fp32 partial sum of its group.
 //
-// At M <= 16 every weight byte is used once and a whole projection is only a
-// few MB, so the kernel is bound by how fast the packed weights can be put in
-// flight: each CTA owns 16*tpc weight rows over the whole reduction (or one
+// At M <= 16 every weight byte is used once: the kernel has to decode the
+// packed weights as fast as a single launch can stream them (a TMA stream of a
+// 30 MB projection reaches ~3.5 TB/s on B200 including the ramp).  Decode is a
+// per-lane copy of a 256-entry shared-memory table mapping a payload byte to
+// the bf16 pair of its two codes: two integer ops and one conflict-free 32-bit
+// shared load per two weights.  (The prmt product table of fl_codebook.cuh
+// costs ~21 integer ops per eight weights at the integer pipe's half rate;
+// measured, table lookups for every word were faster than any mix.)
+//
+// Layout: a CTA owns 32*TW weight rows over the whole reduction (or one
 // cluster slice of it) and, before anything else, queues TMA loads of its
 // first `slots` 512-column chunks (codes with the 128-byte swizzle, plus the
-// chunk's scales) into a ring of shared-memory slots; the grid is one wave of
-// several small CTAs per SM, so decode latency is hidden by other warps.
-// Decode: the 16 operand values bf16(lut[c]) sit in registers as a low-byte
-// and a high-byte plane (the product table of fl_codebook.cuh with scale 1),
-// and prmt looks up eight codes of a payload word at a time — no table to
-// build in shared memory, no shared-memory lookups.  Four
-// warps each take one 128-wide scale group of every chunk; the MMAs are
-// warp-level (mma.sync m16n8k16) with 16 weight rows as A and the tokens as
-// the 8-wide N dimension, X fragments read from global (L2) one chunk ahead.
-// The reduction-split CTAs of a cluster add their partial sums through
-// distributed shared memory; rank 0 adds the LoRA term and writes Y.
+// chunk's scales) into a ring of shared-memory slots.  Eight warps: warp w takes
+// the 128-wide scale group w % 4 of every chunk for the TW 16-row tiles of half
+// w / 4.  The MMAs are warp-level (mma.sync m16n8k16) with 16 weight rows as A
+// and the tokens as the 8-wide N dimension; the chunk's activations arrive in
+// the same slot (TMA, 128-byte swizzle, token rows past M zero-filled).  The reduction-split CTAs of a cluster add
+// their partial sums through distributed shared memory; rank 0 adds the LoRA
+// term (fp32 Blora x bf16 Ts) and writes Y.
+//
+// Ts = bf16(s * X . A^T) is summed here, in a fixed order, from the few FP32
+// partial sums that the small-M low-rank kernel launched just before
+// (fl_lora_down.cu) writes; that kernel lets this grid start while it runs
+// (programmatic dependent launch), and only the final reduction waits for it.
 #include <cuda_bf16.h>
 #include <cstdint>
 
-#include "fl_codebook.cuh"
 #include "fl_host.h"
 #include "fl_ptx.cuh"
 
@@ -37,12 +44,16 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 
 namespace sm {
 
-constexpr int kWarps = 4;                        // one per 128-wide group of a chunk
-constexpr int kThreads = 32 * kWarps;
+constexpr int kGroups = 4;                       // 128-wide scale groups per chunk
+constexpr int kWarps = 2 * kGroups;              // consumer warps: group x tile half
+constexpr int kThreads = 32 * (kWarps + 1);      // + one TMA producer warp
 constexpr int kChunkK = 512;                     // reduction columns per ring slot
-constexpr int kMaxTpc = 8;                       // 16-row tiles per CTA
-constexpr int kCtasPerSm = 3;                    // grid = one wave at this many CTAs per SM (registers allow 3)
-constexpr int kSlotBudget = 40 * 1024;           // ring bytes per CTA
+constexpr int kTableBytes = 256 * 32 * 4;        // [byte][lane] bf16 pairs
+constexpr int kTilesPerWarp = 2;                 // 16-row tiles per warp: 64 rows per CTA
+// After the main loop the table's space holds Ts [16][65] (rows padded so the
+// 16 tokens of a warp's reads fall in different banks) and Blora rows [rows][64] (fp32).
+constexpr int kTsStride = 65;
+static_assert((16 * kTsStride + 32 * kTilesPerWarp * 64) * 4 <= kTableBytes, "epilogue staging");
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -59,41 +70,58 @@ __device__ __forceinline__ uint32_t word4(const uint4& q, int w) {
 
 struct Args {
   const __nv_bfloat16* X;   // [M, K]
-  const __nv_bfloat16* Ts;  // [M, 64] scaled low-rank activations (rank > 0)
+  const float* parts;       // [M][64][n_parts] low-rank partial sums (rank > 0)
+  int n_parts;
+  float s;                  // LoRA scale
   const float* lut;         // [16]
   const float* blora;       // [N, rank]
   __nv_bfloat16* Y;         // [M, N]
   uint32_t* status;
   int M, N, K, rank;
-  int tpc;                  // 16-row tiles per CTA
   int split;                // CTAs of a cluster along the reduction
   int slots;                // ring depth
 };
 
 // Slot layout: codes box 0 (columns 0..255 of the chunk) [rows][128 B],
-// codes box 1 (256..511), scales [rows][4 fp32].
-__host__ __device__ constexpr int slot_bytes(int rows) { return rows * 128 * 2 + rows * 16; }
+// codes box 1 (256..511), eight activation boxes (64 columns each)
+// [8 NT tokens][128 B], all with the 128-byte swizzle, then scales [rows][4 fp32].
+__host__ __device__ constexpr int x_box_bytes(int nt) { return 8 * nt * 128; }
+__host__ __device__ constexpr int slot_bytes(int rows, int nt) {
+  return rows * 128 * 2 + 8 * x_box_bytes(nt) + rows * 16;
+}
+__host__ __device__ constexpr int slot_stride(int rows, int nt) { return (slot_bytes(rows, nt) + 1023) / 1024 * 1024; }
+// Dynamic shared memory: ring | table | partial sums [group][rows][16] | full and empty mbarriers + abort word.
+__host__ __device__ constexpr int smem_bytes(int rows, int nt, int slots) {
+  return 1024 + slots * slot_stride(rows, nt) + kTableBytes + kGroups * rows * 16 * 4 + 2 * slots * 8 + 16;
+}
 
-// NT: 8-token tiles, 1 (M <= 8) or 2 (M <= 16).  TPC: 16-row tiles per CTA,
-// unrolled so the MMA chains of different tiles interleave; with few tiles
-// the k-steps alternate between two partial sums (PS = 2) for the same reason.
-template <int NT, int TPC>
-__global__ void __launch_bounds__(kThreads)
+// NT: 8-token tiles, 1 (M <= 8) or 2 (M <= 16).  TW: 16-row tiles per warp,
+// unrolled so the MMA chains of different tiles interleave; with one tile and
+// one token tile the k-steps alternate between two partial sums (PS = 2).
+template <int NT, int TW>
+__global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
     smallm_kernel(const __grid_constant__ CUtensorMap tm_codes,   // [N, K/2] u8, box {128, rows}, 128B swizzle
+                  const __grid_constant__ CUtensorMap tm_x,       // [M, K] bf16, box {64, 8 NT}, 128B swizzle
                   const __grid_constant__ CUtensorMap tm_scales,  // [N, K/128] fp32, box {4, rows}
                   const Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int PS = TPC * NT <= 2 ? 2 : 1;
-  const int rows = 16 * TPC;
-  const int sbytes = (slot_bytes(rows) + 1023) / 1024 * 1024;
-  uint8_t* ring = smem;                                                // slots x sbytes
-  float* red = reinterpret_cast<float*>(smem + args.slots * sbytes);   // [kWarps][rows][16]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + kWarps * rows * 16);         // [slots], then the abort word
-  volatile uint32_t* abort_word = reinterpret_cast<volatile uint32_t*>(full + args.slots);
+  constexpr int PS = TW * NT <= 1 ? 2 : 1;
+  constexpr int rows = 32 * TW;
+  constexpr int sbytes = slot_stride(rows, NT);
+  constexpr int kXOff = rows * 256;                    // activation boxes within a slot
+  constexpr int kSOff = kXOff + 8 * x_box_bytes(NT);   // scales within a slot
+  uint8_t* ring = smem;                                                    // slots x sbytes
+  uint8_t* table = smem + args.slots * sbytes;                             // [256][32] u32
+  float* red = reinterpret_cast<float*>(table + kTableBytes);              // [group][rows][16]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + kGroups * rows * 16);  // [slots]: TMA bytes landed
+  uint64_t* empty = full + args.slots;                                      // [slots]: every consumer warp done
+  volatile uint32_t* abort_word = reinterpret_cast<volatile uint32_t*>(empty + args.slots);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c4 = lane & 3;
+  const int grp = warp & (kGroups - 1);  // scale group of every chunk
+  const int half = warp / kGroups;       // tiles [half * TW, half * TW + TW) of the CTA
   const int split = args.split;
   const int kslice = split > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   const int n0 = (blockIdx.x / split) * rows;
@@ -108,100 +136,136 @@ __global__ void __launch_bounds__(kThreads)
 
   // Queue the first loads before any other work.
   if (threadIdx.x == 0) {
-    for (int i = 0; i < args.slots; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < args.slots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kWarps);
+    }
     *abort_word = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tm_codes);
+    tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_scales);
   }
   auto issue = [&](int k) {  // chunk c_begin + k into slot k % slots (thread 0)
     const int sl = k % args.slots;
     uint8_t* dst = ring + sl * sbytes;
     const int c = chunk_of(k);
-    mbar_arrive_expect_tx(&full[sl], slot_bytes(rows));
+    mbar_arrive_expect_tx(&full[sl], slot_bytes(rows, NT));
     tma_load_2d(dst, &tm_codes, c * (kChunkK / 2), n0, &full[sl]);
     tma_load_2d(dst + rows * 128, &tm_codes, c * (kChunkK / 2) + 128, n0, &full[sl]);
-    tma_load_2d(dst + rows * 256, &tm_scales, c * 4, n0, &full[sl]);
-  };
-  int issued = 0;  // meaningful in thread 0 only
-  if (threadIdx.x == 0)
-    for (; issued < args.slots && issued < n_ch; ++issued) issue(issued);
-  // Operand table bf16(lut[c]) in registers.
-  const ProductTable table = make_table(args.lut, 1.0f);
-  __syncthreads();
-
-  float acc[TPC][NT][4];
 #pragma unroll
-  for (int t = 0; t < TPC; ++t)
+    for (int b = 0; b < 8; ++b) tma_load_2d(dst + kXOff + b * x_box_bytes(NT), &tm_x, c * kChunkK + 64 * b, 0, &full[sl]);
+    tma_load_2d(dst + kSOff, &tm_scales, c * 4, n0, &full[sl]);
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < args.slots && i < n_ch; ++i) issue(i);
+  // Per-lane byte table: entry e of lane l at table + 128 e + 4 l holds the
+  // bf16 pair {lut[e & 15], lut[e >> 4]}.  Lane l of warp w builds entry
+  // 32 w + l, then the warp writes its 32 entries, one copy per lane.
+  if (warp < kWarps) {
+    const float mine = __ldg(args.lut + (lane & 15));
+    const int e = 32 * warp + lane;
+    const uint32_t packed =
+        pack_bf16x2(__shfl_sync(0xffffffffu, mine, e & 15), __shfl_sync(0xffffffffu, mine, e >> 4));
+    uint32_t* tw = reinterpret_cast<uint32_t*>(table) + 32 * warp * 32 + lane;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) tw[j * 32] = __shfl_sync(0xffffffffu, packed, j);
+  }
+  __syncthreads();
+  const uint32_t tab = smem_u32(table) + static_cast<uint32_t>(lane) * 4;
+  // Byte b of payload word w -> the pair of elements 2b, 2b + 1.
+  auto decode = [&](uint32_t w, uint32_t* out) {
+    out[0] = lds_u32(tab + ((w << 7) & 0x7F80u));
+    out[1] = lds_u32(tab + ((w >> 1) & 0x7F80u));
+    out[2] = lds_u32(tab + ((w >> 9) & 0x7F80u));
+    out[3] = lds_u32(tab + ((w >> 17) & 0x7F80u));
+  };
+
+  float acc[TW][NT][4];
+#pragma unroll
+  for (int t = 0; t < TW; ++t)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[t][nt][0] = acc[t][nt][1] = acc[t][nt][2] = acc[t][nt][3] = 0.f;
 
-  // X fragments of chunk c for this warp's group: tokens g (+8), columns
-  // 512c + 128*warp + 32*c4 + [0, 32) — 64 contiguous bytes per token.
-  auto load_x = [&](int c, uint4 (&xv)[NT][4]) {
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int tok = 8 * nt + g;
-      const uint4* src = reinterpret_cast<const uint4*>(args.X + static_cast<size_t>(tok < args.M ? tok : 0) * args.K +
-                                                        c * kChunkK + 128 * warp + 32 * c4);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) xv[nt][i] = tok < args.M ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
-    }
-  };
+  // X of this warp's group for tokens 8 nt + g: chunk columns 128 grp + 32 c4 + 8 w + [0, 8)
+  // sit in activation box 2 grp + c4 / 2, 16-byte chunk (4 (c4 % 2) + w) ^ g of the token's row.
+  const int xbox = kXOff + (2 * grp + (c4 >> 1)) * x_box_bytes(NT) + g * 128;
 
-  // One chunk: wait for its slot, decode + MMA this warp's group for every
-  // tile, then (all warps past the slot) refill it.  Every warp passes the
-  // same __syncthreads whether or not a wait gave up.
+  // Consumer warps: wait for a slot, decode + MMA this warp's group of its
+  // tiles, release the slot; the producer warp refills each slot once all
+  // eight consumers released it (no CTA-wide barrier per chunk).
   bool ok = true;
-  auto chunk = [&](int k, const uint4 (&xv)[NT][4]) {
+  if (warp == kWarps) {
+    if (lane == 0) {
+      int k = args.slots;
+      for (; k < n_ch; ++k) {
+        const int sl = k % args.slots;
+        if (!mbar_wait(&empty[sl], ((k / args.slots) - 1) & 1, abort_word, args.status, kStatusTimeoutEmpty)) break;
+        fence_proxy_async_smem();  // the consumers' generic reads before the async-proxy refill
+        issue(k);
+      }
+      // Never leave the CTA with bulk copies still landing in its shared memory.
+      const int issued = k < n_ch ? k : n_ch;
+      for (int i = issued > args.slots ? issued - args.slots : 0; i < issued; ++i) {
+        uint32_t dummy = 0;
+        mbar_wait(&full[i % args.slots], (i / args.slots) & 1, &dummy, args.status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+  for (int k = 0; k < n_ch && ok; ++k) {
     const int sl = k % args.slots;
-    if (ok && !mbar_wait_short_warp(&full[sl], (k / args.slots) & 1, abort_word, args.status, kStatusTimeoutFull))
+    if (!mbar_wait_warp(&full[sl], (k / args.slots) & 1, abort_word, args.status, kStatusTimeoutFull)) {
       ok = false;
-    if (ok) {
+      break;
+    }
+    {
       const uint8_t* slot = ring + sl * sbytes;
-      const uint8_t* cbox = slot + (warp >> 1) * rows * 128;  // this warp's group sits in box warp/2
-      const int j = (warp & 1) * 4 + c4;                       // 16-byte chunk of the row in that box
-      const float* scl = reinterpret_cast<const float*>(slot + rows * 256);
-      uint4 q[TPC][2];
+      const uint8_t* cbox = slot + (grp >> 1) * rows * 128;  // this warp's group sits in box grp/2
+      const int j = (grp & 1) * 4 + c4;                       // 16-byte chunk of the row in that box
+      const float* scl = reinterpret_cast<const float*>(slot + kSOff);
+      uint4 q[TW][2];
 #pragma unroll
-      for (int t = 0; t < TPC; ++t)
+      for (int t = 0; t < TW; ++t)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int r = 16 * t + g + 8 * h;
+          const int r = 16 * (half * TW + t) + g + 8 * h;
           q[t][h] = *reinterpret_cast<const uint4*>(cbox + r * 128 + ((j ^ (r & 7)) << 4));
         }
-      float part[PS][TPC][NT][4];
+      float part[PS][TW][NT][4];
 #pragma unroll
       for (int p = 0; p < PS; ++p)
 #pragma unroll
-        for (int t = 0; t < TPC; ++t)
+        for (int t = 0; t < TW; ++t)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) part[p][t][nt][0] = part[p][t][nt][1] = part[p][t][nt][2] = part[p][t][nt][3] = 0.f;
       // Payload word w of the thread's 16 bytes holds columns 32c4 + 8w + [0, 8);
       // MMA k-step kk = 2w + s uses its pairs 2s (columns +4s+{0,1}) and 2s+1 (+{2,3}).
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
+        uint4 xq[NT];
 #pragma unroll
-        for (int t = 0; t < TPC; ++t) {
+        for (int nt = 0; nt < NT; ++nt)
+          xq[nt] = *reinterpret_cast<const uint4*>(slot + xbox + nt * 8 * 128 + (((4 * (c4 & 1) + w) ^ g) << 4));
+#pragma unroll
+        for (int t = 0; t < TW; ++t) {
           uint32_t e0[4], e1[4];  // rows g and g + 8
-          lookup8(table, word4(q[t][0], w), e0);
-          lookup8(table, word4(q[t][1], w), e1);
+          decode(word4(q[t][0], w), e0);
+          decode(word4(q[t][1], w), e1);
 #pragma unroll
           for (int sub = 0; sub < 2; ++sub) {
             const int kk = 2 * w + sub;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              const uint4& xq = xv[nt][w];
-              const uint32_t b0 = sub ? xq.z : xq.x, b1 = sub ? xq.w : xq.y;
+              const uint32_t b0 = sub ? xq[nt].z : xq[nt].x, b1 = sub ? xq[nt].w : xq[nt].y;
               mma16816(part[kk % PS][t][nt], e0[2 * sub], e1[2 * sub], e0[2 * sub + 1], e1[2 * sub + 1], b0, b1);
             }
           }
         }
       }
 #pragma unroll
-      for (int t = 0; t < TPC; ++t) {
-        const int r0 = 16 * t + g, r1 = r0 + 8;
-        const float s0 = scl[r0 * 4 + warp], s1 = scl[r1 * 4 + warp];
+      for (int t = 0; t < TW; ++t) {
+        const int r0 = 16 * (half * TW + t) + g, r1 = r0 + 8;
+        const float s0 = scl[r0 * 4 + grp], s1 = scl[r1 * 4 + grp];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           float v[4];
@@ -214,45 +278,25 @@ __global__ void __launch_bounds__(kThreads)
         }
       }
     }
-    __syncthreads();
-    if (threadIdx.x == 0 && issued < n_ch && !*abort_word) {
-      fence_proxy_async_smem();  // the slot's generic reads before the async-proxy refill
-      issue(issued);
-      ++issued;
-    }
-  };
-  uint4 xa[NT][4], xb[NT][4];
-  if (n_ch > 0) load_x(chunk_of(0), xa);
-  for (int k = 0; k < n_ch; k += 2) {
-    if (k + 1 < n_ch) load_x(chunk_of(k + 1), xb);
-    chunk(k, xa);
-    if (k + 1 < n_ch) {
-      if (k + 2 < n_ch) load_x(chunk_of(k + 2), xa);
-      chunk(k + 1, xb);
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[sl]);
   }
-  // After an abort, loads already queued may still land: wait for them
-  // (bounded) before the shared memory is released.
-  if (threadIdx.x == 0 && *abort_word) {
-    for (int k = issued > args.slots ? issued - args.slots : 0; k < issued; ++k) {
-      uint32_t dummy = 0;
-      mbar_wait_short(&full[k % args.slots], (k / args.slots) & 1, &dummy, args.status, kStatusTimeoutDrain);
-    }
   }
 
   // ------------------------------------------------------------ reductions
-  // Warp partials -> red[warp][row][token]; accumulator element i of tile t:
-  // row 16t + g + 8*(i >> 1), token 8*nt + 2*c4 + (i & 1).
+  // Warp partials -> red[group][row][token]; accumulator element i of tile t:
+  // row 16 (half TW + t) + g + 8*(i >> 1), token 8*nt + 2*c4 + (i & 1).
+  if (warp < kWarps)
 #pragma unroll
-  for (int t = 0; t < TPC; ++t) {
+  for (int t = 0; t < TW; ++t) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        red[(warp * rows + 16 * t + g + 8 * (i >> 1)) * 16 + 8 * nt + 2 * c4 + (i & 1)] = acc[t][nt][i];
+        red[(grp * rows + 16 * (half * TW + t) + g + 8 * (i >> 1)) * 16 + 8 * nt + 2 * c4 + (i & 1)] = acc[t][nt][i];
   }
   __syncthreads();
-  // Sum the four group warps into red[0] (tokens past 8*NT stay unused).
+  // Sum the four groups into red[0] (tokens past 8*NT stay unused).
   for (int idx = threadIdx.x; idx < rows * 16; idx += kThreads)
     red[idx] = red[idx] + red[rows * 16 + idx] + red[2 * rows * 16 + idx] + red[3 * rows * 16 + idx];
   if (split > 1) {
@@ -261,6 +305,29 @@ __global__ void __launch_bounds__(kThreads)
     __syncthreads();
   }
   if (kslice == 0) {
+    // The table's space now holds Ts and this tile's Blora rows.
+    float* ts = reinterpret_cast<float*>(table);
+    float* bl = ts + 16 * kTsStride;
+    if (args.rank > 0) {
+      // Blora rows first: they do not depend on the low-rank kernel.
+#pragma unroll 4
+      for (int idx = threadIdx.x; idx < rows * args.rank; idx += kThreads) {
+        const int r = idx / args.rank, jj = idx % args.rank;
+        bl[r * 64 + jj] = n0 + r < args.N ? __ldg(args.blora + static_cast<size_t>(n0) * args.rank + idx) : 0.f;
+      }
+      griddep_wait();
+      // Ts[m][j] = bf16(s * sum of the partials in order).
+      const int n_cl = args.n_parts;
+      for (int o = threadIdx.x; o < args.M * args.rank; o += kThreads) {
+        const int m = o / args.rank, jj = o % args.rank;
+        const float* src = args.parts + (static_cast<size_t>(m) * 64 + jj) * n_cl;
+        float v = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < n_cl; ++c) v += __ldg(src + c);
+        ts[m * kTsStride + jj] = __bfloat162float(__float2bfloat16_rn(args.s * v));
+      }
+      __syncthreads();
+    }
     const uint32_t red_local = smem_u32(red);
     for (int idx = threadIdx.x; idx < rows * 16; idx += kThreads) {
       const int lr = idx >> 4, tok = idx & 15;
@@ -270,9 +337,9 @@ __global__ void __launch_bounds__(kThreads)
         for (int p = 1; p < split; ++p)
           v += __uint_as_float(ld_shared_cluster_u32(mapa_shared(red_local, static_cast<uint32_t>(p)) + idx * 4));
         if (args.rank > 0) {
-          const __nv_bfloat16* tr = args.Ts + static_cast<size_t>(tok) * 64;
-          const float* br = args.blora + static_cast<size_t>(n) * args.rank;
-          for (int jj = 0; jj < args.rank; ++jj) v = fmaf(__bfloat162float(tr[jj]), __ldg(br + jj), v);
+          const float* tr = ts + tok * kTsStride;
+          const float* br = bl + lr * 64;
+          for (int jj = 0; jj < args.rank; ++jj) v = fmaf(tr[jj], br[jj], v);
         }
         args.Y[static_cast<size_t>(tok) * args.N + n] = __float2bfloat16_rn(v);
       }
@@ -281,94 +348,108 @@ __global__ void __launch_bounds__(kThreads)
   if (split > 1) cluster_sync();  // peers' partials stay valid until rank 0 has read them
 }
 
-template <int NT, int TPC>
-static int launch_nt(const Args& a, const CUtensorMap& tc, const CUtensorMap& ts, int blocks, int smem,
-                     cudaStream_t stream) {
-  static bool attr_set[64] = {false};
+// CTAs of smallm_kernel<NT, TW> resident per SM with `slots` ring slots (sets
+// the kernel's shared-memory limit once per device and ring depth).
+template <int NT, int TW>
+static int resident_per_sm(int slots, int* per_sm) {
+  static int cache[64][9] = {};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&smallm_kernel<NT, TPC>),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "small-M attr: %s", cudaGetErrorString(e));
-    attr_set[dev] = true;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || slots < 1 || slots > 8)
+    return set_error(FL_ERR_CUDA, "small-M: no current device");
+  if (!cache[dev][slots]) {
+    const int smem = smem_bytes(32 * TW, NT, slots);
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&smallm_kernel<NT, TW>),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int n = 0;
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, smallm_kernel<NT, TW>, kThreads, smem);
+    if (e != cudaSuccess || n < 1) return set_error(FL_ERR_CUDA, "small-M occupancy query failed");
+    cache[dev][slots] = n;
   }
+  *per_sm = cache[dev][slots];
+  return FL_OK;
+}
+
+template <int NT, int TW>
+static int launch_tw(Args a, const void* codes, const float* scales, bool pdl, cudaStream_t stream) {
+  constexpr int rows = 32 * TW;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    sms = 148;
+  // Ring depth: the most slots that still fit next to the table at the
+  // occupancy the registers allow.
+  constexpr int want_ctas = TW == 1 ? 3 : 2;
+  int slots = 2;
+  while (slots < 6 && want_ctas * (smem_bytes(rows, NT, slots + 1) + 1024) <= 233472) ++slots;
+  int per_sm = 1;
+  int rc = resident_per_sm<NT, TW>(slots, &per_sm);
+  if (rc) return rc;
+  const int blocks = (a.N + rows - 1) / rows;
+  // Too few row blocks for one full wave: split the reduction across a cluster.
+  const int chunks = a.K / kChunkK;
+  int split = 1;
+  while (split < 8 && blocks * split * 2 <= per_sm * sms && chunks >= 2 * split) split *= 2;
+  a.split = split;
+  a.slots = slots;
+  CUtensorMap tc, tx, ts;
+  rc = make_tensor_map_2d(&tc, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.K / 2, a.N, a.K / 2, 128, rows,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tensor_map_2d(&tx, a.X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.K, a.M, static_cast<uint64_t>(a.K) * 2, 64,
+                          8 * NT, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tensor_map_2d(&ts, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.K / 128, a.N,
+                          static_cast<uint64_t>(a.K / 128) * 4, 4, rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(blocks * a.split);
+  cfg.gridDim = dim3(blocks * split);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = smem_bytes(rows, NT, slots);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = a.split;
+  attr[0].val.clusterDim.x = split;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t le = cudaLaunchKernelEx(&cfg, smallm_kernel<NT, TPC>, tc, ts, a);
+  cfg.numAttrs = pdl ? 2 : 1;
+  cudaError_t le = cudaLaunchKernelEx(&cfg, smallm_kernel<NT, TW>, tc, tx, ts, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "small-M launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }
 
 }  // namespace sm
 
-int launch_smallm_fwd(const void* X, const void* Ts, const uint8_t* codes, const float* scales, const float* lut,
-                      const float* lora, int rank, void* Y, int M, int N, int K, cudaStream_t stream) {
+int launch_smallm_fwd(const void* X, const float* lora_parts, float s, const uint8_t* codes, const float* scales,
+                      const float* lut, const float* lora, int rank, void* Y, int M, int N, int K, cudaStream_t stream,
+                      int layout) {
   using namespace sm;
   if (M < 1 || M > 16) return set_error(FL_ERR_ARG, "small-M path needs 1 <= M <= 16");
   if (K % kChunkK != 0) return set_error(FL_ERR_ARG, "small-M path needs K %% 512 == 0");
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
-    sms = 148;
-  // One wave at kCtasPerSm CTAs per SM: the fewest 16-row tiles per CTA that
-  // fit (1, 2, 4 or 8).
-  const int tiles = (N + 15) / 16;
-  const int want = (tiles + kCtasPerSm * sms - 1) / (kCtasPerSm * sms);
-  int tpc = 1;
-  const int max_tpc = M <= 8 ? kMaxTpc : kMaxTpc / 2;  // 16 tokens x 8 tiles would spill registers
-  while (tpc < want && tpc < max_tpc) tpc *= 2;
-  const int rows = 16 * tpc;
-  const int blocks = (N + rows - 1) / rows;
-  // Too few row blocks: split the reduction across a cluster.
-  const int chunks = K / kChunkK;
-  int split = 1;
-  while (split < 8 && blocks * split * 2 <= kCtasPerSm * sms && chunks >= 2 * split) split *= 2;
-  const int sbytes = (slot_bytes(rows) + 1023) / 1024 * 1024;
-  int slots = kSlotBudget / sbytes;
-  if (slots > 8) slots = 8;
-  if (slots < 2) slots = 2;
-  const int smem = 1024 + slots * sbytes + kWarps * rows * 16 * 4 + slots * 8 + 16;
+  if (layout != 0) return set_error(FL_ERR_UNSUPPORTED, "small-M path: group-128 records only");
   Args a;
   a.X = static_cast<const __nv_bfloat16*>(X);
-  a.Ts = static_cast<const __nv_bfloat16*>(Ts);
+  a.parts = lora_parts;
+  a.n_parts = K / (128 * lora_parts_per_cluster(K));
+  a.s = s;
   a.lut = lut;
   a.blora = lora;
   a.Y = static_cast<__nv_bfloat16*>(Y);
+  int dev = 0;
+  cudaGetDevice(&dev);
   a.status = status_word(dev);
   a.M = M;
   a.N = N;
   a.K = K;
   a.rank = rank;
-  a.tpc = tpc;
-  a.split = split;
-  a.slots = slots;
-  CUtensorMap tc, ts;
-  int rc = make_tensor_map_2d(&tc, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, 128, rows,
-                              CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  rc = make_tensor_map_2d(&ts, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, K / 128, N, static_cast<uint64_t>(K / 128) * 4,
-                          4, rows, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
-  if (M <= 8) {
-    if (tpc == 1) return launch_nt<1, 1>(a, tc, ts, blocks, smem, stream);
-    if (tpc == 2) return launch_nt<1, 2>(a, tc, ts, blocks, smem, stream);
-    if (tpc == 4) return launch_nt<1, 4>(a, tc, ts, blocks, smem, stream);
-    return launch_nt<1, 8>(a, tc, ts, blocks, smem, stream);
-  }
-  if (tpc == 1) return launch_nt<2, 1>(a, tc, ts, blocks, smem, stream);
-  if (tpc == 2) return launch_nt<2, 2>(a, tc, ts, blocks, smem, stream);
-  return launch_nt<2, 4>(a, tc, ts, blocks, smem, stream);
+  a.split = 1;
+  a.slots = 2;
+  // With a LoRA term the preceding launch produced Ts: start while it runs.
+  const bool pdl = rank > 0;
+  if (M <= 8) return launch_tw<1, kTilesPerWarp>(a, codes, scales, pdl, stream);
+  return launch_tw<2, kTilesPerWarp>(a, codes, scales, pdl, stream);
 }
 
 }  // namespace fl

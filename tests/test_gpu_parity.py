@@ -217,17 +217,21 @@ SMALLM_CASES = [
     (16, 4096, 14336, 16),
     (13, 200, 512, 64),      # ragged rows and tokens
     (16, 1024, 1024, 8),     # reduction split over a 2-CTA cluster
-    (3, 1000, 2048, 32),     # row count not a multiple of 16
+    (3, 1000, 2048, 32),     # row count not a multiple of 32
     (16, 8192, 512, 16),     # one 512-wide chunk per CTA
     (9, 4096, 14336, 64),    # 28 chunks through the slot ring, rank 64
+    (7, 640, 384, 16),       # K % 512 != 0: the tile GEMM
+    (16, 8, 128, 4),         # one group, 8 valid rows (tile GEMM)
+    (2, 29568, 4096, 0),     # 924 row blocks: no split
 ]
 
 
 @pytest.mark.parametrize("codec_name", ["int4-sym-g128", "nf4-g128"])
 @pytest.mark.parametrize("M,N,K,rank", SMALLM_CASES)
 def test_small_m_fwd_parity(cuda_lib, codec_name, M, N, K, rank):
-    """M <= 16 with K % 512 == 0 runs the decode-step kernel (operand bf16(lut), scale on the partial
-    sums); other K take the tile GEMM."""
+    """M <= 16 with K % 512 == 0 runs the decode-step kernel (operand bf16(lut), scale on each
+    group's partial sum, LoRA term added in FP32 from the bf16 Ts of the small-M low-rank kernel);
+    other K take the tile GEMM."""
     from spilltune_b200 import ops
     pw, x, A, B, _ = _problem(M, N, K, rank, codec_name, seed=M * 11 + N + K)
     s = 2.0

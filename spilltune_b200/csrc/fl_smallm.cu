@@ -90,10 +90,12 @@ __host__ __device__ constexpr int slot_bytes(int rows, int nt) {
   return rows * 128 * 2 + 8 * x_box_bytes(nt) + rows * 16;
 }
 __host__ __device__ constexpr int slot_stride(int rows, int nt) { return (slot_bytes(rows, nt) + 1023) / 1024 * 1024; }
-// Dynamic shared memory: ring | table | partial sums [group][rows][16] | full and empty mbarriers + abort word.
+// Dynamic shared memory: ring | table | full and empty mbarriers + abort word.  After the
+// main loop the ring's space holds the partial sums [group][rows][16].
 __host__ __device__ constexpr int smem_bytes(int rows, int nt, int slots) {
-  return 1024 + slots * slot_stride(rows, nt) + kTableBytes + kGroups * rows * 16 * 4 + 2 * slots * 8 + 16;
+  return 1024 + slots * slot_stride(rows, nt) + kTableBytes + 2 * slots * 8 + 16;
 }
+__host__ __device__ constexpr int red_bytes(int rows) { return kGroups * rows * 16 * 4; }
 
 // NT: 8-token tiles, 1 (M <= 8) or 2 (M <= 16).  TW: 16-row tiles per warp,
 // unrolled so the MMA chains of different tiles interleave; with one tile and
@@ -113,8 +115,8 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
   constexpr int kSOff = kXOff + 8 * x_box_bytes(NT);   // scales within a slot
   uint8_t* ring = smem;                                                    // slots x sbytes
   uint8_t* table = smem + args.slots * sbytes;                             // [256][32] u32
-  float* red = reinterpret_cast<float*>(table + kTableBytes);              // [group][rows][16]
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + kGroups * rows * 16);  // [slots]: TMA bytes landed
+  float* red = reinterpret_cast<float*>(ring);                             // [group][rows][16], after the loop
+  uint64_t* full = reinterpret_cast<uint64_t*>(table + kTableBytes);        // [slots]: TMA bytes landed
   uint64_t* empty = full + args.slots;                                      // [slots]: every consumer warp done
   volatile uint32_t* abort_word = reinterpret_cast<volatile uint32_t*>(empty + args.slots);
 
@@ -284,8 +286,11 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
   }
 
   // ------------------------------------------------------------ reductions
-  // Warp partials -> red[group][row][token]; accumulator element i of tile t:
-  // row 16 (half TW + t) + g + 8*(i >> 1), token 8*nt + 2*c4 + (i & 1).
+  // Warp partials -> red[group][row][token] in the ring's space, once every
+  // copy into the ring has landed (the consumers waited for each chunk; the
+  // producer drained what an abort left in flight): accumulator element i of
+  // tile t: row 16 (half TW + t) + g + 8*(i >> 1), token 8*nt + 2*c4 + (i & 1).
+  __syncthreads();
   if (warp < kWarps)
 #pragma unroll
   for (int t = 0; t < TW; ++t) {
@@ -381,6 +386,8 @@ static int launch_tw(Args a, const void* codes, const float* scales, bool pdl, c
   constexpr int want_ctas = TW == 1 ? 3 : 2;
   int slots = 2;
   while (slots < 6 && want_ctas * (smem_bytes(rows, NT, slots + 1) + 1024) <= 233472) ++slots;
+  if (want_ctas * (smem_bytes(rows, NT, slots) + 1024) > 233472 || red_bytes(rows) > slots * slot_stride(rows, NT))
+    return set_error(FL_ERR_CUDA, "small-M: shared-memory plan does not fit");
   int per_sm = 1;
   int rc = resident_per_sm<NT, TW>(slots, &per_sm);
   if (rc) return rc;

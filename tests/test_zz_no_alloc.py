@@ -55,7 +55,9 @@ def _fwd_noalloc(lib, pw, x, A, B, s):
 
 def test_noalloc_matches_workspace_entry_on_two_calls(cuda_lib):
     s = 2.0
-    for seed, (M, N, K, rank) in ((1, (512, 1024, 4096, 16)), (2, (300, 384, 256, 8))):
+    # The last two are decode-step shapes: the small-M kernel with its LoRA partial sums in the scratch.
+    for seed, (M, N, K, rank) in ((1, (512, 1024, 4096, 16)), (2, (300, 384, 256, 8)), (3, (16, 4096, 4096, 16)),
+                                  (4, (3, 1024, 2048, 8))):
         pw, x, A, B = _case(M, N, K, rank, seed)
         ref = _fwd_with_workspace(cuda_lib, pw, x, A, B, s)
         out = _fwd_noalloc(cuda_lib, pw, x, A, B, s)

@@ -97,7 +97,9 @@ size_t fl_bwd_workspace_bytes(int64_t M, int64_t N, int64_t K, int rank);
  *   dA = scale * (dY . B)^T . X,  dB = scale * dY^T . (X . A^T)  (fp32 out)
  * accumulate != 0 adds into dA/dB (grad_A/grad_B.add_, recompute.py:124-127);
  * accumulate == 0 overwrites them.  dA/dB may be NULL when rank == 0.
- * Requires K % 128 == 0, N % 64 == 0, rank <= 64.
+ * M <= 16 with K % 512 == 0 runs a decode-step kernel (the scale folded into
+ * bf16(dY * scale) instead of into the weight); larger M the tile GEMM.
+ * Requires K % 128 == 0, N % 64 == 0 (N % 128 == 0 when rank > 0), rank <= 64.
  */
 int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* payload,
            const float* scales, const float* lut16, const float* A, const float* B, int rank, float scale,

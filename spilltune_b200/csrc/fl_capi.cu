@@ -132,7 +132,7 @@ static int fwd_impl(const char* who, int layout, const uint16_t* X, int64_t M, i
   // partial sums use the converted-factor scratch (M * 64 * K/128 floats fit).
   if (layout == kLayoutG128 && M <= 16 && K % 512 == 0) {
     float* parts = static_cast<float*>(qc);
-    if (rank > 0 && (rc = launch_lora_parts(X, (int)M, (int)K, A, K, rank, parts, st))) return rc;
+    if (rank > 0 && (rc = launch_lora_parts(X, (int)M, (int)K, A, K, 1, rank, parts, st))) return rc;
     return launch_smallm_fwd(X, parts, scale, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st, layout);
   }
   if (rank > 0) {
@@ -153,6 +153,9 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
   if (!dY || !dX) return set_error(FL_ERR_ARG, "%s: null dY/dX", who);
   if (!aligned16(dY)) return set_error(FL_ERR_ARG, "%s: dY must be 16-byte aligned", who);
   if (rank > 0) {
+    if (N % 128 != 0)
+      return set_error(FL_ERR_ARG, "%s: out_features N=%lld must be a multiple of 128 with a LoRA branch", who,
+                       (long long)N);
     if (!X || !A || !B || !dA || !dB) return set_error(FL_ERR_ARG, "%s: null X or LoRA factor/gradient", who);
     if (!aligned16(X)) return set_error(FL_ERR_ARG, "%s: X must be 16-byte aligned", who);
     if (!workspace || workspace_bytes < fl_bwd_workspace_bytes(M, N, K, rank) || !aligned16(workspace))
@@ -163,9 +166,24 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* us = static_cast<uint8_t*>(workspace);
   uint8_t* ts = us ? us + static_cast<size_t>(M) * 128 : nullptr;
+  uint8_t* qc_b = rank > 0 ? ts + static_cast<size_t>(M) * 128 : nullptr;
+  uint8_t* qc_a = rank > 0 ? qc_b + lora_factor_bytes(N, rank) : nullptr;
+  // Decode-like steps (M <= 16) take the small-M backward, which also finishes
+  // the LoRA gradients; the tile GEMM's 256-token tiles would leave most SMs
+  // idle.  Its low-rank partials use the converted-factor scratch.
+  if (layout == kLayoutG128 && M <= 16 && K % 512 == 0) {
+    float* uparts = reinterpret_cast<float*>(qc_b);
+    float* tparts = reinterpret_cast<float*>(qc_a);
+    if (rank > 0) {
+      // X . A^T over K, then dY . B over N (Q(j, n) = B[n * rank + j]); the
+      // second lets the backward start early.
+      if ((rc = launch_lora_parts(X, (int)M, (int)K, A, K, 1, rank, tparts, st))) return rc;
+      if ((rc = launch_lora_parts(dY, (int)M, (int)N, B, 1, rank, rank, uparts, st))) return rc;
+    }
+    return launch_smallm_bwd(dY, X, uparts, tparts, scale, payload, scales, lut16, A, rank, dX, dA, dB, accumulate,
+                             (int)M, (int)N, (int)K, st);
+  }
   if (rank > 0) {
-    uint8_t* qc_b = ts + static_cast<size_t>(M) * 128;
-    uint8_t* qc_a = qc_b + lora_factor_bytes(N, rank);
     // Us = bf16(s * dY . B): Q(j, n) = B[n * rank + j]
     if ((rc = launch_lora_down(dY, (int)M, (int)N, B, 1, rank, rank, scale, us, qc_b, st))) return rc;
     // Ts = bf16(s * X . A^T): Q(j, k) = A[j * K + k]

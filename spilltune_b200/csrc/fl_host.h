@@ -55,12 +55,13 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
                      float s, void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles = nullptr,
                      const int* tile_count = nullptr, int max_tiles = 0, int64_t q_expert_stride = 0,
                      int experts = 1);
-// Small-M forward form (M <= 16, Q rows contiguous): parts[m][j][c] (j < rank) =
-// sum of P[m, r] * Q(j, r) over the 128 * lora_parts_per_cluster(R) columns of
-// partial c, exact FP32 (parts: M * 64 * R / (128 * per_cluster) floats).  Lets
-// the next launch of the stream start at once (programmatic dependent launch).
-int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj, int rank, float* parts,
-                      cudaStream_t stream);
+// Small-M form (M <= 16): parts[m][j][c] (j < rank) = sum of P[m, r] * Q(j, r),
+// Q(j, r) = q[j * q_sj + r * q_sr], over the 128 * lora_parts_per_cluster(R)
+// columns of partial c, exact FP32 (parts: M * 64 * R / (128 * per_cluster)
+// floats).  Lets the next launch of the stream start at once (programmatic
+// dependent launch).
+int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
+                      float* parts, cudaStream_t stream);
 int lora_parts_per_cluster(int R);  // 128-wide pieces summed into one partial
 int lora_nq(int rank);                           // rank padded to 16, 32 or 64
 size_t lora_factor_bytes(int64_t R, int rank);   // converted-factor scratch for a reduction of R
@@ -82,6 +83,16 @@ int launch_lora_grad(const void* P, int M, int Pdim, const void* Q, int rank, fl
 int launch_smallm_fwd(const void* X, const float* lora_parts, float s, const uint8_t* codes, const float* scales,
                       const float* lut, const float* lora, int rank, void* Y, int M, int N, int K,
                       cudaStream_t stream, int layout = 0);
+
+// The whole projection backward for M <= 16 tokens (fl_smallm_bwd.cu): dX[M,K] =
+// dY . W + Us . Alora and, with rank > 0, dA, dB (+= when accumulate), Us / Ts =
+// bf16(s * the launch_lora_parts partials of dY . B over N / of X . A^T over K).
+// K % 512 == 0, N % 64 == 0 (N % 128 == 0 when rank > 0), layout 0.  With rank >
+// 0 the launch may overlap the preceding one, which must be the launch_lora_parts
+// that wrote the last partials (programmatic dependent launch).
+int launch_smallm_bwd(const void* dY, const void* X, const float* uparts, const float* tparts, float s,
+                      const uint8_t* codes, const float* scales, const float* lut, const float* alora, int rank,
+                      void* dX, float* dA, float* dB, int accumulate, int M, int N, int K, cudaStream_t stream);
 
 // Chunked LM head + cross-entropy (fl_head.cu).
 size_t ce_workspace_bytes(int64_t T, int64_t V);

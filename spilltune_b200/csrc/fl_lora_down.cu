@@ -122,6 +122,9 @@ __global__ void __launch_bounds__(kThreads)
                      const int* __restrict__ tile_count, uint32_t* status) {
   using C = Cfg<NQ>;
   constexpr int NT = NQ / 8;  // n-tiles of 8 rank columns
+  // A launch of the stream that may overlap this one (programmatic dependent
+  // launch, the small-M backward) waits for its completion before reading out.
+  griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::kStage);
@@ -455,7 +458,7 @@ static int launch(const void* P, int M, int R, const float* q, int64_t q_sj, int
 // weights on the same SMs.
 __global__ void __launch_bounds__(kThreads)
     lora_parts_kernel(const __nv_bfloat16* __restrict__ P, int M, int R, const float* __restrict__ q,
-                      int64_t q_sj, int rank, float* __restrict__ parts, int csize) {
+                      int64_t q_sj, int64_t q_sr, int rank, float* __restrict__ parts, int csize) {
   griddep_launch_dependents();
   __shared__ float mine[kMaxRows * 64];  // [m][j] of this CTA's piece
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -465,7 +468,13 @@ __global__ void __launch_bounds__(kThreads)
   for (int m = 0; m < kMaxRows; ++m)
     xv[m] = m < M ? __ldg(reinterpret_cast<const uint2*>(P + static_cast<size_t>(m) * R + r)) : make_uint2(0, 0);
   for (int j = warp; j < rank; j += kWarps) {
-    const float4 qv = __ldg(reinterpret_cast<const float4*>(q + j * q_sj + r));
+    float4 qv;
+    if (q_sr == 1) {
+      qv = __ldg(reinterpret_cast<const float4*>(q + j * q_sj + r));
+    } else {
+      const float* qj = q + j * q_sj + r * q_sr;
+      qv = make_float4(__ldg(qj), __ldg(qj + q_sr), __ldg(qj + 2 * q_sr), __ldg(qj + 3 * q_sr));
+    }
     float acc[kMaxRows];
 #pragma unroll
     for (int m = 0; m < kMaxRows; ++m) {
@@ -503,12 +512,12 @@ __global__ void __launch_bounds__(kThreads)
 
 }  // namespace lds
 
-int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj, int rank, float* parts,
-                      cudaStream_t stream) {
+int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
+                      float* parts, cudaStream_t stream) {
   if (R % 128 != 0 || M < 1 || M > lds::kMaxRows || rank < 1 || rank > 64)
     return set_error(FL_ERR_ARG, "lora_parts: needs R %% 128 == 0, 1 <= M <= 16, 1 <= rank <= 64");
-  if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(parts)) & 15u ||
-      q_sj % 4 != 0)
+  if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(parts)) & 15u ||
+      (q_sr == 1 && ((reinterpret_cast<uintptr_t>(q) & 15u) || q_sj % 4 != 0)))
     return set_error(FL_ERR_ARG, "lora_parts: activations, factor and partials must be 16-byte aligned");
   const int csize = lora_parts_per_cluster(R);
   cudaLaunchConfig_t cfg = {};
@@ -523,7 +532,7 @@ int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, lds::lora_parts_kernel, static_cast<const __nv_bfloat16*>(P), M, R, q, q_sj,
-                                     rank, parts, csize);
+                                     q_sr, rank, parts, csize);
   if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_parts launch: %s", cudaGetErrorString(e));
   return FL_OK;
 }

@@ -90,7 +90,7 @@ extern "C" int fl_fwd_noalloc(const uint16_t* X, int64_t M, int64_t K, const uin
     // LoRA partial sums (M * 64 * K/128 floats) in the factor scratch.
     float* parts = rank > 0 ? reinterpret_cast<float*>(ts + kNoAllocScratchBytes) : nullptr;
     if (rank > 0) {
-      const int rc = launch_lora_parts(X, (int)M, (int)K, A, K, rank, parts, st);
+      const int rc = launch_lora_parts(X, (int)M, (int)K, A, K, 1, rank, parts, st);
       if (rc) return rc;
     }
     return launch_smallm_fwd(X, parts, scale, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st);

@@ -119,8 +119,12 @@ def test_grouped_bwd(cuda_lib, codec_name, lengths, N, K, rank):
                 continue
             ddx, _, _ = ops.bwd(dyc, xc, pe, Ac[e], Bc[e], s)
             _, edA, edB = ops.bwd(dyc[a:b].contiguous(), xc[a:b].contiguous(), pe, Ac[e], Bc[e], s)
-            assert ol.rel_l2(dA[e].cpu(), edA.cpu()) < 1e-5
-            assert ol.rel_l2(dB[e].cpu(), edB.cpu()) < 1e-5
+            # A segment of <= 16 rows takes the decode-step backward when run alone, whose
+            # Us / Ts are exact FP32 sums (the grouped path's low-rank kernel carries ~16
+            # mantissa bits), so a bf16 rounding of Us / Ts may differ there.
+            tol = 1e-5 if b - a > 16 else TIGHT
+            assert ol.rel_l2(dA[e].cpu(), edA.cpu()) < tol
+            assert ol.rel_l2(dB[e].cpu(), edB.cpu()) < tol
         elif a == b:
             continue
         else:

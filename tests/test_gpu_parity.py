@@ -122,6 +122,36 @@ def test_bwd_parity(cuda_lib, codec_name, M, N, K, rank):
     assert max(e) <= BAR and max(e) <= TIGHT, e
 
 
+SMALLM_BWD_CASES = [
+    # M, N, K, rank
+    (1, 4096, 4096, 16),
+    (16, 14336, 4096, 16),   # reduction over 224 chunks of 64 rows, 2-CTA clusters
+    (16, 4096, 14336, 64),   # 112 column blocks, rank 64
+    (7, 1024, 4096, 0),      # plain frozen VJP, 8-CTA clusters
+    (9, 64, 512, 0),         # one chunk, four column blocks
+    (9, 128, 512, 8),        # two chunks, LoRA (its reduction over N needs N % 128 == 0)
+    (13, 256, 1024, 32),     # four chunks over a cluster
+]
+
+
+@pytest.mark.parametrize("codec_name", ["int4-sym-g128", "nf4-g128"])
+@pytest.mark.parametrize("M,N,K,rank", SMALLM_BWD_CASES)
+def test_small_m_bwd_parity(cuda_lib, codec_name, M, N, K, rank):
+    """M <= 16 with K % 512 == 0 runs the decode-step backward (scale folded into bf16(dY * scale),
+    transposed byte-table decode); dA and dB stay on the low-rank kernels."""
+    from spilltune_b200 import ops
+    pw, x, A, B, dy = _problem(M, N, K, rank, codec_name, seed=M * 5 + N + K)
+    s = 2.0
+    dx, dA, dB = ops.bwd(dy.cuda(), x.cuda(), pw.to("cuda"), _cuda(A), _cuda(B), s)
+    W = _decode_cpu(pw)
+    if rank:
+        rdx, rdA, rdB = ol.lora_backward_fp32(x, W, A, B, s, dy)
+        e = (ol.rel_l2(dx.cpu(), rdx), ol.rel_l2(dA.cpu(), rdA), ol.rel_l2(dB.cpu(), rdB))
+    else:
+        e = (ol.rel_l2(dx.cpu(), dy.float() @ W.float()),)
+    assert max(e) <= BAR and max(e) <= TIGHT, e
+
+
 def test_bwd_accumulate(cuda_lib):
     from spilltune_b200 import ops
     pw, x, A, B, dy = _problem(256, 256, 256, 16, "int4-sym-g128", seed=5)

@@ -90,10 +90,12 @@ __host__ __device__ constexpr int slot_bytes(int rows, int nt) {
   return rows * 128 * 2 + 8 * x_box_bytes(nt) + rows * 16;
 }
 __host__ __device__ constexpr int slot_stride(int rows, int nt) { return (slot_bytes(rows, nt) + 1023) / 1024 * 1024; }
-// Dynamic shared memory: ring | table | full and empty mbarriers + abort word.  After the
-// main loop the ring's space holds the partial sums [group][rows][16].
+// Dynamic shared memory: ring | full and empty mbarriers + abort word.  After the main
+// loop the ring's space holds the partial sums [group][rows][16].  The byte table is a
+// static shared array (its address a link-time constant, so a lookup's address needs
+// no add): kTableBytes more per CTA.
 __host__ __device__ constexpr int smem_bytes(int rows, int nt, int slots) {
-  return 1024 + slots * slot_stride(rows, nt) + kTableBytes + 2 * slots * 8 + 16;
+  return 1024 + slots * slot_stride(rows, nt) + 2 * slots * 8 + 16;
 }
 __host__ __device__ constexpr int red_bytes(int rows) { return kGroups * rows * 16 * 4; }
 
@@ -107,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
                   const __grid_constant__ CUtensorMap tm_scales,  // [N, K/128] fp32, box {4, rows}
                   const Args args) {
   extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(1024) uint32_t s_table[kTableBytes / 4];  // [256][32] bf16 pairs
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int PS = TW * NT <= 1 ? 2 : 1;
   constexpr int rows = 32 * TW;
@@ -114,9 +117,9 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
   constexpr int kXOff = rows * 256;                    // activation boxes within a slot
   constexpr int kSOff = kXOff + 8 * x_box_bytes(NT);   // scales within a slot
   uint8_t* ring = smem;                                                    // slots x sbytes
-  uint8_t* table = smem + args.slots * sbytes;                             // [256][32] u32
+  uint8_t* table = reinterpret_cast<uint8_t*>(s_table);
   float* red = reinterpret_cast<float*>(ring);                             // [group][rows][16], after the loop
-  uint64_t* full = reinterpret_cast<uint64_t*>(table + kTableBytes);        // [slots]: TMA bytes landed
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + args.slots * sbytes);  // [slots]: TMA bytes landed
   uint64_t* empty = full + args.slots;                                      // [slots]: every consumer warp done
   volatile uint32_t* abort_word = reinterpret_cast<volatile uint32_t*>(empty + args.slots);
 
@@ -174,13 +177,15 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
     for (int j = 0; j < 32; ++j) tw[j * 32] = __shfl_sync(0xffffffffu, packed, j);
   }
   __syncthreads();
-  const uint32_t tab = smem_u32(table) + static_cast<uint32_t>(lane) * 4;
-  // Byte b of payload word w -> the pair of elements 2b, 2b + 1.
+  // Byte b of payload word w -> the pair of elements 2b, 2b + 1, at entry byte * 128 + lane * 4
+  // (bits 7..14 and 2..6: an OR).
+  const uint32_t tab0 = smem_u32(s_table);
+  const uint32_t lane4 = static_cast<uint32_t>(lane) * 4;
   auto decode = [&](uint32_t w, uint32_t* out) {
-    out[0] = lds_u32(tab + ((w << 7) & 0x7F80u));
-    out[1] = lds_u32(tab + ((w >> 1) & 0x7F80u));
-    out[2] = lds_u32(tab + ((w >> 9) & 0x7F80u));
-    out[3] = lds_u32(tab + ((w >> 17) & 0x7F80u));
+    out[0] = lds_u32(tab0 + (((w << 7) & 0x7F80u) | lane4));
+    out[1] = lds_u32(tab0 + (((w >> 1) & 0x7F80u) | lane4));
+    out[2] = lds_u32(tab0 + (((w >> 9) & 0x7F80u) | lane4));
+    out[3] = lds_u32(tab0 + (((w >> 17) & 0x7F80u) | lane4));
   };
 
   float acc[TW][NT][4];
@@ -385,8 +390,9 @@ static int launch_tw(Args a, const void* codes, const float* scales, bool pdl, c
   // occupancy the registers allow.
   constexpr int want_ctas = TW == 1 ? 3 : 2;
   int slots = 2;
-  while (slots < 6 && want_ctas * (smem_bytes(rows, NT, slots + 1) + 1024) <= 233472) ++slots;
-  if (want_ctas * (smem_bytes(rows, NT, slots) + 1024) > 233472 || red_bytes(rows) > slots * slot_stride(rows, NT))
+  while (slots < 6 && want_ctas * (smem_bytes(rows, NT, slots + 1) + kTableBytes + 1024) <= 233472) ++slots;
+  if (want_ctas * (smem_bytes(rows, NT, slots) + kTableBytes + 1024) > 233472 ||
+      red_bytes(rows) > slots * slot_stride(rows, NT))
     return set_error(FL_ERR_CUDA, "small-M: shared-memory plan does not fit");
   int per_sm = 1;
   int rc = resident_per_sm<NT, TW>(slots, &per_sm);

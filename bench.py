@@ -19,8 +19,9 @@ alternating per-layer buffer sets (each layer touches ~2 GB, far above L2).
 `e2e`    : tokens/s through the public API with host buffers: packed layers in
            pinned host memory streamed by PackedSlotSession (2 VRAM slots,
            one-layer prefetch on a copy stream, reloaded for the backward like
-           the reference), the stack input copied H2D and the step's gradient
-           norm read back D2H every step.
+           the reference; with N > 1 each rank copies 1/N of every layer and the
+           slot is all-gathered over NVLink), the stack input copied H2D and the
+           step's gradient norm read back D2H every step.
 """
 import argparse
 import contextlib
@@ -416,7 +417,15 @@ def main():
         for lw in weights:
             lw.clear()
         torch.cuda.empty_cache()
-        sess = PackedSlotSession(host_layers, dev, slots=2)
+        # N > 1: each rank copies its 1/N of every layer from the host and the
+        # slot is all-gathered over NVLink on a communicator of its own.
+        wgroup = None
+        if world > 1:
+            import torch.distributed as dist
+            wgroup = dist.new_group(backend="nccl")
+        sess = PackedSlotSession(host_layers, dev, slots=2, group=wgroup)
+        if wgroup is not None:
+            host_layers = None  # the session keeps this rank's shards only
         x0_host = torch.randn(M, HIDDEN, dtype=torch.float32).to(torch.bfloat16).pin_memory()
         norm_host = torch.empty(1, dtype=torch.float32).pin_memory()
         estep = Step(sess.borrow, loras, bufs, world, opt)
@@ -447,6 +456,10 @@ def main():
                "d2h_bytes_per_step": 4, "ms_per_step": ems,
                "slot_h2d_gbs": (sess.h2d_bytes / copy_s / 1e9) if copy_s > 0 else None,
                "weights": "pinned host, 2 VRAM slots, one-layer prefetch (fwd + bwd reload)"}
+        if wgroup is not None:
+            e2e["weights"] = (f"pinned host, 1/{world} of each layer per rank, copied into 2 VRAM slots and "
+                              "all-gathered over NVLink (NCCL, own communicator), one-layer prefetch")
+            e2e["nvlink_gather_bytes_per_step"] = int(sess.h2d_bytes * (world - 1) / args.steps)
         sess.close()
 
     # ------------------------------------------------------------ report

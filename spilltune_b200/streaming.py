@@ -15,6 +15,14 @@ extended to the compressed blocks ``PrefetchSession`` refuses today
   next overwrite (prefetch.py:217-218);
 * no device-wide synchronize on the load path (memory.py:204-206 does one per load).
 
+With a process group (data parallel over the GPUs of one box), a rank keeps and
+copies only its 1/W byte range of each layer's slot image, and the slot is
+completed by an in-place NCCL all-gather over NVLink on the copy stream: host
+traffic (and pinned host memory) per GPU drops W-fold, which matters because the
+GPUs of a box share the host's memory bandwidth.  The group should be one of
+its own (``torch.distributed.new_group``), so weight gathers never interleave
+with other collectives on the same communicator.
+
 Failures poison the session, like the reference's (prefetch.py:94-101).
 """
 from contextlib import contextmanager
@@ -41,10 +49,36 @@ def layer_bytes(layer):
     return _align(total)
 
 
+def _parts(layer):
+    """(slot offset, byte view) of every part of a layer, in slot-image order."""
+    out = []
+    off = 0
+    for w in layer.values():
+        for t in (w.payload, w.scales, w.lut):
+            off = _align(off)
+            b = t.reshape(-1).view(torch.uint8)
+            out.append((off, b))
+            off += b.numel()
+    return out
+
+
+def shard_image(layer, start, size, out=None):
+    """Bytes [start, start + size) of the layer's slot image (zero past its parts), as a CPU tensor."""
+    if out is None:
+        out = torch.zeros(size, dtype=torch.uint8)
+    else:
+        out.zero_()
+    for off, b in _parts(layer):
+        lo, hi = max(off, start), min(off + b.numel(), start + size)
+        if lo < hi:
+            out[lo - start:hi - start].copy_(b[lo - off:hi - off])
+    return out
+
+
 class PackedSlotSession:
     """Two (or more) device slots fed from pinned host layers on a copy stream."""
 
-    def __init__(self, layers, device, *, slots=2, copy_stream=None):
+    def __init__(self, layers, device, *, slots=2, copy_stream=None, group=None):
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("unsupported_capability: slot streaming needs a CUDA device")
@@ -61,6 +95,19 @@ class PackedSlotSession:
                         raise ValueError("host records must be contiguous pinned CPU tensors")
         self.layers = list(layers)
         self.capacity = max(layer_bytes(layer) for layer in self.layers)
+        self.group = group
+        self.world, self.rank = 1, 0
+        if group is not None:
+            import torch.distributed as dist
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.host_shards = None
+        if self.world > 1:
+            # Equal 256-byte-aligned shards; this rank's range of every layer, pinned.
+            step = self.world * _ALIGN
+            self.capacity = (self.capacity + step - 1) // step * step
+            self.shard = self.capacity // self.world
+            self.host_shards = [shard_image(layer, self.rank * self.shard, self.shard).pin_memory()
+                                for layer in self.layers]
         with torch.cuda.device(self.device):
             self.copy_stream = copy_stream or torch.cuda.Stream(device=self.device)
             self.slots = []
@@ -115,12 +162,21 @@ class PackedSlotSession:
             start = torch.cuda.Event(enable_timing=True)
             end = torch.cuda.Event(enable_timing=True)
             start.record(self.copy_stream)
-            for name, w in src.items():
-                v = views[name]
-                v.payload.copy_(w.payload, non_blocking=True)
-                v.scales.copy_(w.scales, non_blocking=True)
-                v.lut.copy_(w.lut, non_blocking=True)
-                nbytes += w.payload.numel() + 4 * w.scales.numel() + 64
+            if self.host_shards is not None:
+                import torch.distributed as dist
+                buf = slot["buffer"]
+                mine = buf.narrow(0, self.rank * self.shard, self.shard)
+                mine.copy_(self.host_shards[idx], non_blocking=True)
+                nbytes = self.shard
+                # In place: every rank's chunk of the slot -> the whole slot on every rank.
+                dist.all_gather_into_tensor(buf, mine, group=self.group, async_op=True).wait()
+            else:
+                for name, w in src.items():
+                    v = views[name]
+                    v.payload.copy_(w.payload, non_blocking=True)
+                    v.scales.copy_(w.scales, non_blocking=True)
+                    v.lut.copy_(w.lut, non_blocking=True)
+                    nbytes += w.payload.numel() + 4 * w.scales.numel() + 64
             end.record(self.copy_stream)
         slot.update(layer=idx, ready=end, views=views)
         self.copy_events.append((start, end, nbytes))
@@ -171,7 +227,8 @@ class PackedSlotSession:
                 self._lock.release()
 
     def h2d_seconds(self):
-        """Sum of copy-stream durations of completed uploads (synchronizes their events)."""
+        """Sum of copy-stream durations of completed uploads (synchronizes their events; with a
+        group this includes the all-gather)."""
         total = 0.0
         for s, e, _ in self.copy_events:
             e.synchronize()

@@ -103,3 +103,24 @@ def test_unpinned_sources_rejected(fake_cuda, monkeypatch):
     monkeypatch.setattr(torch.Tensor, "is_pinned", lambda self: False)
     with pytest.raises(ValueError, match="pinned"):
         streaming.PackedSlotSession(_layers(2), "cuda:0", slots=2)
+
+
+def test_shard_images_reassemble_the_slot_image():
+    """With a process group each rank keeps bytes [r*S, (r+1)*S) of a layer's slot image; the
+    all-gathered shards must give back every part at the offset the slot views read it from."""
+    from spilltune_b200 import codec
+    from spilltune_b200.streaming import _parts, layer_bytes, shard_image
+    g = torch.Generator().manual_seed(5)
+    layer = {name: codec.encode(torch.randn(n, k, generator=g) * 0.02, "nf4-g128")
+             for name, n, k in (("q", 256, 384), ("k", 128, 384), ("down", 384, 256))}
+    for world in (2, 3, 8):
+        step = world * 256
+        cap = (layer_bytes(layer) + step - 1) // step * step
+        shard = cap // world
+        image = torch.cat([shard_image(layer, r * shard, shard) for r in range(world)])
+        assert image.numel() == cap
+        end = 0
+        for off, b in _parts(layer):
+            assert torch.equal(image[off:off + b.numel()], b)
+            end = off + b.numel()
+        assert int(image[end:].count_nonzero()) == 0  # padding past the last part

@@ -175,10 +175,10 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
     float* uparts = reinterpret_cast<float*>(qc_b);
     float* tparts = reinterpret_cast<float*>(qc_a);
     if (rank > 0) {
-      // X . A^T over K, then dY . B over N (Q(j, n) = B[n * rank + j]); the
-      // second lets the backward start early.
-      if ((rc = launch_lora_parts(X, (int)M, (int)K, A, K, 1, rank, tparts, st))) return rc;
-      if ((rc = launch_lora_parts(dY, (int)M, (int)N, B, 1, rank, rank, uparts, st))) return rc;
+      // X . A^T over K and dY . B over N (Q(j, n) = B[n * rank + j]) in one
+      // launch, which lets the backward start at once.
+      if ((rc = launch_lora_parts2(X, (int)K, A, K, 1, tparts, dY, (int)N, B, 1, rank, uparts, (int)M, rank, st)))
+        return rc;
     }
     return launch_smallm_bwd(dY, X, uparts, tparts, scale, payload, scales, lut16, A, rank, dX, dA, dB, accumulate,
                              (int)M, (int)N, (int)K, st);

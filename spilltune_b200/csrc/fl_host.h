@@ -62,7 +62,14 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
 // dependent launch).
 int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
                       float* parts, cudaStream_t stream);
-int lora_parts_per_cluster(int R);  // 128-wide pieces summed into one partial
+// Two such reductions over the same M rows in one launch (the backward's X·Aᵀ and
+// dY·B): both use the common cluster size lora_parts_per_cluster(R0, R1), so
+// partial counts are R0 / (128 * it) and R1 / (128 * it).
+int launch_lora_parts2(const void* P0, int R0, const float* q0, int64_t q0_sj, int64_t q0_sr, float* parts0,
+                       const void* P1, int R1, const float* q1, int64_t q1_sj, int64_t q1_sr, float* parts1, int M,
+                       int rank, cudaStream_t stream);
+// 128-wide pieces summed into one partial (R1 > 0: the common size for both).
+int lora_parts_per_cluster(int R0, int R1 = 0);
 int lora_nq(int rank);                           // rank padded to 16, 32 or 64
 size_t lora_factor_bytes(int64_t R, int rank);   // converted-factor scratch for a reduction of R
 
@@ -86,10 +93,10 @@ int launch_smallm_fwd(const void* X, const float* lora_parts, float s, const uin
 
 // The whole projection backward for M <= 16 tokens (fl_smallm_bwd.cu): dX[M,K] =
 // dY . W + Us . Alora and, with rank > 0, dA, dB (+= when accumulate), Us / Ts =
-// bf16(s * the launch_lora_parts partials of dY . B over N / of X . A^T over K).
-// K % 512 == 0, N % 64 == 0 (N % 128 == 0 when rank > 0), layout 0.  With rank >
-// 0 the launch may overlap the preceding one, which must be the launch_lora_parts
-// that wrote the last partials (programmatic dependent launch).
+// bf16(s * the launch_lora_parts2 partials of X . A^T over K (job 0) and of dY . B
+// over N (job 1)).  K % 512 == 0, N % 64 == 0 (N % 128 == 0 when rank > 0),
+// layout 0.  With rank > 0 the launch may overlap the preceding one, which must be
+// that launch_lora_parts2 (programmatic dependent launch).
 int launch_smallm_bwd(const void* dY, const void* X, const float* uparts, const float* tparts, float s,
                       const uint8_t* codes, const float* scales, const float* lut, const float* alora, int rank,
                       void* dX, float* dA, float* dB, int accumulate, int M, int N, int K, cudaStream_t stream);

@@ -448,21 +448,39 @@ static int launch(const void* P, int M, int R, const float* q, int64_t q_sj, int
 }
 
 
-// Partial form for the small-M forward: CTA p takes the 128-wide piece p of the
-// reduction (exact FP32 sums in shared memory); the clusters of lora_parts_per_cluster(R)
+// One reduction of a lora_parts launch: P [M, R] bf16, Q(j, r) = q[j * q_sj + r * q_sr].
+struct PartsJob {
+  const __nv_bfloat16* P;
+  const float* q;
+  int64_t q_sj, q_sr;
+  float* parts;
+  int R;
+};
+
+// Partial form for the small-M forward and backward: CTA p takes the 128-wide piece p of the
+// reduction (exact FP32 sums in shared memory); the clusters of lora_parts_per_cluster(R0, R1)
 // CTAs add their pieces in rank order through distributed shared memory, and
 // cluster c writes parts[m][j][c] (j < rank; the partials of one output
 // contiguous) for the consumer to add in order.  One piece per CTA keeps every
 // CTA to a single round of loads, so the kernel finishes early even while the
 // frozen projection that follows (programmatic dependent launch) streams its
 // weights on the same SMs.
+// One launch runs one or two reductions: blocks [0, R0/128) take job 0, the
+// rest job 1 (clusters never straddle: csize divides both piece counts).
 __global__ void __launch_bounds__(kThreads)
-    lora_parts_kernel(const __nv_bfloat16* __restrict__ P, int M, int R, const float* __restrict__ q,
-                      int64_t q_sj, int64_t q_sr, int rank, float* __restrict__ parts, int csize) {
+    lora_parts_kernel(const PartsJob j0, const PartsJob j1, int M, int rank, int csize) {
   griddep_launch_dependents();
   __shared__ float mine[kMaxRows * 64];  // [m][j] of this CTA's piece
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * 128 + lane * 4;
+  const int pieces0 = j0.R / 128;
+  const bool second = static_cast<int>(blockIdx.x) >= pieces0;
+  const __nv_bfloat16* P = second ? j1.P : j0.P;
+  const float* q = second ? j1.q : j0.q;
+  const int64_t q_sj = second ? j1.q_sj : j0.q_sj, q_sr = second ? j1.q_sr : j0.q_sr;
+  float* parts = second ? j1.parts : j0.parts;
+  const int R = second ? j1.R : j0.R;
+  const int blk = second ? static_cast<int>(blockIdx.x) - pieces0 : static_cast<int>(blockIdx.x);
+  const int r = blk * 128 + lane * 4;
   uint2 xv[kMaxRows];
 #pragma unroll
   for (int m = 0; m < kMaxRows; ++m)
@@ -495,8 +513,8 @@ __global__ void __launch_bounds__(kThreads)
   cluster_sync();
   const int crank = static_cast<int>(cluster_ctarank());
   if (crank == 0) {
-    const int n_cl = gridDim.x / csize;
-    const int cl = blockIdx.x / csize;
+    const int n_cl = (R / 128) / csize;
+    const int cl = blk / csize;
     const uint32_t local = smem_u32(mine);
     for (int idx = threadIdx.x; idx < M * rank; idx += kThreads) {
       const int m = idx / rank, j = idx % rank;
@@ -512,16 +530,36 @@ __global__ void __launch_bounds__(kThreads)
 
 }  // namespace lds
 
-int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
-                      float* parts, cudaStream_t stream) {
-  if (R % 128 != 0 || M < 1 || M > lds::kMaxRows || rank < 1 || rank > 64)
-    return set_error(FL_ERR_ARG, "lora_parts: needs R %% 128 == 0, 1 <= M <= 16, 1 <= rank <= 64");
-  if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(parts)) & 15u ||
-      (q_sr == 1 && ((reinterpret_cast<uintptr_t>(q) & 15u) || q_sj % 4 != 0)))
-    return set_error(FL_ERR_ARG, "lora_parts: activations, factor and partials must be 16-byte aligned");
-  const int csize = lora_parts_per_cluster(R);
+static bool parts_job_ok(const void* P, int R, const float* q, int64_t q_sj, int64_t q_sr, const float* parts) {
+  if (R % 128 != 0 || R <= 0) return false;
+  if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(parts)) & 15u) return false;
+  if (q_sr == 1 && ((reinterpret_cast<uintptr_t>(q) & 15u) || q_sj % 4 != 0)) return false;
+  return true;
+}
+
+int lora_parts_per_cluster(int R0, int R1) {
+  auto one = [](int R) {
+    const int pieces = R / 128;
+    return pieces % 8 == 0 ? 8 : pieces % 4 == 0 ? 4 : pieces % 2 == 0 ? 2 : 1;
+  };
+  const int a = one(R0);
+  if (R1 <= 0) return a;
+  const int b = one(R1);
+  return a < b ? a : b;
+}
+
+int launch_lora_parts2(const void* P0, int R0, const float* q0, int64_t q0_sj, int64_t q0_sr, float* parts0,
+                       const void* P1, int R1, const float* q1, int64_t q1_sj, int64_t q1_sr, float* parts1, int M,
+                       int rank, cudaStream_t stream) {
+  if (M < 1 || M > lds::kMaxRows || rank < 1 || rank > 64)
+    return set_error(FL_ERR_ARG, "lora_parts: needs 1 <= M <= 16, 1 <= rank <= 64");
+  if (!parts_job_ok(P0, R0, q0, q0_sj, q0_sr, parts0) || (R1 > 0 && !parts_job_ok(P1, R1, q1, q1_sj, q1_sr, parts1)))
+    return set_error(FL_ERR_ARG, "lora_parts: needs R %% 128 == 0 and 16-byte aligned activations, factor, partials");
+  const int csize = lora_parts_per_cluster(R0, R1);
+  lds::PartsJob j0{static_cast<const __nv_bfloat16*>(P0), q0, q0_sj, q0_sr, parts0, R0};
+  lds::PartsJob j1{static_cast<const __nv_bfloat16*>(P1), q1, q1_sj, q1_sr, parts1, R1 > 0 ? R1 : 0};
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(R / 128);
+  cfg.gridDim = dim3(R0 / 128 + (R1 > 0 ? R1 / 128 : 0));
   cfg.blockDim = dim3(lds::kThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -531,15 +569,14 @@ int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, lds::lora_parts_kernel, static_cast<const __nv_bfloat16*>(P), M, R, q, q_sj,
-                                     q_sr, rank, parts, csize);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lds::lora_parts_kernel, j0, j1, M, rank, csize);
   if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_parts launch: %s", cudaGetErrorString(e));
   return FL_OK;
 }
 
-int lora_parts_per_cluster(int R) {
-  const int pieces = R / 128;
-  return pieces % 8 == 0 ? 8 : pieces % 4 == 0 ? 4 : pieces % 2 == 0 ? 2 : 1;
+int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
+                      float* parts, cudaStream_t stream) {
+  return launch_lora_parts2(P, R, q, q_sj, q_sr, parts, nullptr, 0, nullptr, 0, 1, nullptr, M, rank, stream);
 }
 
 int lora_nq(int rank) { return rank <= 16 ? 16 : rank <= 32 ? 32 : 64; }

@@ -374,8 +374,9 @@ int launch_smallm_bwd(const void* dY, const void* X, const float* uparts, const 
   a.X = static_cast<const __nv_bfloat16*>(X);
   a.uparts = uparts;
   a.tparts = tparts;
-  a.n_uparts = N / (128 * lora_parts_per_cluster(N));
-  a.n_tparts = K / (128 * lora_parts_per_cluster(K));
+  const int csize = lora_parts_per_cluster(K, N);  // the one launch_lora_parts2 made both with
+  a.n_uparts = N / (128 * csize);
+  a.n_tparts = K / (128 * csize);
   a.s = s;
   a.dA = dA;
   a.dB = dB;

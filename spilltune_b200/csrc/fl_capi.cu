@@ -139,8 +139,10 @@ static int fwd_impl(const char* who, int layout, const uint16_t* X, int64_t M, i
     rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, workspace, qc, st);
     if (rc) return rc;
   }
+  // Chain prepass -> lora_down -> GEMM: each waits for the previous grid only
+  // before it reads that grid's output (the GEMM: before its LoRA stage).
   return launch_fwd_gemm(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st,
-                         nullptr, nullptr, 1, 0, layout);
+                         nullptr, nullptr, 1, 0, layout, /*pdl=*/true);
 }
 
 static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N,
@@ -183,20 +185,36 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
     return launch_smallm_bwd(dY, X, uparts, tparts, scale, payload, scales, lut16, A, rank, dX, dA, dB, accumulate,
                              (int)M, (int)N, (int)K, st);
   }
+  // One chain of programmatic dependent launches after the gradient clears:
+  // prepass(B) -> lora_down(Us) -> prepass(A) -> lora_down(Ts) -> backward GEMM
+  // -> lora_grad(dA) -> lora_grad(dB).  Each kernel waits for the previous grid
+  // before reading what the chain produced; the gradient kernels start once the
+  // GEMM has seen Us and Ts complete and fill the SMs its last tiles leave idle.
+  if (rank > 0 && !accumulate) {
+    cudaError_t e = cudaMemsetAsync(dA, 0, static_cast<size_t>(rank) * K * sizeof(float), st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dB, 0, static_cast<size_t>(N) * rank * sizeof(float), st);
+    if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "%s: gradient clear: %s", who, cudaGetErrorString(e));
+  }
   if (rank > 0) {
     // Us = bf16(s * dY . B): Q(j, n) = B[n * rank + j]
     if ((rc = launch_lora_down(dY, (int)M, (int)N, B, 1, rank, rank, scale, us, qc_b, st))) return rc;
     // Ts = bf16(s * X . A^T): Q(j, k) = A[j * K + k]
-    if ((rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, qc_a, st))) return rc;
+    if ((rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, qc_a, st, nullptr, nullptr, 0, 0, 1,
+                               /*pdl=*/true)))
+      return rc;
   }
   if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, (int)M, (int)N, (int)K, status, st,
-                            nullptr, nullptr, 1, 0, layout)))
+                            nullptr, nullptr, 1, 0, layout, /*pdl=*/true)))
     return rc;
   if (rank > 0) {
     // dA[j, k] = sum_m Us[m, j] X[m, k]
-    if ((rc = launch_lora_grad(X, (int)M, (int)K, us, rank, dA, 1, K, accumulate, st))) return rc;
+    if ((rc = launch_lora_grad(X, (int)M, (int)K, us, rank, dA, 1, K, 1, st, nullptr, nullptr, 0, 0, 0,
+                               /*pdl=*/true)))
+      return rc;
     // dB[n, j] = sum_m dY[m, n] Ts[m, j]
-    if ((rc = launch_lora_grad(dY, (int)M, (int)N, ts, rank, dB, rank, 1, accumulate, st))) return rc;
+    if ((rc = launch_lora_grad(dY, (int)M, (int)N, ts, rank, dB, rank, 1, 1, st, nullptr, nullptr, 0, 0, 0,
+                               /*pdl=*/true)))
+      return rc;
   }
   return FL_OK;
 }

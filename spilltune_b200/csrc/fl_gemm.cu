@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (has_lora) tma_prefetch_desc(&tm_low);
       int g = 0;  // stage counter over all tiles of this pair
       bool ok = true;
+      bool ts_ready = false;
       for (int t = pair; t < n_tiles && ok; t += num_pairs) {
         const Tile tile = tile_at(args, t, num_w, num_m);
         const int l0 = tile.w_tile * (2 * kLanes) + static_cast<int>(crank) * kLanes;
@@ -213,11 +214,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(xs + s * kXBytes, &tm_act, r0, mh, &bars->full[s]);
             tma_load_2d(qs + s * kQBytes, &tm_code, r0 / 2, wrow0 + l0, &bars->full[s]);  // 128 rows x 32 B
           } else {
+            // Ts is the previous launch's output (lora_down, programmatic
+            // dependent launch): wait for that grid before the first read.
+            if (!ts_ready) {
+              griddep_wait();
+              ts_ready = true;
+            }
             mbar_arrive_expect_tx(&bars->full[s], kXBytes);
             tma_load_2d(xs + s * kXBytes, &tm_low, 0, mh, &bars->full[s]);
           }
         }
       }
+      // Finish no earlier than the previous launch (also on the abort path).
+      griddep_wait();
       // Drain: never leave the CTA with bulk copies still landing in its smem.
       for (int i = g > kStages ? g - kStages : 0; i < g; ++i) {
         const int s = i % kStages;
@@ -537,7 +546,7 @@ int resident_pairs(const void* kernel, int threads, int smem, int* pairs) {
 int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
                     const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles,
-                    int layout) {
+                    int layout, bool pdl) {
   if (layout != kLayoutG128 && layout != kLayoutNf4Dq64) return set_error(FL_ERR_ARG, "fwd gemm: unknown layout");
   if (layout != kLayoutG128 && tiles) return set_error(FL_ERR_UNSUPPORTED, "grouped launches use layout 0");
   CUtensorMap tm_act, tm_low, tm_code;
@@ -589,13 +598,15 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl && rank > 0 ? 2 : 1;
   cudaError_t le = layout == kLayoutG128
                        ? cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<kLayoutG128>, tm_act, tm_low, tm_code, tm_out, a)
                        : cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<kLayoutNf4Dq64>, tm_act, tm_low, tm_code, tm_out, a);

@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (has_lora) tma_prefetch_desc(&tm_us);
       int g = 0;
       bool ok = true;
+      bool us_ready = false;
       for (int t = pair; t < n_tiles && ok; t += num_pairs) {
         const Tile tile = tile_at(args, t, num_k, num_m);
         const int kb = tile.k_tile * 2 * kColHalf + static_cast<int>(crank) * kColHalf;
@@ -189,11 +190,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(as + s * kABytes, &tm_dy, n0, mh, &bars->full[s]);
             tma_load_2d(qs + s * kQBytes, &tm_code, kb / 2, wrow0 + n0, &bars->full[s]);
           } else {
+            // Us comes from an earlier launch of the call chain (programmatic
+            // dependent launch): wait for the previous grid, whose completion
+            // implies every earlier one's, before the first read.  Only then
+            // may the gradient kernels that read Us and Ts launch.
+            if (!us_ready) {
+              griddep_wait();
+              griddep_launch_dependents();
+              us_ready = true;
+            }
             mbar_arrive_expect_tx(&bars->full[s], kABytes);
             tma_load_2d(as + s * kABytes, &tm_us, 0, mh, &bars->full[s]);
           }
         }
       }
+      // Finish no earlier than the previous launch (also on the abort path).
+      griddep_wait();
       for (int i = g > kStages ? g - kStages : 0; i < g; ++i) {
         uint32_t dummy_abort = 0;
         mbar_wait(&bars->full[i % kStages], (i / kStages) & 1, &dummy_abort, args.status, kStatusTimeoutDrain);
@@ -403,7 +415,7 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles,
-                    int layout) {
+                    int layout, bool pdl) {
   using namespace bwd;
   if (layout != kLayoutG128 && layout != kLayoutNf4Dq64) return set_error(FL_ERR_ARG, "bwd gemm: unknown layout");
   if (layout != kLayoutG128 && tiles) return set_error(FL_ERR_UNSUPPORTED, "grouped launches use layout 0");
@@ -448,13 +460,15 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl && rank > 0 ? 2 : 1;
   cudaError_t le = layout == kLayoutG128
                        ? cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutG128>, tm_dy, tm_us, tm_code, a)
                        : cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutNf4Dq64>, tm_dy, tm_us, tm_code, a);

@@ -12,14 +12,22 @@ int set_error(int code, const char* fmt, ...);
 
 uint32_t* status_word(int device);  // device status word of the calling device
 
-// Y[M,N] = X . W^T + Ts . Blora^T (fl_gemm.cu).
+// Call chains.  `pdl` launches a kernel as a programmatic dependent of the
+// previous launch of the stream, which must be the chain's producer of the
+// operand named below; every kernel that can be so launched waits for the
+// previous grid before it reads that operand and again before it exits, so a
+// chain's completion stays ordered.  Inputs written before the chain's first
+// (ordinary) launch are read without waiting.
+//
+// Y[M,N] = X . W^T + Ts . Blora^T (fl_gemm.cu).  pdl: Ts is the previous
+// launch's (lora_down) output.
 // Grouped (MoE) form: `tiles`/`tile_count` from launch_moe_plan, the weight a
 // stacked [experts, N, K] record, blora [experts, N, rank]; grid sized for
 // `max_tiles`.  tiles == nullptr: one weight, experts = 1.
 int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
                     const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
-                    int experts = 1, int max_tiles = 0, int layout = 0);
+                    int experts = 1, int max_tiles = 0, int layout = 0, bool pdl = false);
 
 // 2-CTA clusters of `kernel` that can be resident at once on the current
 // device (also raises the kernel's dynamic shared-memory limit to `smem`).
@@ -34,11 +42,13 @@ int launch_moe_plan(const int* seg, int experts, int total_rows, int rows, int c
                     int max_tiles, int* count, uint32_t* status, cudaStream_t stream);
 int moe_max_tiles(int total_rows, int experts, int rows, int col_tiles);
 
-// dX[M,K] = dY . W + Us . Alora (fl_gemm_bwd.cu).
+// dX[M,K] = dY . W + Us . Alora (fl_gemm_bwd.cu).  pdl: Us comes from the chain
+// (the previous launch completes after it); dependents are released only once
+// Us and Ts are complete (the gradient kernels read them without waiting).
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
-                    int experts = 1, int max_tiles = 0, int layout = 0);
+                    int experts = 1, int max_tiles = 0, int layout = 0, bool pdl = false);
 
 int launch_dequant(const uint8_t* payload, const float* scales, const float* lut, int64_t numel, void* out,
                    cudaStream_t stream, int layout = 0);
@@ -51,10 +61,13 @@ int launch_nf4dq_prologue(const uint8_t* absmax_q, const float* nested_absmax, c
 // rank) per expert, 16-byte aligned (the converted factor).
 // Grouped (MoE) form: 128-row tiles over expert-sorted rows, the factor of tile
 // t at q + tiles[t].x * q_expert_stride, `experts` factors converted.
+// Two launches: the factor prepass, then the projection as its programmatic
+// dependent.  pdl: the prepass is itself a dependent of the previous launch
+// (it reads only q, written before the chain).
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
                      float s, void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles = nullptr,
                      const int* tile_count = nullptr, int max_tiles = 0, int64_t q_expert_stride = 0,
-                     int experts = 1);
+                     int experts = 1, bool pdl = false);
 // Small-M form (M <= 16): parts[m][j][c] (j < rank) = sum of P[m, r] * Q(j, r),
 // Q(j, r) = q[j * q_sj + r * q_sr], over the 128 * lora_parts_per_cluster(R)
 // columns of partial c, exact FP32 (parts: M * 64 * R / (128 * per_cluster)
@@ -78,10 +91,12 @@ size_t lora_factor_bytes(int64_t R, int rank);   // converted-factor scratch for
 // Grouped (MoE) form: token slices {expert, first row, end row, 0} over
 // expert-sorted rows; slice t accumulates into out + tiles[t].x * out_expert_stride
 // (out then holds all experts: `out_total` floats are cleared when !accumulate).
+// pdl: launched after the backward GEMM or another lora_grad of the chain (P and
+// Q complete; a chain clears `out` before its first launch).
 int launch_lora_grad(const void* P, int M, int Pdim, const void* Q, int rank, float* out, int64_t o_sp,
                      int64_t o_sj, int accumulate, cudaStream_t stream, const int4* tiles = nullptr,
                      const int* tile_count = nullptr, int max_tiles = 0, int64_t out_expert_stride = 0,
-                     int64_t out_total = 0);
+                     int64_t out_total = 0, bool pdl = false);
 
 // Y[M,N] for M <= 16 tokens (fl_smallm.cu); K % 512 == 0, layout 0.  With rank > 0 the
 // LoRA term uses Ts = bf16(s * sum of the K/128 pieces of lora_parts), and the

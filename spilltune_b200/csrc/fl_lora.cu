@@ -47,6 +47,10 @@ __global__ void __launch_bounds__(kThreads)
                      float* __restrict__ out, int64_t o_sp, int64_t o_sj, int rank, int M, int Pdim,
                      int m_per_cta, const int4* __restrict__ tiles, const int* __restrict__ tile_count,
                      int64_t out_expert_stride, uint32_t* status) {
+  // Launched as a dependent of the backward GEMM (programmatic dependent
+  // launch), which lets it start only once Us and Ts are complete: the next
+  // gradient kernel may start at once too.
+  griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ps = smem;                          // kStages x 16 KiB
@@ -170,6 +174,8 @@ __global__ void __launch_bounds__(kThreads)
       tc_fence_before();
     }
   }
+  // Finish no earlier than the previous launch, so completion stays ordered.
+  griddep_wait();
   __syncthreads();
   if (warp == 1) {
     __syncwarp();
@@ -185,7 +191,7 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 
 int launch_lora_grad(const void* P, int M, int Pdim, const void* Q, int rank, float* out, int64_t o_sp,
                      int64_t o_sj, int accumulate, cudaStream_t stream, const int4* tiles, const int* tile_count,
-                     int max_tiles, int64_t out_expert_stride, int64_t out_total) {
+                     int max_tiles, int64_t out_expert_stride, int64_t out_total, bool pdl) {
   using namespace lg;
   if (Pdim % 64 != 0) return set_error(FL_ERR_ARG, "lora_grad: dim %d not a multiple of 64", Pdim);
   if (!accumulate) {
@@ -229,9 +235,18 @@ int launch_lora_grad(const void* P, int M, int Pdim, const void* Q, int rank, fl
     slices = (M + m_per_cta - 1) / m_per_cta;
   }
   if (slices < 1) return FL_OK;
-  lora_grad_kernel<<<dim3(ptiles, slices), kThreads, kSmemBytes, stream>>>(
-      tm_p, tm_q, out, o_sp, o_sj, rank, M, Pdim, m_per_cta, tiles, tile_count, out_expert_stride, status_word(dev));
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ptiles, slices);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, lora_grad_kernel, tm_p, tm_q, out, o_sp, o_sj, rank, M, Pdim, m_per_cta,
+                                     tiles, tile_count, out_expert_stride, status_word(dev));
   if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_grad launch: %s", cudaGetErrorString(e));
   return FL_OK;
 }

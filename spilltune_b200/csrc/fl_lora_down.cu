@@ -68,6 +68,9 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
 // One thread per (e, j, 8 consecutive r).
 __global__ void prep_kernel(const float* __restrict__ q, int64_t q_sj, int64_t q_sr, int64_t q_es, int rank, int R,
                             int nq, int experts, __nv_bfloat16* __restrict__ qc) {
+  // lora_down follows at once (programmatic dependent launch) and starts
+  // streaming its activations; it waits for this grid before reading qc.
+  griddep_launch_dependents();
   const int r8s = R / 8;
   const int64_t total = static_cast<int64_t>(experts) * nq * r8s;
   const int64_t plane = static_cast<int64_t>(nq) * R;
@@ -106,6 +109,9 @@ __global__ void prep_kernel(const float* __restrict__ q, int64_t q_sj, int64_t q
     *reinterpret_cast<uint4*>(base + off) = make_uint4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<uint4*>(base + plane + off) = make_uint4(l[0], l[1], l[2], l[3]);
   }
+  // Launched as a dependent itself (the second factor of a backward): finish
+  // no earlier than the launch before, so completion stays ordered.
+  griddep_wait();
 }
 
 __device__ __forceinline__ uint32_t word(const uint4& a, const uint4& b, int w) {
@@ -172,17 +178,26 @@ __global__ void __launch_bounds__(kThreads)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_p);
+      // The activations of the first ring's worth of units go out at once; the
+      // converted factor is the previous launch's output (programmatic
+      // dependent launch of the prepass): wait for that grid before reading it.
+      const int pre = n_units < kStages ? n_units : kStages;
+      for (int k = 0; k < pre; ++k) {
+        mbar_arrive_expect_tx(&full[k], C::kStage);
+        tma_load_2d(smem + k * C::kStage, &tm_p, (u0 + k) * 64, m0, &full[k]);
+      }
+      griddep_wait();
       int issued = 0;
       for (int k = 0; k < n_units; ++k) {
         const int st = k % kStages;
-        if (k >= kStages &&
-            !mbar_wait_short(&empty[st], ((k / kStages) - 1) & 1, abort_word, status, kStatusTimeoutEmpty))
-          break;
         const int u = u0 + k;
         uint8_t* stage = smem + st * C::kStage;
         const __nv_bfloat16* qsrc = qc + static_cast<int64_t>(u) * NQ * 64;
-        mbar_arrive_expect_tx(&full[st], C::kStage);
-        tma_load_2d(stage, &tm_p, u * 64, m0, &full[st]);
+        if (k >= pre) {
+          if (!mbar_wait_short(&empty[st], ((k / kStages) - 1) & 1, abort_word, status, kStatusTimeoutEmpty)) break;
+          mbar_arrive_expect_tx(&full[st], C::kStage);
+          tma_load_2d(stage, &tm_p, u * 64, m0, &full[st]);
+        }
         bulk_load(stage + kXBytes, qsrc, C::kQPlane, &full[st]);
         bulk_load(stage + kXBytes + C::kQPlane, qsrc + plane, C::kQPlane, &full[st]);
         ++issued;
@@ -326,13 +341,17 @@ static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  // A programmatic dependent of the prepass that converted qc (the launch
+  // just before it): the producer waits for that grid before reading qc.
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = split;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   CUtensorMap tm;
   int rc = make_tensor_map_2d(&tm, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, R, M, static_cast<uint64_t>(R) * 2, 64,
                               kRows, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -585,7 +604,7 @@ size_t lora_factor_bytes(int64_t R, int rank) { return 4u * static_cast<size_t>(
 
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank, float s,
                      void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles, const int* tile_count,
-                     int max_tiles, int64_t q_expert_stride, int experts) {
+                     int max_tiles, int64_t q_expert_stride, int experts, bool pdl) {
   if (R % 128 != 0) return set_error(FL_ERR_ARG, "lora_down: reduction dim %d not a multiple of 128", R);
   if (rank < 1 || rank > 64) return set_error(FL_ERR_ARG, "lora_down: rank %d outside [1, 64]", rank);
   if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(out64) |
@@ -601,8 +620,16 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
     const int threads = 256;
     const int64_t want = (total + threads - 1) / threads;
     const int grid = static_cast<int>(want < 4096 ? want : 4096);
-    ld::prep_kernel<<<grid, threads, 0, stream>>>(q, q_sj, q_sr, q_expert_stride, rank, R, nq, experts, qc);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, ld::prep_kernel, q, q_sj, q_sr, q_expert_stride, rank, R, nq, experts, qc);
     if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down prepass: %s", cudaGetErrorString(e));
   }
   const int64_t qc_es = 2 * static_cast<int64_t>(nq) * R;

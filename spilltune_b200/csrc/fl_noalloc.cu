@@ -99,5 +99,6 @@ extern "C" int fl_fwd_noalloc(const uint16_t* X, int64_t M, int64_t K, const uin
     const int rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, ts + kNoAllocScratchBytes, st);
     if (rc) return rc;
   }
-  return launch_fwd_gemm(X, ts, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st);
+  return launch_fwd_gemm(X, ts, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st, nullptr,
+                         nullptr, 1, 0, 0, /*pdl=*/true);
 }

@@ -194,17 +194,18 @@ class Step:
         self.events = []
         self.launches = 0
 
-    def _fwd(self, x, w, A, B, name):
+    def _fwd(self, x, w, A, B, name, return_ts=False):
         if self.record and name == self.timed_name:
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
-            y = self.ops.fwd(x, w, A, B, self.scale)
+            out = self.ops.fwd(x, w, A, B, self.scale, return_ts=return_ts)
             e.record()
             self.events.append((s, e))
         else:
-            y = self.ops.fwd(x, w, A, B, self.scale)
-        self.launches += 2
-        return y
+            out = self.ops.fwd(x, w, A, B, self.scale, return_ts=return_ts)
+        # Kernels of one fl_fwd call at these sizes: factor prepass, lora_down, GEMM.
+        self.launches += 3
+        return out
 
     def __call__(self):
         L = len(self.loras)
@@ -221,9 +222,12 @@ class Step:
             with self.weights_for(l, "backward") as W:
                 for name, _N, _K, src in reversed(PROJ):
                     A, B = self.loras[l][name]
-                    self._fwd(x[src], W[name], A, B, name)  # recompute
+                    # Recompute; the backward reuses its Ts = bf16(s * x . A^T)
+                    # as the reference's autograd reuses F.linear(x, A).
+                    _y, ts = self._fwd(x[src], W[name], A, B, name, return_ts=True)
                     self.ops.bwd(dy[name], x[src], W[name], A, B, self.scale, dA=A.grad, dB=B.grad,
-                                 accumulate=False)
+                                 accumulate=False, ts=ts)
+                    # prepass(B), lora_down(Us), backward GEMM, lora_grad x 2
                     self.launches += 5
             # Data parallel: this layer's LoRA gradients are final; all-reduce
             # them on a side stream while the next layer recomputes.

@@ -107,6 +107,24 @@ int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t 
            void* stream);
 
 /*
+ * fl_bwd given the forward's low-rank activations Ts = bf16(scale * X . A^T)
+ * ([M, 64] bf16, 128-byte rows, zero past the rank), the intermediate the
+ * reference's autograd keeps from the recomputed forward for grad_B
+ * (F.linear(F.linear(x, A), B) in finetune/lora.py:219-220; its backward in
+ * training/recompute.py:102-127).  fl_fwd leaves exactly these bytes in the
+ * first M * 128 bytes of its workspace whenever this function reads them, so
+ * the results equal fl_bwd's bit for bit while X . A^T is not recomputed.
+ * Ts is not read when rank == 0, or when M <= 16 with K % 512 == 0 and the
+ * group-128 layout (the decode-step kernels, which form Ts themselves); it may
+ * then be NULL, as it may always be (then this is fl_bwd).  Ts must be 16-byte
+ * aligned.  Other arguments and the workspace as fl_bwd.
+ */
+int fl_bwd_ts(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* payload,
+              const float* scales, const float* lut16, const float* A, const float* B, int rank, float scale,
+              const uint16_t* Ts, uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace,
+              size_t workspace_bytes, void* stream);
+
+/*
  * Same result as fl_fwd, for callers that cannot allocate device memory at
  * call time (a host binding without a device allocator, a trainer whose
  * device budget is fixed up front).  No counterpart in the reference.  It

@@ -111,6 +111,12 @@ static int check_common(const char* who, int64_t M, int64_t N, int64_t K, int ra
 }  // extern "C"
 
 // Forward / backward bodies shared by the two record layouts.
+// The decode-step (small-M) kernels take the call: fl_fwd then leaves LoRA
+// partial sums, not Ts, in its workspace, and fl_bwd_ts does not read Ts.
+static bool small_m_path(int layout, int64_t M, int64_t K) {
+  return layout == kLayoutG128 && M <= 16 && K % 512 == 0;
+}
+
 static int fwd_impl(const char* who, int layout, const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload,
                     const float* scales, const float* lut16, int64_t N, const float* A, const float* B, int rank,
                     float scale, uint16_t* Y, void* workspace, size_t workspace_bytes, void* stream) {
@@ -130,7 +136,7 @@ static int fwd_impl(const char* who, int layout, const uint16_t* X, int64_t M, i
   // Decode-like steps (M <= 16) are bound by the weight bytes: dedicated kernel
   // (it streams 512-wide column chunks; other K take the tile GEMM).  Its LoRA
   // partial sums use the converted-factor scratch (M * 64 * K/128 floats fit).
-  if (layout == kLayoutG128 && M <= 16 && K % 512 == 0) {
+  if (small_m_path(layout, M, K)) {
     float* parts = static_cast<float*>(qc);
     if (rank > 0 && (rc = launch_lora_parts(X, (int)M, (int)K, A, K, 1, rank, parts, st))) return rc;
     return launch_smallm_fwd(X, parts, scale, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, st, layout);
@@ -148,7 +154,7 @@ static int fwd_impl(const char* who, int layout, const uint16_t* X, int64_t M, i
 static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N,
                     int64_t K, const uint8_t* payload, const float* scales, const float* lut16, const float* A,
                     const float* B, int rank, float scale, uint16_t* dX, float* dA, float* dB, int accumulate,
-                    void* workspace, size_t workspace_bytes, void* stream) {
+                    void* workspace, size_t workspace_bytes, void* stream, const uint16_t* ts_in = nullptr) {
   int rc = check_common(who, M, N, K, rank, payload, scales, lut16);
   if (rc) return rc;
   if (N % 64 != 0) return set_error(FL_ERR_ARG, "%s: out_features N=%lld must be a multiple of 64", who, (long long)N);
@@ -173,7 +179,7 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
   // Decode-like steps (M <= 16) take the small-M backward, which also finishes
   // the LoRA gradients; the tile GEMM's 256-token tiles would leave most SMs
   // idle.  Its low-rank partials use the converted-factor scratch.
-  if (layout == kLayoutG128 && M <= 16 && K % 512 == 0) {
+  if (small_m_path(layout, M, K)) {
     float* uparts = reinterpret_cast<float*>(qc_b);
     float* tparts = reinterpret_cast<float*>(qc_a);
     if (rank > 0) {
@@ -186,10 +192,15 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
                              (int)M, (int)N, (int)K, st);
   }
   // One chain of programmatic dependent launches after the gradient clears:
-  // prepass(B) -> lora_down(Us) -> prepass(A) -> lora_down(Ts) -> backward GEMM
-  // -> lora_grad(dA) -> lora_grad(dB).  Each kernel waits for the previous grid
+  // prepass(B) -> lora_down(Us) -> [prepass(A) -> lora_down(Ts), unless the
+  // caller passed the forward's Ts] -> backward GEMM -> lora_grad(dA) ->
+  // lora_grad(dB).  Each kernel waits for the previous grid
   // before reading what the chain produced; the gradient kernels start once the
   // GEMM has seen Us and Ts complete and fill the SMs its last tiles leave idle.
+  if (rank > 0 && ts_in != nullptr) {
+    if (!aligned16(ts_in)) return set_error(FL_ERR_ARG, "%s: Ts must be 16-byte aligned", who);
+    ts = reinterpret_cast<uint8_t*>(const_cast<uint16_t*>(ts_in));  // read only
+  }
   if (rank > 0 && !accumulate) {
     cudaError_t e = cudaMemsetAsync(dA, 0, static_cast<size_t>(rank) * K * sizeof(float), st);
     if (e == cudaSuccess) e = cudaMemsetAsync(dB, 0, static_cast<size_t>(N) * rank * sizeof(float), st);
@@ -198,8 +209,10 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
   if (rank > 0) {
     // Us = bf16(s * dY . B): Q(j, n) = B[n * rank + j]
     if ((rc = launch_lora_down(dY, (int)M, (int)N, B, 1, rank, rank, scale, us, qc_b, st))) return rc;
-    // Ts = bf16(s * X . A^T): Q(j, k) = A[j * K + k]
-    if ((rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, qc_a, st, nullptr, nullptr, 0, 0, 1,
+    // Ts = bf16(s * X . A^T): Q(j, k) = A[j * K + k], unless the caller kept
+    // the forward's.
+    if (ts_in == nullptr &&
+        (rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, qc_a, st, nullptr, nullptr, 0, 0, 1,
                                /*pdl=*/true)))
       return rc;
   }
@@ -255,6 +268,14 @@ int fl_dequant_nf4dq(const uint8_t* packed, const float* block_scales, const flo
   if (!packed || !block_scales || !quant_map || !out_bf16) return set_error(FL_ERR_ARG, "fl_dequant_nf4dq: null pointer");
   return launch_dequant(packed, block_scales, quant_map, numel, out_bf16, static_cast<cudaStream_t>(stream),
                         kLayoutNf4Dq64);
+}
+
+int fl_bwd_ts(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* payload,
+              const float* scales, const float* lut16, const float* A, const float* B, int rank, float scale,
+              const uint16_t* Ts, uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  return bwd_impl("fl_bwd_ts", kLayoutG128, dY, X, M, N, K, payload, scales, lut16, A, B, rank, scale, dX, dA, dB,
+                  accumulate, workspace, workspace_bytes, stream, Ts);
 }
 
 int fl_fwd_nf4dq(const uint16_t* X, int64_t M, int64_t K, const uint8_t* packed, const float* block_scales,

@@ -136,7 +136,7 @@ template <int kLayout>
 __global__ void __launch_bounds__(kThreads, 1)
     fl_tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,   // X, [M, K] bf16, box {64, 128}
                       const __grid_constant__ CUtensorMap tm_low,   // Ts, [M, 64] bf16, box {64, 128}
-                      const __grid_constant__ CUtensorMap tm_code,  // payload [E*N, K/2] u8
+                      const __grid_constant__ CUtensorMap tm_code,  // payload [E*N, K/2] u8, box {32, 128}, 32B swizzle
                       const __grid_constant__ CUtensorMap tm_out,   // Y [M, N] bf16, box {128, 256}
                       const GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -408,8 +408,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t v[32];
             if (it < n_main) {
               if constexpr (kBlock64) table = make_table(lut_s, it == pit ? sc_a : sc_b);
-              const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + row * 32);
-              const uint4 q0 = q[0], q1 = q[1];
+              // Row chunk c sits at chunk c ^ ((row >> 2) & 1) (32-byte swizzle):
+              // eight consecutive rows then read distinct banks.
+              const uint8_t* qrow = qs + s * kQBytes + row * 32;
+              const uint32_t sw = (row >> 2) & 1;
+              const uint4 q0 = *reinterpret_cast<const uint4*>(qrow + (sw << 4));
+              const uint4 q1 = *reinterpret_cast<const uint4*>(qrow + ((1u ^ sw) << 4));
               lookup8_l<kLayout>(table, q0.x, v + 0);
               lookup8_l<kLayout>(table, q0.y, v + 4);
               lookup8_l<kLayout>(table, q0.z, v + 8);
@@ -561,7 +565,7 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
     tm_low = tm_act;
   }
   rc = make_tensor_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, static_cast<uint64_t>(N) * experts,
-                          K / 2, 32, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+                          K / 2, 32, 128, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
   // Output tiles leave by TMA when the row pitch and base allow it.
   const bool tma_store = (N % 8) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;

@@ -115,7 +115,7 @@ template <int kLayout>
 __global__ void __launch_bounds__(kThreads, 1)
     fl_bwd_ss_kernel(const __grid_constant__ CUtensorMap tm_dy,    // dY [M, N] bf16, box {64, 128}
                      const __grid_constant__ CUtensorMap tm_us,    // Us [M, 64] bf16, box {64, 128}
-                     const __grid_constant__ CUtensorMap tm_code,  // payload [E*N, K/2] u8, box {64, 64}
+                     const __grid_constant__ CUtensorMap tm_code,  // payload [E*N, K/2] u8, box {64, 64}, 64B swizzle
                      const Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -254,9 +254,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ decode warps
     const int dw = warp - 2;
     const int grp = dw >> 2;                 // stage-pair group
-    const int t = (dw & 3) * 32 + lane;      // 0..127 within the group
-    const int r = t >> 1;                    // reduction row within the stage (0..63)
-    const int khalf = t & 1;                 // which 64 of the CTA's 128 columns
+    // Lanes 0-15 take 16 rows' first 64 columns, lanes 16-31 the same rows'
+    // second 64: the eight lanes of a 16-byte shared-memory phase then hold eight
+    // consecutive rows, whose swizzled chunks (decoded B rows, codes) fall on
+    // distinct banks.
+    const int r = (dw & 3) * 16 + (lane & 15);  // reduction row within the stage (0..63)
+    const int khalf = lane >> 4;                // which 64 of the CTA's 128 columns
     const uint32_t afull_leader = mapa_shared(smem_u32(&bars->afull[0]), 0);
     const uint32_t acc_empty_leader = mapa_shared(smem_u32(&bars->acc_empty[0]), 0);
     const int quarter = warp & 3;
@@ -344,8 +347,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
                 break;
               }
-              const uint4* q = reinterpret_cast<const uint4*>(qs + s * kQBytes + r * 64 + khalf * 32);
-              const uint4 q0 = q[0], q1 = q[1];
+              // Row r's 16-byte chunk c sits at chunk c ^ ((r >> 1) & 3) (64-byte swizzle).
+              const uint8_t* qrow = qs + s * kQBytes + r * 64;
+              const uint32_t sw = (r >> 1) & 3;
+              const uint4 q0 = *reinterpret_cast<const uint4*>(qrow + (((2 * khalf) ^ sw) << 4));
+              const uint4 q1 = *reinterpret_cast<const uint4*>(qrow + (((2 * khalf + 1) ^ sw) << 4));
               lookup8_l<kLayout>(table, q0.x, v + 0);
               lookup8_l<kLayout>(table, q0.y, v + 4);
               lookup8_l<kLayout>(table, q0.z, v + 8);
@@ -433,7 +439,7 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
     tm_us = tm_dy;
   }
   rc = make_tensor_map_2d(&tm_code, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, static_cast<uint64_t>(N) * experts,
-                          K / 2, kColHalf / 2, kStageN, CU_TENSOR_MAP_SWIZZLE_NONE);
+                          K / 2, kColHalf / 2, kStageN, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
   Args a;
   a.scales = scales;

@@ -60,8 +60,15 @@ def _matrix_shape(weight: PackedWeight):
     return weight.shape
 
 
-def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0):
-    """Y = x . W^T + scale * (x . A^T) . B^T  (bf16 out; plain frozen linear if A is None)."""
+def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0, return_ts=False):
+    """Y = x . W^T + scale * (x . A^T) . B^T  (bf16 out; plain frozen linear if A is None).
+
+    return_ts: also return Ts = bf16(scale * x . A^T) ([tokens, 64] bf16, zero past
+    the rank) as a view of the call's workspace, for ``bwd(..., ts=)`` -- the
+    intermediate the reference's autograd keeps from the forward for grad_B
+    (finetune/lora.py:219-220).  None when rank == 0 or when the decode-step
+    kernels take the call (<= 16 tokens, K % 512 == 0: they form Ts themselves).
+    """
     N, K = _matrix_shape(weight)
     x2 = _flat(x, K)
     rank = 0 if A is None else A.shape[0]
@@ -79,11 +86,20 @@ def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0):
     if M:
         _lib.call("fl_fwd", _ptr(x2), M, K, _ptr(weight.payload), _ptr(weight.scales), _ptr(weight.lut), N,
                   _ptr(A), _ptr(B), rank, float(scale), _ptr(y), _ptr(ws), ws_bytes, _stream())
-    return y.view(*x.shape[:-1], N)
+    y = y.view(*x.shape[:-1], N)
+    if not return_ts:
+        return y
+    # fl_fwd leaves Ts in the first M * 128 bytes of its workspace except on the
+    # decode-step path (the rule fl_bwd_ts documents).
+    keeps_ts = rank > 0 and M > 0 and not (M <= 16 and K % 512 == 0)
+    return y, (ws[:M * 128].view(torch.bfloat16).view(M, 64) if keeps_ts else None)
 
 
-def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False):
-    """Returns (dX, dA, dB) of fwd(); dA/dB are fp32 (accumulated into when given and accumulate)."""
+def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False, ts=None):
+    """Returns (dX, dA, dB) of fwd(); dA/dB are fp32 (accumulated into when given and accumulate).
+
+    ts: the Ts that ``fwd(..., return_ts=True)`` returned for the same x, A and
+    scale; X . A^T is then not recomputed (results identical)."""
     N, K = _matrix_shape(weight)
     dy2 = _flat(dy, N)
     rank = 0 if A is None else A.shape[0]
@@ -102,7 +118,15 @@ def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None
             accumulate = False
     ws_bytes = _lib.load().fl_bwd_workspace_bytes(M, N, K, rank)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dy2.device) if ws_bytes else None
-    if M:
+    if ts is not None and rank:
+        if ts.dtype != torch.bfloat16 or tuple(ts.shape) != (M, 64) or not ts.is_contiguous():
+            raise ValueError("ts must be the [tokens, 64] bf16 Ts that fwd(..., return_ts=True) returned")
+        _need_cuda(ts)
+    if M and ts is not None and rank:
+        _lib.call("fl_bwd_ts", _ptr(dy2), _ptr(x2), M, N, K, _ptr(weight.payload), _ptr(weight.scales),
+                  _ptr(weight.lut), _ptr(A), _ptr(B), rank, float(scale), _ptr(ts), _ptr(dx), _ptr(dA),
+                  _ptr(dB), int(bool(accumulate)), _ptr(ws), ws_bytes, _stream())
+    elif M:
         _lib.call("fl_bwd", _ptr(dy2), _ptr(x2), M, N, K, _ptr(weight.payload), _ptr(weight.scales),
                   _ptr(weight.lut), _ptr(A), _ptr(B), rank, float(scale), _ptr(dx), _ptr(dA), _ptr(dB),
                   int(bool(accumulate)), _ptr(ws), ws_bytes, _stream())
@@ -124,13 +148,19 @@ class FrozenLoRALinear(torch.autograd.Function):
             ctx.save_for_backward(x, A, B)
         else:
             ctx.save_for_backward(x)
-        return fwd(x, weight, A, B, scale)
+        if not ctx.has_lora:
+            return fwd(x, weight)
+        # Keep Ts = bf16(scale * x . A^T) for the backward, as the reference's
+        # autograd keeps F.linear(x, A) for grad_B.
+        y, ctx.ts = fwd(x, weight, A, B, scale, return_ts=True)
+        return y
 
     @staticmethod
     def backward(ctx, dy):
         if ctx.has_lora:
             x, A, B = ctx.saved_tensors
-            dx, dA, dB = bwd(dy.contiguous(), x, ctx.weight, A, B, ctx.scale)
+            dx, dA, dB = bwd(dy.contiguous(), x, ctx.weight, A, B, ctx.scale, ts=ctx.ts)
+            ctx.ts = None
             return dx, dA, dB, None, None
         (x,) = ctx.saved_tensors
         dx, _, _ = bwd(dy.contiguous(), x, ctx.weight)

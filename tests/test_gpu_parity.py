@@ -164,6 +164,32 @@ def test_bwd_accumulate(cuda_lib):
     assert ol.rel_l2(dA.cpu(), dA1.cpu()) < 1e-6
 
 
+@pytest.mark.parametrize("M,N,K,rank", [(512, 1024, 4096, 16), (300, 384, 256, 8), (3, 640, 384, 4),
+                                         (16, 512, 1024, 16)])
+def test_bwd_with_forward_ts_matches_bwd(cuda_lib, M, N, K, rank):
+    """fl_bwd_ts given the forward's Ts gives fl_bwd's results: dX bit for bit, dA
+    and dB up to the order of the gradient kernels' atomic adds.  The last shape
+    takes the decode-step kernels, where the forward keeps no Ts."""
+    from spilltune_b200 import ops
+    s = 2.0
+    pw, x, A, B, dy = _problem(M, N, K, rank, "nf4-g128", seed=21)
+    pw, x, A, B, dy = pw.to("cuda"), x.cuda(), A.cuda(), B.cuda(), dy.cuda()
+    y, ts = ops.fwd(x, pw, A, B, s, return_ts=True)
+    assert torch.equal(y, ops.fwd(x, pw, A, B, s))
+    if M <= 16 and K % 512 == 0:
+        assert ts is None
+    else:
+        # Ts = bf16(s * x . A^T) against FP32 (one bf16 rounding), zero past the rank.
+        ref = s * x.float().cpu() @ A.cpu().t()
+        assert ol.rel_l2(ts[:, :rank].float().cpu(), ref) <= TIGHT
+        assert int(ts[:, rank:].count_nonzero()) == 0
+    dx0, dA0, dB0 = ops.bwd(dy, x, pw, A, B, s)
+    dx1, dA1, dB1 = ops.bwd(dy, x, pw, A, B, s, ts=ts)
+    torch.cuda.synchronize()
+    assert torch.equal(dx0, dx1)
+    assert ol.rel_l2(dA1.cpu(), dA0.cpu()) < 1e-6 and ol.rel_l2(dB1.cpu(), dB0.cpu()) < 1e-6
+
+
 def test_reference_golden_through_cuda_path(cuda_lib):
     """LoRAProjection.forward + autograd produced by the reference itself."""
     from spilltune_b200 import codec, ops

@@ -318,15 +318,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr bool kBlock64 = kLayout == kLayoutNf4Dq64;
       const int spr = kBlock64 ? 2 * groups_per_row : groups_per_row;
       const int gsc = tile_valid ? (kBlock64 ? kb / 64 + khalf : kb / 128) : 0;
-      // The row's scale for the next stage this group owns is loaded one owned
-      // stage ahead (stages 2g, 2g+1, 2g+2*kGroups, ...).
+      // The row's scales for the group's next stage pair (stages 2g, 2g+1,
+      // 2g+2*kGroups, ...) are loaded when the current pair starts: a whole
+      // rotation of the groups ahead, so the gather has landed when used.
       auto load_scale = [&](int it) {
         return (tile_valid && it < n_main)
                    ? __ldg(args.scales + static_cast<size_t>(wrow0 + it * kStageN + r) * spr + gsc)
                    : 0.0f;
       };
-      float next_scale = load_scale(2 * grp);
+      float next0 = load_scale(2 * grp), next1 = load_scale(2 * grp + 1);
       for (int pit = 2 * grp; pit < n_iter || (pit == 2 * grp && tl > 0); pit += 2 * kGroups) {
+        const float pair_scale[2] = {next0, next1};
+        next0 = load_scale(pit + 2 * kGroups);
+        next1 = load_scale(pit + 2 * kGroups + 1);
         if (pit < n_iter && ok) {
           for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
             const int gi = g0 + it;
@@ -339,8 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             uint32_t v[32];
-            const float scale = next_scale;
-            next_scale = load_scale((it & 1) == 0 ? it + 1 : it + 2 * kGroups - 1);
+            const float scale = pair_scale[it - pit];
             if (it < n_main) {
               const ProductTable table = make_table(bars->lut, scale);
               if (!mbar_wait_warp(&bars->full[s], ph, abort_word, args.status, kStatusTimeoutFull)) {

@@ -168,6 +168,7 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
     if (!aligned16(X)) return set_error(FL_ERR_ARG, "%s: X must be 16-byte aligned", who);
     if (!workspace || workspace_bytes < fl_bwd_workspace_bytes(M, N, K, rank) || !aligned16(workspace))
       return set_error(FL_ERR_ARG, "%s: workspace missing, short or misaligned", who);
+    if (ts_in != nullptr && !aligned16(ts_in)) return set_error(FL_ERR_ARG, "%s: Ts must be 16-byte aligned", who);
   }
   uint32_t* status = nullptr;
   if ((rc = current_status(&status))) return rc;
@@ -197,10 +198,7 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
   // lora_grad(dB).  Each kernel waits for the previous grid
   // before reading what the chain produced; the gradient kernels start once the
   // GEMM has seen Us and Ts complete and fill the SMs its last tiles leave idle.
-  if (rank > 0 && ts_in != nullptr) {
-    if (!aligned16(ts_in)) return set_error(FL_ERR_ARG, "%s: Ts must be 16-byte aligned", who);
-    ts = reinterpret_cast<uint8_t*>(const_cast<uint16_t*>(ts_in));  // read only
-  }
+  if (rank > 0 && ts_in != nullptr) ts = reinterpret_cast<uint8_t*>(const_cast<uint16_t*>(ts_in));  // read only
   if (rank > 0 && !accumulate) {
     cudaError_t e = cudaMemsetAsync(dA, 0, static_cast<size_t>(rank) * K * sizeof(float), st);
     if (e == cudaSuccess) e = cudaMemsetAsync(dB, 0, static_cast<size_t>(N) * rank * sizeof(float), st);

@@ -69,6 +69,10 @@ def test_argument_validation_without_gpu(lib):
     P = 1024
     rc = lib.fl_bwd(P, P, 16, 100, 256, P, P, P, None, None, 0, 1.0, P, None, None, 0, None, 0, None)
     assert rc == FL_ERR_ARG and b"multiple of 64" in lib.fl_last_error()
+    # fl_bwd_ts: the forward's Ts must be 16-byte aligned (checked before any device work).
+    ws = lib.fl_bwd_workspace_bytes(300, 256, 256, 8)
+    rc = lib.fl_bwd_ts(P, P, 300, 256, 256, P, P, P, P, P, 8, 1.0, P + 8, P, P, P, 0, P, ws, None)
+    assert rc == FL_ERR_ARG and b"Ts must be 16-byte aligned" in lib.fl_last_error()
 
 
 def test_ops_reject_cpu_tensors():

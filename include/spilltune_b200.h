@@ -204,6 +204,13 @@ int fl_bwd_nf4dq(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, in
                  const float* block_scales, const float* quant_map, const float* A, const float* B, int rank,
                  float scale, uint16_t* dX, float* dA, float* dB, int accumulate, void* workspace,
                  size_t workspace_bytes, void* stream);
+/* fl_bwd_ts for such a record: Ts as fl_fwd_nf4dq left it in the first
+ * M * 128 bytes of its workspace (read whenever rank > 0: every M takes the
+ * tile GEMM here). */
+int fl_bwd_nf4dq_ts(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* packed,
+                    const float* block_scales, const float* quant_map, const float* A, const float* B, int rank,
+                    float scale, const uint16_t* Ts, uint16_t* dX, float* dA, float* dB, int accumulate,
+                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Chunked LM head + shifted cross-entropy, one token chunk per call: the body

@@ -41,6 +41,8 @@ SIGNATURES = {
     "fl_fwd_nf4dq": ([_P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _INT, _F, _P, _P, _SZ, _P], _INT),
     "fl_bwd_nf4dq": ([_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _INT, _F, _P, _P, _P, _INT, _P, _SZ, _P],
                      _INT),
+    "fl_bwd_nf4dq_ts": ([_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _INT, _F, _P, _P, _P, _P, _INT, _P, _SZ,
+                         _P], _INT),
     "fl_ce_workspace_bytes": ([_I64, _I64], _SZ),
     "fl_ce_chunk": ([_P, _I64, _I64, _P, _I64, _P, _F, _P, _P, _P, _SZ, _P], _INT),
     "fl_grouped_workspace_bytes": ([_I64, _INT, _I64, _I64, _INT], _SZ),

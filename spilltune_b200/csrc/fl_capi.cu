@@ -276,6 +276,14 @@ int fl_bwd_ts(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64
                   accumulate, workspace, workspace_bytes, stream, Ts);
 }
 
+int fl_bwd_nf4dq_ts(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* packed,
+                    const float* block_scales, const float* quant_map, const float* A, const float* B, int rank,
+                    float scale, const uint16_t* Ts, uint16_t* dX, float* dA, float* dB, int accumulate,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  return bwd_impl("fl_bwd_nf4dq_ts", kLayoutNf4Dq64, dY, X, M, N, K, packed, block_scales, quant_map, A, B, rank,
+                  scale, dX, dA, dB, accumulate, workspace, workspace_bytes, stream, Ts);
+}
+
 int fl_fwd_nf4dq(const uint16_t* X, int64_t M, int64_t K, const uint8_t* packed, const float* block_scales,
                  const float* quant_map, int64_t N, const float* A, const float* B, int rank, float scale, uint16_t* Y,
                  void* workspace, size_t workspace_bytes, void* stream) {

@@ -171,7 +171,9 @@ def _factors(A, B, N, K):
     return rank
 
 
-def fwd(x, staged: StagedNF4DQ, A=None, B=None, scale=0.0):
+def fwd(x, staged: StagedNF4DQ, A=None, B=None, scale=0.0, return_ts=False):
+    """return_ts: also return Ts = bf16(scale * x . A^T) ([tokens, 64] bf16, a view
+    of the workspace) for ``bwd(..., ts=)``; None when rank == 0."""
     N, K = staged.shape
     x2 = _flat(x, K)
     rank = _factors(A, B, N, K)
@@ -186,10 +188,16 @@ def fwd(x, staged: StagedNF4DQ, A=None, B=None, scale=0.0):
     if M:
         _lib.call("fl_fwd_nf4dq", _ptr(x2), M, K, _ptr(rec.packed), _ptr(staged.block_scales), _ptr(rec.quant_map),
                   N, _ptr(A), _ptr(B), rank, float(scale), _ptr(y), _ptr(ws), ws_bytes, _stream())
-    return y.view(*x.shape[:-1], N)
+    y = y.view(*x.shape[:-1], N)
+    if not return_ts:
+        return y
+    # Every M takes the tile GEMM for these records: Ts leads the workspace.
+    return y, (ws[:M * 128].view(torch.bfloat16).view(M, 64) if rank and M else None)
 
 
-def bwd(dy, x, staged: StagedNF4DQ, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False):
+def bwd(dy, x, staged: StagedNF4DQ, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False, ts=None):
+    """ts: the Ts ``fwd(..., return_ts=True)`` returned for the same x, A and
+    scale (X . A^T is then not recomputed; results identical)."""
     N, K = staged.shape
     dy2 = _flat(dy, N)
     rank = _factors(A, B, N, K)
@@ -208,7 +216,15 @@ def bwd(dy, x, staged: StagedNF4DQ, A=None, B=None, scale=0.0, dA=None, dB=None,
             accumulate = False
     ws_bytes = _lib.load().fl_bwd_workspace_bytes(M, N, K, rank)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dy2.device) if ws_bytes else None
-    if M:
+    if ts is not None and rank:
+        if ts.dtype != torch.bfloat16 or tuple(ts.shape) != (M, 64) or not ts.is_contiguous():
+            raise ValueError("ts must be the [tokens, 64] bf16 Ts that fwd(..., return_ts=True) returned")
+        _need_cuda(ts)
+    if M and ts is not None and rank:
+        _lib.call("fl_bwd_nf4dq_ts", _ptr(dy2), _ptr(x2), M, N, K, _ptr(rec.packed), _ptr(staged.block_scales),
+                  _ptr(rec.quant_map), _ptr(A), _ptr(B), rank, float(scale), _ptr(ts), _ptr(dx), _ptr(dA),
+                  _ptr(dB), int(bool(accumulate)), _ptr(ws), ws_bytes, _stream())
+    elif M:
         _lib.call("fl_bwd_nf4dq", _ptr(dy2), _ptr(x2), M, N, K, _ptr(rec.packed), _ptr(staged.block_scales),
                   _ptr(rec.quant_map), _ptr(A), _ptr(B), rank, float(scale), _ptr(dx), _ptr(dA), _ptr(dB),
                   int(bool(accumulate)), _ptr(ws), ws_bytes, _stream())
@@ -223,13 +239,18 @@ class NF4DQLinear(torch.autograd.Function):
     def forward(ctx, x, A, B, staged, scale):
         ctx.staged, ctx.scale, ctx.has_lora = staged, scale, A is not None
         ctx.save_for_backward(*((x, A, B) if ctx.has_lora else (x,)))
-        return fwd(x, staged, A, B, scale)
+        if not ctx.has_lora:
+            return fwd(x, staged)
+        # Ts kept for the backward, as autograd keeps the LoRA down-projection.
+        y, ctx.ts = fwd(x, staged, A, B, scale, return_ts=True)
+        return y
 
     @staticmethod
     def backward(ctx, dy):
         if ctx.has_lora:
             x, A, B = ctx.saved_tensors
-            dx, dA, dB = bwd(dy.contiguous(), x, ctx.staged, A, B, ctx.scale)
+            dx, dA, dB = bwd(dy.contiguous(), x, ctx.staged, A, B, ctx.scale, ts=ctx.ts)
+            ctx.ts = None
             return dx, dA, dB, None, None
         (x,) = ctx.saved_tensors
         dx, _, _ = bwd(dy.contiguous(), x, ctx.staged)

@@ -125,6 +125,14 @@ def test_fwd_bwd_parity(cuda_lib, M, N, K, rank):
     else:
         errs = [ol.rel_l2(dx.cpu(), dy.float() @ W.float())]
     assert max(errs) <= TIGHT, errs
+    if rank:
+        # fl_bwd_nf4dq_ts with the forward's Ts: dX bit for bit, dA/dB up to the
+        # order of the gradient kernels' atomic adds.
+        y2, ts = nf4dq.fwd(x.cuda(), st, cu(A), cu(B), s, return_ts=True)
+        assert torch.equal(y2.cpu(), y)
+        dx2, dA2, dB2 = nf4dq.bwd(dy.cuda(), x.cuda(), st, cu(A), cu(B), s, ts=ts)
+        assert torch.equal(dx2, dx)
+        assert ol.rel_l2(dA2.cpu(), dA.cpu()) < 1e-6 and ol.rel_l2(dB2.cpu(), dB.cpu()) < 1e-6
 
 
 @pytest.mark.gpu

@@ -335,6 +335,15 @@ def cpu_baseline_adaptive(tokens, codec_name, target_s=10.0, cap=8192):
         t = min(cap, max(2 * t, int(t * target_s / max(layer_s, 1e-3))))
 
 
+def bench_config(args, world):
+    """The workload both arms report (the reference arm times the same step on the host)."""
+    return {"workload": "llama3-8b frozen-linear stack: 32 layers x (q,k,v,o,gate,up,down), "
+                        "fwd + recompute + bwd(dX,dA,dB) + AdamW",
+            "layers": args.layers, "tokens_per_gpu": args.tokens, "micro_batch": 4, "seq_len": 2048, "rank": RANK,
+            "alpha": ALPHA, "codec": args.codec, "parallelism": f"dp{world}",
+            "l2": "inputs > L2 (per-layer working set ~2 GB, alternating buffer sets)"}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return 0
@@ -355,8 +364,7 @@ def run_reference(args, world, rank):
             "impl": "reference", "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * args.tokens / value, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "llama3-8b frozen-linear stack (32 layers x q,k,v,o,gate,up,down)",
-                       "tokens_per_gpu": args.tokens, "rank": RANK, "alpha": ALPHA, "codec": args.codec},
+            "config": bench_config(args, world),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
                              "sample": info["sample"]},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -481,11 +489,7 @@ def main():
             "value": world * M / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "llama3-8b frozen-linear stack: 32 layers x (q,k,v,o,gate,up,down), "
-                                   "fwd + recompute + bwd(dX,dA,dB) + AdamW",
-                       "layers": L, "tokens_per_gpu": M, "micro_batch": 4, "seq_len": 2048, "rank": RANK,
-                       "alpha": ALPHA, "codec": args.codec, "parallelism": f"dp{world}",
-                       "l2": "inputs > L2 (per-layer working set ~2 GB, alternating buffer sets)"},
+            "config": bench_config(args, world),
             "step_tflops": total_flops / (ms / 1e3) / 1e12,
             "roofline": {"bound": "tensor", "kernel": "fl_fwd (fused dequant-GEMM + LoRA) gate_proj 8192x14336x4096",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,

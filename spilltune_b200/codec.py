@@ -125,6 +125,17 @@ def _groups(w):
     return chunk.view(g, GROUP), n
 
 
+def _reject_bf16_overflow(codes, scale, lut):
+    """The reference rejects a record any of whose decoded values, fp32(lut[c] * scale)
+    rounded to BF16, is not finite (quantization/codecs.py:110-114).  |fp32(a * s)|
+    grows with |a|, so each group's largest |lut[c]| over its codes decides it."""
+    mag = lut.abs()
+    for i in range(0, codes.shape[0], 8192):  # bounded scratch
+        top = mag[codes[i:i + 8192].long()].amax(1)
+        if not torch.isfinite((top * scale[i:i + 8192]).to(torch.bfloat16)).all():
+            raise ValueError("quantized value overflows BF16 compute range")
+
+
 def encode_int4_sym(w):
     """int4-sym-g128 encoder (same arithmetic as codecs.py:86-105).  Runs on the
     tensor's device (CPU, or a CUDA device for large synthetic models)."""
@@ -133,9 +144,12 @@ def encode_int4_sym(w):
         raise ValueError("nonfinite quantization input")
     scale = chunk.abs().amax(1) / 7
     scale = torch.where(scale == 0, torch.ones_like(scale), scale)
-    q = ((chunk / scale[:, None]).clamp(-7, 7).round().to(torch.uint8) + 8).flatten().view(-1, 2)
+    q = ((chunk / scale[:, None]).clamp(-7, 7).round().to(torch.uint8) + 8)
+    lut = INT4_SYM_LUT.to(chunk.device)
+    _reject_bf16_overflow(q, scale, lut)
+    q = q.flatten().view(-1, 2)
     payload = (q[:, 0] | (q[:, 1] << 4)).contiguous()
-    return PackedWeight(payload, scale.contiguous(), INT4_SYM_LUT.to(chunk.device), tuple(w.shape), INT4_SYM)
+    return PackedWeight(payload, scale.contiguous(), lut, tuple(w.shape), INT4_SYM)
 
 
 def encode_nf4(w, lut=None):
@@ -152,6 +166,7 @@ def encode_nf4(w, lut=None):
     for i in range(0, normalized.shape[0], 8192):  # bounded scratch
         part = normalized[i:i + 8192]
         codes[i:i + 8192] = (part[..., None] - lut).abs().argmin(-1).to(torch.uint8)
+    _reject_bf16_overflow(codes, scale, lut)
     q = codes.flatten().view(-1, 2)
     payload = (q[:, 0] | (q[:, 1] << 4)).contiguous()
     return PackedWeight(payload, scale.contiguous(), lut.clone(), tuple(w.shape), NF4)

@@ -41,3 +41,17 @@ def test_from_record_wraps_reference_layout():
         codec.from_record(dict(spec, codec="int8-sym-g128"), parts)
     with pytest.raises(ValueError, match="payload"):
         codec.PackedWeight(parts["payload"][:-1], parts["scales"], codec.INT4_SYM_LUT, (32, 256))
+
+
+@pytest.mark.parametrize("name", ["int4-sym-g128", "nf4-g128"])
+def test_host_encoders_reject_what_the_reference_rejects(name):
+    """As the reference's encoder does (its tests/test_quantization.py:114-136): a
+    nonfinite input, and a value whose decoded BF16 would overflow, raise ValueError."""
+    from spilltune_b200 import codec
+    x = torch.ones(1, 128)
+    x[0, 0] = float("nan")
+    with pytest.raises(ValueError, match="nonfinite"):
+        codec.encode(x, name)
+    with pytest.raises(ValueError, match="BF16"):
+        codec.encode(torch.full((1, 128), 3.4e38), name)
+    codec.encode(torch.full((1, 128), 3.3e38), name)  # the largest values that still fit are kept

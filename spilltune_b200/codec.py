@@ -116,6 +116,38 @@ def from_record(spec, parts):
     return PackedWeight(parts["payload"], parts["scales"], lut, shape, codec)
 
 
+def validate(w: PackedWeight, chunk_groups=1 << 20):
+    """The value checks of the reference's ``validate_spec`` (quantization/codecs.py:
+    119-156), which it runs on every stored record when a slot session is built
+    (memory.py:128): scales finite and positive, no reserved int4 code (stored
+    nibble 0, the value -8), padding past ``numel`` decoding to zero, and no
+    decoded value fp32(lut[c] * scale) overflowing BF16.  Raises ValueError with
+    the reference's messages.  Runs where the record lives, in bounded chunks."""
+    scales = w.scales
+    if not torch.isfinite(scales).all() or (scales <= 0).any():
+        raise ValueError("invalid stored scales")
+    mag = w.lut.abs()
+    limit = mag.max()
+    n = w.numel
+    for g0 in range(0, scales.numel(), chunk_groups):
+        g1 = min(g0 + chunk_groups, scales.numel())
+        raw = w.payload[g0 * 64:g1 * 64]
+        codes = torch.stack((raw & 15, raw >> 4), 1).view(-1)  # element order
+        if w.codec == INT4_SYM and (codes == 0).any():
+            raise ValueError("reserved int4 -8 code")
+        valid = max(0, min(codes.numel(), n - g0 * GROUP))
+        if valid < codes.numel() and (w.lut[codes[valid:].long()] != 0).any():
+            raise ValueError("nonzero quantized tail padding")
+        sc = scales[g0:g1]
+        # Only a group whose largest codebook magnitude overflows can overflow:
+        # those get the exact per-code check.
+        risky = ~torch.isfinite((limit * sc).to(torch.bfloat16))
+        if risky.any():
+            top = mag[codes.view(-1, GROUP)[risky].long()].amax(1)
+            if not torch.isfinite((top * sc[risky]).to(torch.bfloat16)).all():
+                raise ValueError("quantized value overflows BF16 compute range")
+
+
 def _groups(w):
     flat = w.detach().reshape(-1).to(torch.float32)
     n = flat.numel()

@@ -30,7 +30,7 @@ import threading
 
 import torch
 
-from .codec import PackedWeight
+from .codec import PackedWeight, validate
 
 _ALIGN = 256
 
@@ -93,6 +93,9 @@ class PackedSlotSession:
                 for t in (w.payload, w.scales, w.lut):
                     if t.device.type != "cpu" or not t.is_pinned() or not t.is_contiguous():
                         raise ValueError("host records must be contiguous pinned CPU tensors")
+                # The reference validates every stored record when its session is
+                # built (memory.py:128); same checks, same errors.
+                validate(w)
         self.layers = list(layers)
         self.capacity = max(layer_bytes(layer) for layer in self.layers)
         self.group = group

@@ -55,3 +55,33 @@ def test_host_encoders_reject_what_the_reference_rejects(name):
     with pytest.raises(ValueError, match="BF16"):
         codec.encode(torch.full((1, 128), 3.4e38), name)
     codec.encode(torch.full((1, 128), 3.3e38), name)  # the largest values that still fit are kept
+
+
+@pytest.mark.parametrize("name", ["int4-sym-g128", "nf4-g128"])
+def test_validate_restates_the_reference_record_checks(name):
+    """codec.validate raises what the reference's validate_spec raises
+    (quantization/codecs.py:119-156) and accepts what the encoder produces."""
+    from spilltune_b200 import codec
+    w = codec.encode(torch.randn(3, 43) * 0.02, name)  # 129 elements: a ragged second group
+    codec.validate(w)
+
+    def broken(fn):
+        b = codec.PackedWeight(w.payload.clone(), w.scales.clone(), w.lut.clone(), w.shape, w.codec)
+        fn(b)
+        return b
+
+    with pytest.raises(ValueError, match="invalid stored scales"):
+        codec.validate(broken(lambda b: b.scales.__setitem__(0, 0.0)))
+    with pytest.raises(ValueError, match="invalid stored scales"):
+        codec.validate(broken(lambda b: b.scales.__setitem__(1, float("inf"))))
+    with pytest.raises(ValueError, match="padding"):
+        codec.validate(broken(lambda b: b.payload.__setitem__(-1, int(b.payload[-1]) ^ 0x10)))
+    with pytest.raises(ValueError, match="BF16"):
+        codec.validate(broken(lambda b: b.scales.fill_(3.4e38)))
+    if name == "int4-sym-g128":
+        with pytest.raises(ValueError, match="reserved"):
+            codec.validate(broken(lambda b: b.payload.__setitem__(0, int(b.payload[0]) & 0xF0)))
+        # Exact overflow rule: a scale at which code -8 would overflow is fine when the
+        # group's largest stored magnitude (7) does not.
+        ok = codec.encode(torch.full((1, 128), 3.0e38), name)
+        codec.validate(ok)

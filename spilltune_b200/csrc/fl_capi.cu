@@ -55,7 +55,7 @@ using namespace fl;
 
 extern "C" {
 
-int fl_version(void) { return 101; }
+int fl_version(void) { return 200; }  // 0.2.0: fl_bwd_ts, fl_bwd_nf4dq_ts
 
 const char* fl_last_error(void) { return g_err; }
 

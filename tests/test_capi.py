@@ -43,7 +43,7 @@ def test_python_binding_covers_header():
 
 
 def test_version_and_workspace_sizes(lib):
-    assert lib.fl_version() >= 101
+    assert lib.fl_version() >= 200  # 0.2.0 adds fl_bwd_ts and fl_bwd_nf4dq_ts
     # Ts (M x 64 bf16) + the factor converted to a bf16 hi/lo pair (4 * rank' * K).
     assert lib.fl_fwd_workspace_bytes(8192, 4096, 16) == 8192 * 128 + 4 * 16 * 4096
     assert lib.fl_fwd_workspace_bytes(8192, 4096, 20) == 8192 * 128 + 4 * 32 * 4096

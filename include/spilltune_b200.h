@@ -50,6 +50,27 @@ const char* fl_last_error(void);
  * bounded waits expired.  Synchronises the device.  reset != 0 clears it. */
 int fl_status(int reset, uint32_t* status_out);
 
+/* Status bits (fl_status). */
+#define FL_STATUS_TIMEOUT_FULL (1u << 0)   /* a consumer's wait for a filled stage expired */
+#define FL_STATUS_TIMEOUT_EMPTY (1u << 1)  /* a producer's wait for a free stage expired */
+#define FL_STATUS_TIMEOUT_ACCUM (1u << 2)  /* a wait for the accumulator expired */
+#define FL_STATUS_TIMEOUT_DRAIN (1u << 3)  /* the exit-time drain of in-flight copies expired */
+#define FL_STATUS_BAD_LAUNCH (1u << 4)     /* inconsistent launch data (e.g. MoE segment offsets) */
+#define FL_STATUS_BAD_INPUT (1u << 5)      /* an input value outside its domain (a CE target) */
+
+/*
+ * Self-test of the kernels' bounded device waits; no counterpart in the
+ * reference.  Every wait in this library on a pipeline barrier gives up after
+ * 2 s of wall time, sets a status bit and lets its kernel drain and exit, so a
+ * stalled pipeline becomes an error the host reads instead of a hung GPU.  This
+ * runs that wait code with `limit_ns` (<= 2 s) on a barrier phase that nothing
+ * completes, synchronises `stream` and reads the status word: it returns
+ * FL_ERR_DEVICE with FL_STATUS_TIMEOUT_FULL set when the wait expired and the
+ * kernel returned (the expected outcome), FL_OK if the wait did not give up.
+ * The status word is not cleared (fl_status(1, ...) does that).
+ */
+int fl_wait_selftest(uint64_t limit_ns, void* stream);
+
 /*
  * Dequantize one group-128 record into a BF16 buffer, bit-exact with the
  * reference's decode_into (ram_vram_finetune/quantization/codecs.py:158-170,
@@ -98,8 +119,9 @@ size_t fl_bwd_workspace_bytes(int64_t M, int64_t N, int64_t K, int rank);
  * accumulate != 0 adds into dA/dB (grad_A/grad_B.add_, recompute.py:124-127);
  * accumulate == 0 overwrites them.  dA/dB may be NULL when rank == 0.
  * M <= 16 with K % 512 == 0 runs a decode-step kernel (the scale folded into
- * bf16(dY * scale) instead of into the weight); larger M the tile GEMM.
- * Requires K % 128 == 0, N % 64 == 0 (N % 128 == 0 when rank > 0), rank <= 64.
+ * bf16(dY * scale) instead of into the weight) unless rank > 0 and
+ * N % 128 != 0; otherwise the tile GEMM.
+ * Requires K % 128 == 0, N % 64 == 0, rank <= 64.
  */
 int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t K, const uint8_t* payload,
            const float* scales, const float* lut16, const float* A, const float* B, int rank, float scale,
@@ -132,9 +154,11 @@ int fl_bwd_ts(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64
  * device memory (held on every GPU that loads the library), so when rank > 0 M
  * is limited to 32768 tokens and rank' * K to 2^21 (rank' = rank rounded up to
  * 16, 32 or 64; FL_ERR_ARG beyond).  The first call on a device
- * looks up that array's address; make it before any stream capture.  All calls
- * on a device share the array: calls whose kernels overlap on the GPU race and
- * must be serialised by the caller.
+ * looks up that array's address; make it before any stream capture.  The
+ * address is kept for the life of the process, so after cudaDeviceReset on a
+ * device this process must not call the library on that device again.  All
+ * calls on a device share the array: calls whose kernels overlap on the GPU
+ * race and must be serialised by the caller.
  */
 int fl_fwd_noalloc(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, const float* scales,
                    const float* lut16, int64_t N, const float* A, const float* B, int rank, float scale,
@@ -219,6 +243,10 @@ int fl_bwd_nf4dq_ts(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N,
  *   h       bf16 [T, H]   normalized hidden states of the chunk's tokens;
  *   head    bf16 [V, H]   frozen LM head;
  *   targets int64 [T]     next-token labels, -100 = no loss for that token;
+ *                         any other value outside [0, V) adds no loss, gets a
+ *                         zero gradient row and sets FL_STATUS bit 5 (read
+ *                         with fl_status; the reference's F.cross_entropy
+ *                         raises for it);
  *   loss_sum fp32 scalar (device) += sum over targeted tokens of
  *            logsumexp(logits) - logits[target], logits = bf16(h . head^T);
  *   dh      bf16 [T, H]   = d(loss / normalization) / dh, inv_norm = 1/normalization.

@@ -29,6 +29,7 @@ SIGNATURES = {
     "fl_version": ([], _INT),
     "fl_last_error": ([], ctypes.c_char_p),
     "fl_status": ([_INT, _P], _INT),
+    "fl_wait_selftest": ([ctypes.c_uint64, _P], _INT),
     "fl_dequant": ([_P, _P, _P, _I64, _P, _P], _INT),
     "fl_fwd_workspace_bytes": ([_I64, _I64, _INT], _SZ),
     "fl_fwd": ([_P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _INT, _F, _P, _P, _SZ, _P], _INT),
@@ -86,6 +87,14 @@ def check(code, what=""):
         if code == FL_ERR_ARG:
             raise ValueError(f"{what}: {msg}")
         raise FLError(code, f"{what}: {msg}")
+
+
+def status(reset=False):
+    """The current device's status word (FL_STATUS_* bits of kernels that gave
+    up a bounded wait or saw bad input); synchronises the device."""
+    v = ctypes.c_uint32(0)
+    check(load().fl_status(int(bool(reset)), ctypes.byref(v)), "fl_status")
+    return v.value
 
 
 def call(name, *args):

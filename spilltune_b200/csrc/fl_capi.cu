@@ -49,13 +49,51 @@ static int current_status(uint32_t** out) {
   return FL_OK;
 }
 
+// Self-test of the bounded waits every pipeline uses (mbar_wait_warp): one CTA
+// waits, with the given limit, on an mbarrier phase that nothing completes.
+// Every lane's wait gives up, sets kStatusTimeoutFull in *status and returns;
+// the phase is then completed so the barrier is not left pending at exit.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, uint32_t* status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t abort_word;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_word = 0u;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  (void)mbar_wait_warp(&bar, 0, &abort_word, status, kStatusTimeoutFull, limit_ns);
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_arrive(&bar);
+}
+
 }  // namespace fl
 
 using namespace fl;
 
 extern "C" {
 
-int fl_version(void) { return 200; }  // 0.2.0: fl_bwd_ts, fl_bwd_nf4dq_ts
+int fl_version(void) { return 300; }  // 0.3.0: fl_wait_selftest, CE target status bit
+
+int fl_wait_selftest(uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > kWaitLimitNs)
+    return set_error(FL_ERR_ARG, "fl_wait_selftest: limit must be in (0, %llu] ns", (unsigned long long)kWaitLimitNs);
+  uint32_t* w = nullptr;
+  int rc = current_status(&w);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  wait_selftest_kernel<<<1, 64, 0, st>>>(limit_ns, w);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "fl_wait_selftest: %s", cudaGetErrorString(e));
+  uint32_t v = 0;
+  e = cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "fl_wait_selftest: status read: %s", cudaGetErrorString(e));
+  if (v & kStatusTimeoutFull)
+    return set_error(FL_ERR_DEVICE, "fl_wait_selftest: bounded wait expired after %llu ns (status 0x%x)",
+                     (unsigned long long)limit_ns, v);
+  return set_error(FL_OK, "");
+}
 
 const char* fl_last_error(void) { return g_err; }
 
@@ -161,9 +199,6 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
   if (!dY || !dX) return set_error(FL_ERR_ARG, "%s: null dY/dX", who);
   if (!aligned16(dY)) return set_error(FL_ERR_ARG, "%s: dY must be 16-byte aligned", who);
   if (rank > 0) {
-    if (N % 128 != 0)
-      return set_error(FL_ERR_ARG, "%s: out_features N=%lld must be a multiple of 128 with a LoRA branch", who,
-                       (long long)N);
     if (!X || !A || !B || !dA || !dB) return set_error(FL_ERR_ARG, "%s: null X or LoRA factor/gradient", who);
     if (!aligned16(X)) return set_error(FL_ERR_ARG, "%s: X must be 16-byte aligned", who);
     if (!workspace || workspace_bytes < fl_bwd_workspace_bytes(M, N, K, rank) || !aligned16(workspace))
@@ -179,8 +214,13 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
   uint8_t* qc_a = rank > 0 ? qc_b + lora_factor_bytes(N, rank) : nullptr;
   // Decode-like steps (M <= 16) take the small-M backward, which also finishes
   // the LoRA gradients; the tile GEMM's 256-token tiles would leave most SMs
-  // idle.  Its low-rank partials use the converted-factor scratch.
-  if (small_m_path(layout, M, K)) {
+  // idle.  Its low-rank partials use the converted-factor scratch, and its
+  // reduction of dY . B runs over 128-wide pieces of N: with a LoRA branch and
+  // N % 128 != 0 the tile path takes the call.  The forward of such a call ran
+  // the decode-step kernel and left no Ts, so a Ts passed in is never read.
+  const bool small = small_m_path(layout, M, K);
+  if (small) ts_in = nullptr;
+  if (small && (rank == 0 || N % 128 == 0)) {
     float* uparts = reinterpret_cast<float*>(qc_b);
     float* tparts = reinterpret_cast<float*>(qc_a);
     if (rank > 0) {

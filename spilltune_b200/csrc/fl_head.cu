@@ -311,10 +311,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// A target the loss reads: in [0, V).  kIgnore rows add nothing; any other
+// value is invalid (F.cross_entropy raises for it): the row adds nothing, its
+// dlogits are zero and kStatusBadInput is set.
+__device__ __forceinline__ bool valid_target(int64_t t, int V) { return t >= 0 && t < V; }
+
 // Row combine: lse[m] = max + log(sum s_i exp(max_i - max)); loss += lse - target
-// logit for rows with a target.
+// logit for rows with a valid target.
 __global__ void ce_rows_kernel(const float2* __restrict__ part, int n_tiles, const int64_t* __restrict__ targets,
-                               const float* __restrict__ tgt, int M, float* __restrict__ lse, float* __restrict__ loss) {
+                               const float* __restrict__ tgt, int M, int V, float* __restrict__ lse,
+                               float* __restrict__ loss, uint32_t* __restrict__ status) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= M) return;
   const float2* p = part + static_cast<size_t>(warp) * n_tiles;
@@ -329,12 +335,16 @@ __global__ void ce_rows_kernel(const float2* __restrict__ part, int n_tiles, con
   if (lane == 0) {
     const float l = mx + __logf(s);
     lse[warp] = l;
-    if (targets[warp] != kIgnore) atomicAdd(loss, l - tgt[warp]);
+    const int64_t t = targets[warp];
+    if (valid_target(t, V))
+      atomicAdd(loss, l - tgt[warp]);
+    else if (t != kIgnore)
+      atomicOr(status, kStatusBadInput);
   }
 }
 
 // dlogits in place: (exp(x - lse) - [v == target]) * inv_norm, zero for
-// ignored rows; rounded to bf16.
+// ignored and invalid-target rows; rounded to bf16.
 __global__ void dlogits_kernel(__nv_bfloat16* __restrict__ logits, int M, int V, const float* __restrict__ lse,
                                const int64_t* __restrict__ targets, float inv_norm) {
   const int64_t per_row = V / 8;  // 8 bf16 per vector (V % 8 == 0)
@@ -345,7 +355,7 @@ __global__ void dlogits_kernel(__nv_bfloat16* __restrict__ logits, int M, int V,
     const int v0 = static_cast<int>(i % per_row) * 8;
     const int64_t tv = targets[m];
     uint4* p = reinterpret_cast<uint4*>(logits + static_cast<size_t>(m) * V + v0);
-    if (tv == kIgnore) {
+    if (!valid_target(tv, V)) {
       *p = make_uint4(0, 0, 0, 0);
       continue;
     }
@@ -413,6 +423,7 @@ int launch_ce_chunk(const void* h, int T, int H, const void* head, int V, const 
   int dev = 0;
   cudaGetDevice(&dev);
   uint32_t* status = status_word(dev);
+  if (!status) return set_error(FL_ERR_CUDA, "fl_ce_chunk: status word unavailable on device %d", dev);
 
   // 1. logits = h . head^T with the CE partials
   CUtensorMap ta, tb;
@@ -434,7 +445,7 @@ int launch_ce_chunk(const void* h, int T, int H, const void* head, int V, const 
   a.tgt = tgt;
   if ((rc = launch_gemm<false, kEpiCE>(ta, tb, a, stream))) return rc;
   // 2. rows
-  ce_rows_kernel<<<(T * 32 + 255) / 256, 256, 0, stream>>>(part, nt, targets, tgt, T, lse, loss_sum);
+  ce_rows_kernel<<<(T * 32 + 255) / 256, 256, 0, stream>>>(part, nt, targets, tgt, T, V, lse, loss_sum, status);
   // 3. dlogits in place
   {
     const int64_t total = static_cast<int64_t>(T) * (V / 8);

@@ -605,12 +605,14 @@ size_t lora_factor_bytes(int64_t R, int rank) { return 4u * static_cast<size_t>(
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank, float s,
                      void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles, const int* tile_count,
                      int max_tiles, int64_t q_expert_stride, int experts, bool pdl) {
-  if (R % 128 != 0) return set_error(FL_ERR_ARG, "lora_down: reduction dim %d not a multiple of 128", R);
+  if (R % 64 != 0) return set_error(FL_ERR_ARG, "lora_down: reduction dim %d not a multiple of 64", R);
   if (rank < 1 || rank > 64) return set_error(FL_ERR_ARG, "lora_down: rank %d outside [1, 64]", rank);
   if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(out64) |
        reinterpret_cast<uintptr_t>(qc_scratch)) & 15u)
     return set_error(FL_ERR_ARG, "lora_down: activations, output and scratch must be 16-byte aligned");
-  if (tiles == nullptr && M <= lds::kMaxRows && q_sr == 1 && q_sj % 4 == 0 &&
+  // The small-M kernel takes 128-wide pieces of the reduction; the tiled
+  // kernel 64-wide units (any R % 64 == 0).
+  if (tiles == nullptr && M <= lds::kMaxRows && R % 128 == 0 && q_sr == 1 && q_sj % 4 == 0 &&
       (reinterpret_cast<uintptr_t>(q) & 15u) == 0)
     return lds::launch(P, M, R, q, q_sj, rank, s, out64, stream);
   const int nq = lora_nq(rank);

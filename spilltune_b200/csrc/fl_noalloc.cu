@@ -17,7 +17,10 @@
 //  * Every GPU that loads the library holds the 12 MiB array until exit.
 //  * The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current.  Make that first call
-//    before any stream capture.
+//    before any stream capture.  The address is kept for the life of the
+//    process: after cudaDeviceReset on a device (which frees the module's
+//    device memory), this process must not call the library on that device
+//    again.
 //  * All calls on a device share the one array and it keeps the last call's
 //    contents.  Calls whose kernels overlap on the GPU (different streams
 //    without ordering between them) race on it; serialise them.  Nothing in the
@@ -63,6 +66,7 @@ extern "C" int fl_fwd_noalloc(const uint16_t* X, int64_t M, int64_t K, const uin
                               const float* lut16, int64_t N, const float* A, const float* B, int rank, float scale,
                               uint16_t* Y, void* stream) {
   if (M <= 0 || N <= 0 || K <= 0) return set_error(FL_ERR_ARG, "fl_fwd_noalloc: dims must be positive");
+  if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return set_error(FL_ERR_ARG, "fl_fwd_noalloc: dims too large");
   if (rank > 0 && static_cast<uint64_t>(M) * 128u > kNoAllocScratchBytes)
     return set_error(FL_ERR_ARG, "fl_fwd_noalloc: M=%lld tokens exceeds the %zu-byte scratch (max %zu tokens)",
                      (long long)M, kNoAllocScratchBytes, kNoAllocScratchBytes / 128);

@@ -16,6 +16,7 @@ enum : uint32_t {
   kStatusTimeoutAccum = 1u << 2,  // epilogue gave up waiting for the accumulator
   kStatusTimeoutDrain = 1u << 3,  // exit-time drain of in-flight copies gave up
   kStatusBadLaunch = 1u << 4,     // kernel saw an inconsistent launch shape
+  kStatusBadInput = 1u << 5,      // an input value outside its domain (a CE target not in [0, V) nor -100)
 };
 
 // Wait limit for one mbarrier phase: 2 s of wall time.
@@ -82,13 +83,14 @@ __device__ __forceinline__ bool mbar_try_wait_short(uint64_t* bar, uint32_t pari
 }
 
 __device__ __forceinline__ bool mbar_wait_short(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_word,
-                                                uint32_t* status, uint32_t err_bit) {
+                                                uint32_t* status, uint32_t err_bit,
+                                                uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait_short(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait_short(bar, parity)) return true;
     if (*abort_word) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort_word = 1u;
       atomicOr(status, err_bit);
       return false;
@@ -100,13 +102,14 @@ __device__ __forceinline__ bool mbar_wait_short(uint64_t* bar, uint32_t parity, 
 // setting `err_bit` in *status and in the CTA-local abort word) on timeout or
 // when another thread of the CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_word,
-                                          uint32_t* status, uint32_t err_bit) {
+                                          uint32_t* status, uint32_t err_bit,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_word) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort_word = 1u;
       atomicOr(status, err_bit);
       return false;
@@ -117,8 +120,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Warp-uniform variant for warps that go on to execute .sync.aligned
 // instructions: the whole warp proceeds only if every lane saw the phase.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_word,
-                                               uint32_t* status, uint32_t err_bit) {
-  const bool ok = mbar_wait(bar, parity, abort_word, status, err_bit);
+                                               uint32_t* status, uint32_t err_bit,
+                                               uint64_t limit_ns = kWaitLimitNs) {
+  const bool ok = mbar_wait(bar, parity, abort_word, status, err_bit, limit_ns);
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
@@ -136,13 +140,14 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 }
 
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_word,
-                                                  uint32_t* status, uint32_t err_bit) {
+                                                  uint32_t* status, uint32_t err_bit,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if (*abort_word) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort_word = 1u;
       atomicOr(status, err_bit);
       return false;

@@ -25,7 +25,10 @@ IGNORE = -100
 def ce_chunk(h, head, targets, normalization, loss_acc):
     """One chunk: h [T, H] bf16, head [V, H] bf16 (frozen), targets int64 [T]
     (IGNORE = no loss).  Adds the chunk's summed CE into ``loss_acc`` (fp32
-    scalar on the device) and returns dh = d(CE / normalization) / dh (bf16)."""
+    scalar on the device) and returns dh = d(CE / normalization) / dh (bf16).
+    Targets are not checked on the host here (that would synchronise): a value
+    outside [0, V) other than IGNORE adds no loss, gets a zero ``dh`` row and
+    sets status bit 5, which ``_lib.status()`` reports."""
     _need_cuda(h, head, targets, loss_acc)
     h = h.contiguous()
     head = head.contiguous()
@@ -50,6 +53,11 @@ class _ChunkedCE(torch.autograd.Function):
             raise ValueError("invalid terminal token chunk/normalization")
         if labels.shape != normalized.shape[:2] or head.requires_grad:
             raise ValueError("invalid terminal labels/trainable frozen head")
+        # F.cross_entropy raises for a target outside [0, V) that is not the
+        # ignore index; so does this (one host check per call, not per chunk).
+        bad = (labels != IGNORE) & ((labels < 0) | (labels >= head.shape[0]))
+        if bool(bad.any()):
+            raise ValueError(f"Target {int(labels[bad].reshape(-1)[0])} is out of bounds.")
         vjp = torch.zeros_like(normalized)
         total = torch.zeros((), dtype=torch.float32, device=normalized.device)
         Bsz, _, H = normalized.shape

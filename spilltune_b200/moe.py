@@ -220,32 +220,19 @@ def grouped_bwd(dy, xs, segs: ExpertSegments, weight: PackedWeight, A=None, B=No
     return dx, dA, dB
 
 
-class GroupedFrozenLoRALinear(torch.autograd.Function):
-    """Autograd node of a grouped expert projection (experts frozen, A/B trainable)."""
-
-    @staticmethod
-    def forward(ctx, xs, A, B, segs, weight, scale):
-        ctx.segs = segs
-        ctx.weight = weight
-        ctx.scale = scale
-        ctx.has_lora = A is not None
-        if ctx.has_lora:
-            ctx.save_for_backward(xs, A, B)
-        return grouped_fwd(xs, segs, weight, A, B, scale)
-
-    @staticmethod
-    def backward(ctx, dy):
-        if ctx.has_lora:
-            xs, A, B = ctx.saved_tensors
-            dx, dA, dB = grouped_bwd(dy.contiguous(), xs, ctx.segs, ctx.weight, A, B, ctx.scale)
-            return dx, dA, dB, None, None, None
-        dx, _, _ = grouped_bwd(dy.contiguous(), None, ctx.segs, ctx.weight)
-        return dx, None, None, None, None, None
-
-
 def grouped_frozen_lora_linear(xs, segs, weight: PackedWeight, A=None, B=None, scale=0.0):
-    """Autograd-capable grouped projection of expert-sorted rows."""
-    return GroupedFrozenLoRALinear.apply(xs, A, B, segs, weight, float(scale))
+    """Autograd-capable grouped projection of expert-sorted rows (experts frozen,
+    A/B trainable), through the ``spilltune_b200::grouped_frozen_lora_linear``
+    custom op (``spilltune_b200.library``)."""
+    from . import library  # noqa: F401  (registers the ops)
+    E, N, K = _stacked_shape(weight)
+    if xs.dtype != torch.bfloat16 or xs.dim() != 2 or xs.shape[1] != K:
+        raise ValueError(f"expert rows must be bf16 [rows, {K}]")
+    _check_lora(A, B, E, N, K)
+    _need_cuda(xs, segs.seg, weight.payload, A, B)
+    _check_segs(xs, segs, E)
+    return torch.ops.spilltune_b200.grouped_frozen_lora_linear(xs, segs.seg, weight.payload, weight.scales,
+                                                               weight.lut, E, N, A, B, float(scale))
 
 
 # ------------------------------------------------------------ expert layers

@@ -24,7 +24,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from .ops import _flat, _need_cuda, _ptr, _stream
+from .ops import _flat, _need_cuda, _ptr, _stream, keeps_ts, launch_bwd, launch_fwd, ts_view
 
 BLOCK = 64
 NESTED_BLOCK = 256
@@ -178,21 +178,13 @@ def fwd(x, staged: StagedNF4DQ, A=None, B=None, scale=0.0, return_ts=False):
     x2 = _flat(x, K)
     rank = _factors(A, B, N, K)
     rec = staged.record
-    _need_cuda(x2, rec.packed, A, B)
-    if rank:
-        A, B = A.detach().contiguous(), B.detach().contiguous()
-    M = x2.shape[0]
-    y = torch.empty((M, N), dtype=torch.bfloat16, device=x2.device)
-    ws_bytes = _lib.load().fl_fwd_workspace_bytes(M, K, rank)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device) if ws_bytes else None
-    if M:
-        _lib.call("fl_fwd_nf4dq", _ptr(x2), M, K, _ptr(rec.packed), _ptr(staged.block_scales), _ptr(rec.quant_map),
-                  N, _ptr(A), _ptr(B), rank, float(scale), _ptr(y), _ptr(ws), ws_bytes, _stream())
+    y, ws = launch_fwd(1, x2, rec.packed, staged.block_scales, rec.quant_map, N, A, B, scale)
     y = y.view(*x.shape[:-1], N)
     if not return_ts:
         return y
     # Every M takes the tile GEMM for these records: Ts leads the workspace.
-    return y, (ws[:M * 128].view(torch.bfloat16).view(M, 64) if rank and M else None)
+    M = x2.shape[0]
+    return y, (ts_view(ws, M) if keeps_ts(1, M, K, rank) else None)
 
 
 def bwd(dy, x, staged: StagedNF4DQ, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False, ts=None):
@@ -202,59 +194,10 @@ def bwd(dy, x, staged: StagedNF4DQ, A=None, B=None, scale=0.0, dA=None, dB=None,
     dy2 = _flat(dy, N)
     rank = _factors(A, B, N, K)
     rec = staged.record
-    M = dy2.shape[0]
     x2 = _flat(x, K) if rank else None
-    _need_cuda(dy2, x2, rec.packed, A, B)
-    dx = torch.empty((M, K), dtype=torch.bfloat16, device=dy2.device)
-    if rank:
-        A, B = A.detach().contiguous(), B.detach().contiguous()
-        if dA is None:
-            dA = torch.empty((rank, K), dtype=torch.float32, device=dy2.device)
-            accumulate = False
-        if dB is None:
-            dB = torch.empty((N, rank), dtype=torch.float32, device=dy2.device)
-            accumulate = False
-    ws_bytes = _lib.load().fl_bwd_workspace_bytes(M, N, K, rank)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dy2.device) if ws_bytes else None
-    if ts is not None and rank:
-        if ts.dtype != torch.bfloat16 or tuple(ts.shape) != (M, 64) or not ts.is_contiguous():
-            raise ValueError("ts must be the [tokens, 64] bf16 Ts that fwd(..., return_ts=True) returned")
-        _need_cuda(ts)
-    if M and ts is not None and rank:
-        _lib.call("fl_bwd_nf4dq_ts", _ptr(dy2), _ptr(x2), M, N, K, _ptr(rec.packed), _ptr(staged.block_scales),
-                  _ptr(rec.quant_map), _ptr(A), _ptr(B), rank, float(scale), _ptr(ts), _ptr(dx), _ptr(dA),
-                  _ptr(dB), int(bool(accumulate)), _ptr(ws), ws_bytes, _stream())
-    elif M:
-        _lib.call("fl_bwd_nf4dq", _ptr(dy2), _ptr(x2), M, N, K, _ptr(rec.packed), _ptr(staged.block_scales),
-                  _ptr(rec.quant_map), _ptr(A), _ptr(B), rank, float(scale), _ptr(dx), _ptr(dA), _ptr(dB),
-                  int(bool(accumulate)), _ptr(ws), ws_bytes, _stream())
-    elif rank and not accumulate:
-        dA.zero_()
-        dB.zero_()
+    dx, dA, dB = launch_bwd(1, dy2, x2, rec.packed, staged.block_scales, rec.quant_map, K, A, B, scale, dA, dB,
+                            accumulate, ts)
     return dx.view(*dy.shape[:-1], K), dA, dB
-
-
-class NF4DQLinear(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, A, B, staged, scale):
-        ctx.staged, ctx.scale, ctx.has_lora = staged, scale, A is not None
-        ctx.save_for_backward(*((x, A, B) if ctx.has_lora else (x,)))
-        if not ctx.has_lora:
-            return fwd(x, staged)
-        # Ts kept for the backward, as autograd keeps the LoRA down-projection.
-        y, ctx.ts = fwd(x, staged, A, B, scale, return_ts=True)
-        return y
-
-    @staticmethod
-    def backward(ctx, dy):
-        if ctx.has_lora:
-            x, A, B = ctx.saved_tensors
-            dx, dA, dB = bwd(dy.contiguous(), x, ctx.staged, A, B, ctx.scale, ts=ctx.ts)
-            ctx.ts = None
-            return dx, dA, dB, None, None
-        (x,) = ctx.saved_tensors
-        dx, _, _ = bwd(dy.contiguous(), x, ctx.staged)
-        return dx, None, None, None, None
 
 
 def nf4dq_linear(inputs, staged: StagedNF4DQ, A=None, B=None, scale=0.0):
@@ -271,4 +214,8 @@ def nf4dq_linear(inputs, staged: StagedNF4DQ, A=None, B=None, scale=0.0):
         raise ValueError("inputs must have at least one dimension")
     if inputs.shape[-1] != staged.shape[1]:
         raise ValueError(f"input feature size {inputs.shape[-1]} does not match NF4 weight size {staged.shape[1]}")
-    return NF4DQLinear.apply(inputs, A, B, staged, float(scale))
+    from . import library
+    rec = staged.record
+    N, K = staged.shape
+    _factors(A, B, N, K)
+    return library.frozen_linear(inputs, rec.packed, staged.block_scales, rec.quant_map, N, K, 1, A, B, scale)

@@ -60,54 +60,58 @@ def _matrix_shape(weight: PackedWeight):
     return weight.shape
 
 
-def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0, return_ts=False):
-    """Y = x . W^T + scale * (x . A^T) . B^T  (bf16 out; plain frozen linear if A is None).
+# Entry points per record layout: 0 = group-128 (int4-sym / NF4 codebook),
+# 1 = bitsandbytes NF4-DQ64 (packed high nibble first, FP32 block scales).
+_FWD_ENTRY = {0: "fl_fwd", 1: "fl_fwd_nf4dq"}
+_BWD_ENTRY = {0: ("fl_bwd", "fl_bwd_ts"), 1: ("fl_bwd_nf4dq", "fl_bwd_nf4dq_ts")}
 
-    return_ts: also return Ts = bf16(scale * x . A^T) ([tokens, 64] bf16, zero past
-    the rank) as a view of the call's workspace, for ``bwd(..., ts=)`` -- the
-    intermediate the reference's autograd keeps from the forward for grad_B
-    (finetune/lora.py:219-220).  None when rank == 0 or when the decode-step
-    kernels take the call (<= 16 tokens, K % 512 == 0: they form Ts themselves).
-    """
-    N, K = _matrix_shape(weight)
-    x2 = _flat(x, K)
+
+def keeps_ts(layout, M, K, rank):
+    """Whether the forward leaves Ts = bf16(s * X . A^T) in the first M * 128
+    bytes of its workspace (the rule fl_bwd_ts documents): every LoRA call but
+    the decode-step kernels' (group-128 layout, <= 16 tokens, K % 512 == 0)."""
+    return rank > 0 and M > 0 and not (layout == 0 and M <= 16 and K % 512 == 0)
+
+
+def launch_fwd(layout, x2, payload, scales, lut, N, A=None, B=None, scale=0.0):
+    """One forward call on raw record parts: x2 bf16 [M, K] contiguous ->
+    (Y bf16 [M, N], workspace uint8 or None).  A/B fp32 [rank, K] / [N, rank]."""
+    M, K = x2.shape
     rank = 0 if A is None else A.shape[0]
-    _need_cuda(x2, weight.payload, A, B)
+    _need_cuda(x2, payload, A, B)
     if rank:
-        if A.dtype != torch.float32 or B.dtype != torch.float32 or tuple(A.shape) != (rank, K) \
+        if A.dtype != torch.float32 or B is None or B.dtype != torch.float32 or tuple(A.shape) != (rank, K) \
                 or tuple(B.shape) != (N, rank):
             raise ValueError("LoRA factors must be fp32 A[rank, K] and B[N, rank]")
         A = A.detach().contiguous()
         B = B.detach().contiguous()
-    M = x2.shape[0]
     y = torch.empty((M, N), dtype=torch.bfloat16, device=x2.device)
     ws_bytes = _lib.load().fl_fwd_workspace_bytes(M, K, rank)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device) if ws_bytes else None
     if M:
-        _lib.call("fl_fwd", _ptr(x2), M, K, _ptr(weight.payload), _ptr(weight.scales), _ptr(weight.lut), N,
-                  _ptr(A), _ptr(B), rank, float(scale), _ptr(y), _ptr(ws), ws_bytes, _stream())
-    y = y.view(*x.shape[:-1], N)
-    if not return_ts:
-        return y
-    # fl_fwd leaves Ts in the first M * 128 bytes of its workspace except on the
-    # decode-step path (the rule fl_bwd_ts documents).
-    keeps_ts = rank > 0 and M > 0 and not (M <= 16 and K % 512 == 0)
-    return y, (ws[:M * 128].view(torch.bfloat16).view(M, 64) if keeps_ts else None)
+        _lib.call(_FWD_ENTRY[layout], _ptr(x2), M, K, _ptr(payload), _ptr(scales), _ptr(lut), N, _ptr(A), _ptr(B),
+                  rank, float(scale), _ptr(y), _ptr(ws), ws_bytes, _stream())
+    return y, ws
 
 
-def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False, ts=None):
-    """Returns (dX, dA, dB) of fwd(); dA/dB are fp32 (accumulated into when given and accumulate).
+def ts_view(ws, M):
+    """The Ts rows a forward left at the start of its workspace ([M, 64] bf16)."""
+    return ws[:M * 128].view(torch.bfloat16).view(M, 64)
 
-    ts: the Ts that ``fwd(..., return_ts=True)`` returned for the same x, A and
-    scale; X . A^T is then not recomputed (results identical)."""
-    N, K = _matrix_shape(weight)
-    dy2 = _flat(dy, N)
+
+def launch_bwd(layout, dy2, x2, payload, scales, lut, K, A=None, B=None, scale=0.0, dA=None, dB=None,
+               accumulate=False, ts=None):
+    """One backward call on raw record parts -> (dX bf16 [M, K], dA, dB)."""
+    M, N = dy2.shape
     rank = 0 if A is None else A.shape[0]
-    M = dy2.shape[0]
-    x2 = _flat(x, K) if rank else None
-    _need_cuda(dy2, x2, weight.payload, A, B)
+    _need_cuda(dy2, x2, payload, A, B)
     dx = torch.empty((M, K), dtype=torch.bfloat16, device=dy2.device)
     if rank:
+        if A.dtype != torch.float32 or B is None or B.dtype != torch.float32 or tuple(A.shape) != (rank, K) \
+                or tuple(B.shape) != (N, rank):
+            raise ValueError("LoRA factors must be fp32 A[rank, K] and B[N, rank]")
+        if x2 is None or tuple(x2.shape) != (M, K):
+            raise ValueError(f"the LoRA backward needs the forward's input [{M}, {K}]")
         A = A.detach().contiguous()
         B = B.detach().contiguous()
         if dA is None:
@@ -122,54 +126,66 @@ def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None
         if ts.dtype != torch.bfloat16 or tuple(ts.shape) != (M, 64) or not ts.is_contiguous():
             raise ValueError("ts must be the [tokens, 64] bf16 Ts that fwd(..., return_ts=True) returned")
         _need_cuda(ts)
+    plain, with_ts = _BWD_ENTRY[layout]
     if M and ts is not None and rank:
-        _lib.call("fl_bwd_ts", _ptr(dy2), _ptr(x2), M, N, K, _ptr(weight.payload), _ptr(weight.scales),
-                  _ptr(weight.lut), _ptr(A), _ptr(B), rank, float(scale), _ptr(ts), _ptr(dx), _ptr(dA),
-                  _ptr(dB), int(bool(accumulate)), _ptr(ws), ws_bytes, _stream())
+        _lib.call(with_ts, _ptr(dy2), _ptr(x2), M, N, K, _ptr(payload), _ptr(scales), _ptr(lut), _ptr(A), _ptr(B),
+                  rank, float(scale), _ptr(ts), _ptr(dx), _ptr(dA), _ptr(dB), int(bool(accumulate)), _ptr(ws),
+                  ws_bytes, _stream())
     elif M:
-        _lib.call("fl_bwd", _ptr(dy2), _ptr(x2), M, N, K, _ptr(weight.payload), _ptr(weight.scales),
-                  _ptr(weight.lut), _ptr(A), _ptr(B), rank, float(scale), _ptr(dx), _ptr(dA), _ptr(dB),
-                  int(bool(accumulate)), _ptr(ws), ws_bytes, _stream())
+        _lib.call(plain, _ptr(dy2), _ptr(x2), M, N, K, _ptr(payload), _ptr(scales), _ptr(lut), _ptr(A), _ptr(B),
+                  rank, float(scale), _ptr(dx), _ptr(dA), _ptr(dB), int(bool(accumulate)), _ptr(ws), ws_bytes,
+                  _stream())
     elif rank and not accumulate:
         dA.zero_()
         dB.zero_()
+    return dx, dA, dB
+
+
+def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0, return_ts=False):
+    """Y = x . W^T + scale * (x . A^T) . B^T  (bf16 out; plain frozen linear if A is None).
+
+    return_ts: also return Ts = bf16(scale * x . A^T) ([tokens, 64] bf16, zero past
+    the rank) as a view of the call's workspace, for ``bwd(..., ts=)`` -- the
+    intermediate the reference's autograd keeps from the forward for grad_B
+    (finetune/lora.py:219-220).  None when rank == 0 or when the decode-step
+    kernels take the call (<= 16 tokens, K % 512 == 0: they form Ts themselves).
+    """
+    N, K = _matrix_shape(weight)
+    x2 = _flat(x, K)
+    rank = 0 if A is None else A.shape[0]
+    y, ws = launch_fwd(0, x2, weight.payload, weight.scales, weight.lut, N, A, B, scale)
+    y = y.view(*x.shape[:-1], N)
+    if not return_ts:
+        return y
+    M = x2.shape[0]
+    return y, (ts_view(ws, M) if keeps_ts(0, M, K, rank) else None)
+
+
+def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False, ts=None):
+    """Returns (dX, dA, dB) of fwd(); dA/dB are fp32 (accumulated into when given and accumulate).
+
+    ts: the Ts that ``fwd(..., return_ts=True)`` returned for the same x, A and
+    scale; X . A^T is then not recomputed (results identical)."""
+    N, K = _matrix_shape(weight)
+    dy2 = _flat(dy, N)
+    rank = 0 if A is None else A.shape[0]
+    x2 = _flat(x, K) if rank else None
+    dx, dA, dB = launch_bwd(0, dy2, x2, weight.payload, weight.scales, weight.lut, K, A, B, scale, dA, dB,
+                            accumulate, ts)
     return dx.view(*dy.shape[:-1], K), dA, dB
 
 
-class FrozenLoRALinear(torch.autograd.Function):
-    """Autograd node of the fused frozen projection (weight frozen, A/B trainable)."""
-
-    @staticmethod
-    def forward(ctx, x, A, B, weight, scale):
-        ctx.weight = weight
-        ctx.scale = scale
-        ctx.has_lora = A is not None
-        if ctx.has_lora:
-            ctx.save_for_backward(x, A, B)
-        else:
-            ctx.save_for_backward(x)
-        if not ctx.has_lora:
-            return fwd(x, weight)
-        # Keep Ts = bf16(scale * x . A^T) for the backward, as the reference's
-        # autograd keeps F.linear(x, A) for grad_B.
-        y, ctx.ts = fwd(x, weight, A, B, scale, return_ts=True)
-        return y
-
-    @staticmethod
-    def backward(ctx, dy):
-        if ctx.has_lora:
-            x, A, B = ctx.saved_tensors
-            dx, dA, dB = bwd(dy.contiguous(), x, ctx.weight, A, B, ctx.scale, ts=ctx.ts)
-            ctx.ts = None
-            return dx, dA, dB, None, None
-        (x,) = ctx.saved_tensors
-        dx, _, _ = bwd(dy.contiguous(), x, ctx.weight)
-        return dx, None, None, None, None
-
-
 def frozen_lora_linear(x, weight: PackedWeight, A=None, B=None, scale=0.0):
-    """Autograd-capable Y = x . W^T + scale * (x . A^T) . B^T over a packed frozen weight."""
-    return FrozenLoRALinear.apply(x, A, B, weight, float(scale))
+    """Autograd-capable Y = x . W^T + scale * (x . A^T) . B^T over a packed frozen weight.
+
+    Runs the ``spilltune_b200::frozen_lora_linear`` custom op (registered in
+    ``spilltune_b200.library``), whose backward returns (dX, dA, dB) from one
+    fused call, so ``torch.autograd.grad(output, [hidden, A0, B0, ...])`` inside
+    the reference's ``StreamingBlockFunction.backward`` (training/recompute.py:
+    102-127) accumulates into ``grad_A``/``grad_B`` exactly as before."""
+    from . import library
+    N, K = _matrix_shape(weight)
+    return library.frozen_linear(x, weight.payload, weight.scales, weight.lut, N, K, 0, A, B, scale)
 
 
 def lora_projection_forward(proj, x, weight: PackedWeight, base_bias=None):

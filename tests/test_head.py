@@ -29,6 +29,14 @@ def test_argument_checks():
         hd._ChunkedCE.forward(None, n, h, l[:, :4], 1.0, 4, ((0, 4),))
     with pytest.raises(ValueError, match="CUDA tensors"):
         hd.chunked_causal_loss(n, h, l, normalization=1.0, token_chunk=4)
+    # A target outside [0, V) that is not the ignore index: F.cross_entropy raises, so does this.
+    bad = l.clone()
+    bad[0, 3] = 32
+    with pytest.raises(ValueError, match="out of bounds"):
+        hd._ChunkedCE.forward(None, n, h, bad, 1.0, 4, ((0, 4),))
+    bad[0, 3] = -3
+    with pytest.raises(ValueError, match="out of bounds"):
+        hd._ChunkedCE.forward(None, n, h, bad, 1.0, 4, ((0, 4),))
 
 
 @pytest.mark.gpu

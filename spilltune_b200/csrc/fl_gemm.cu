@@ -65,6 +65,9 @@ constexpr int kQBytes = kLanes * kStageK / 2;  // 4 KiB packed-code tile
 constexpr int kGroups = 3;                     // dequant warp groups (4 warps each)
 constexpr int kThreads = 64 + 128 * kGroups;   // 2 control warps + dequant/epilogue warps
 static_assert(kAccCols + kStages * kAStageCols <= kTmemCols, "TMEM budget");
+// A decode group's consecutive stages are at most 2 * kGroups apart; at most
+// kStages keeps its parity waits on a ring slot within one phase.
+static_assert(2 * kGroups <= kStages, "decode-group rotation longer than the stage ring");
 
 struct GemmArgs {
   const float* scales;  // fp32 [N * K/128]
@@ -352,7 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     // Order per tile: the group's first stage pair of this tile, then the
-    // previous tile's epilogue, then the rest of this tile.  The first pairs of
+    // previous tile's epilogue, then the rest of this tile (see `first` below
+    // for which pairs a group takes).  The first pairs of
     // all groups fill the stage ring, so the MMA issuer restarts on decoded
     // stages as soon as the accumulator is released.  Every epilogue warp
     // walks every tile of the pair (also after an abort): the named barriers
@@ -360,6 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int g0 = 0;  // stage counter at the start of the tile
     int tl = 0;
     Tile prev{};
+    const int pairs_per_tile = (n_iter + 1) / 2;  // the last one a single stage when n_iter is odd
     for (int t = pair; t < n_tiles; t += num_pairs, g0 += n_iter, ++tl) {
       const Tile tile = tile_at(args, t, num_w, num_m);
       const int l0 = tile.w_tile * (2 * kLanes) + static_cast<int>(crank) * kLanes;
@@ -373,9 +378,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr bool kBlock64 = kLayout == kLayoutNf4Dq64;
       const int spr = kBlock64 ? 2 * groups_per_row : groups_per_row;
       const float* srow = args.scales + static_cast<size_t>(wrow0 + (valid ? n : 0)) * spr;
-      float next_scale = (valid && grp < groups_per_row) ? __ldg(srow + (kBlock64 ? 2 * grp : grp)) : 0.0f;
-      float next_scale2 = (kBlock64 && valid && grp < groups_per_row) ? __ldg(srow + 2 * grp + 1) : 0.0f;
-      for (int pit = 2 * grp; pit < n_iter || (pit == 2 * grp && tl > 0); pit += 2 * kGroups) {
+      // The groups take the stage pairs of the CTA pair's whole stage sequence in
+      // turn (tile tl starts a new pair, number tl * pairs_per_tile), not afresh
+      // per tile: consecutive stages of one group are then never more than
+      // 2 * kGroups <= kStages apart, so a group never waits on a ring slot
+      // whose barrier is two phases behind (the parity wait would pass).
+      const int first = (grp - (tl * pairs_per_tile) % kGroups + kGroups) % kGroups;
+      const int pit0 = 2 * first;
+      float next_scale = (valid && first < groups_per_row) ? __ldg(srow + (kBlock64 ? 2 * first : first)) : 0.0f;
+      float next_scale2 = (kBlock64 && valid && first < groups_per_row) ? __ldg(srow + 2 * first + 1) : 0.0f;
+      for (int pit = pit0; pit < n_iter || (pit == pit0 && tl > 0); pit += 2 * kGroups) {
         if (pit < n_iter && ok) {
           ProductTable table;
           float sc_a = 0.f, sc_b = 0.f;  // layout 1: the pair's two block scales
@@ -441,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ok = __all_sync(0xffffffffu, ok) != 0;
         }
-        if (pit == 2 * grp && tl > 0) epilogue(prev, tl - 1);
+        if (pit == pit0 && tl > 0) epilogue(prev, tl - 1);
       }
       prev = tile;
     }

@@ -43,6 +43,9 @@ constexpr int kGroupM = 4;                 // token tiles per band: a band's pai
 constexpr int kGroups = 3;                 // decode warp groups
 constexpr int kThreads = 64 + 128 * kGroups;
 constexpr int kEpiWarps = 4 * kGroups;
+// A decode group's consecutive stages are at most 2 * kGroups apart; at most
+// kStages keeps its parity waits on a ring slot within one phase.
+static_assert(2 * kGroups <= kStages, "decode-group rotation longer than the stage ring");
 constexpr int kAccCols = 256;              // fp32 accumulator columns (pair N)
 constexpr int kTmemCols = 2 * kAccCols;    // two accumulators: tile t+1 accumulates while tile t drains
 constexpr int kABytes = kTokHalf * kStageN * 2;   // 16 KiB dY (or Us) tile
@@ -307,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int g0 = 0;
     int tl = 0;
     Tile prev{};
+    const int pairs_per_tile = (n_iter + 1) / 2;  // the last one a single stage when n_iter is odd
     for (int tt = pair; tt < n_tiles; tt += num_pairs, g0 += n_iter, ++tl) {
       const Tile tile = tile_at(args, tt, num_k, num_m);
       const int kb = tile.k_tile * 2 * kColHalf + static_cast<int>(crank) * kColHalf;
@@ -326,8 +330,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                    ? __ldg(args.scales + static_cast<size_t>(wrow0 + it * kStageN + r) * spr + gsc)
                    : 0.0f;
       };
-      float next0 = load_scale(2 * grp), next1 = load_scale(2 * grp + 1);
-      for (int pit = 2 * grp; pit < n_iter || (pit == 2 * grp && tl > 0); pit += 2 * kGroups) {
+      // The groups take the stage pairs of the CTA pair's whole stage sequence
+      // in turn (tile tl starts a new pair, number tl * pairs_per_tile), not
+      // afresh per tile: consecutive stages of one group are then never more
+      // than 2 * kGroups == kStages apart, so a group never waits on a ring
+      // slot whose barrier is two phases behind (the parity wait would pass).
+      const int first = (grp - (tl * pairs_per_tile) % kGroups + kGroups) % kGroups;
+      const int pit0 = 2 * first;
+      float next0 = load_scale(pit0), next1 = load_scale(pit0 + 1);
+      for (int pit = pit0; pit < n_iter || (pit == pit0 && tl > 0); pit += 2 * kGroups) {
         const float pair_scale[2] = {next0, next1};
         next0 = load_scale(pit + 2 * kGroups);
         next1 = load_scale(pit + 2 * kGroups + 1);
@@ -389,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ok = __all_sync(0xffffffffu, ok) != 0;
         }
-        if (pit == 2 * grp && tl > 0) epilogue(prev, tl - 1);
+        if (pit == pit0 && tl > 0) epilogue(prev, tl - 1);
       }
       prev = tile;
     }

@@ -21,6 +21,16 @@ reference; they only read these committed vectors.
 * ``deepseek_route.npz`` — the reference's DeepSeek-V3 router
   (``adapters/deepseek.py:115-126``): 16 experts in 4 groups, 2 kept, top-4,
   normalised, scale 2.5; indices and weights sorted by expert id per token.
+* ``head_small.npz`` — the reference's ``chunked_causal_loss``
+  (``quantization/native_terminal.py:11-47``) on seeded bf16 hidden states,
+  a bf16 head and labels with ignored (-100) positions: loss and the hidden
+  states' gradient.
+* ``tiny_llama_train.npz`` — the reference's own training engine
+  (``training/engine.py:run``, adapter ``llama``, int4-sym-g128 storage, CPU)
+  on the tiny Llama of ``tests/e2e_tiny.py`` for 50 AdamW steps: the per-step
+  losses, every LoRA projection's gradients after steps 1 and 2, its A and B
+  after step 50, and checksums of the initial A (to confirm the tests draw the
+  same initial state).
 """
 import os
 import sys
@@ -32,8 +42,11 @@ from ram_vram_finetune.quantization import codecs
 from ram_vram_finetune.finetune.lora import LoRAProjection
 from ram_vram_finetune.adapters.qwen3_moe import moe_feed_forward
 from ram_vram_finetune.adapters.deepseek import route as deepseek_route
+from ram_vram_finetune.quantization.native_terminal import chunked_causal_loss
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(HERE))  # tests/: the shared tiny-Llama definition
+import e2e_tiny  # noqa: E402
 
 
 def bits(t):
@@ -128,9 +141,85 @@ def moe_case():
         scale=2.5, indices=torch.gather(ri, 1, order).numpy(), weights=torch.gather(rw, 1, order).numpy())
 
 
+def head_case():
+    Bsz, S, H, V, chunk = 2, 70, 128, 512, 32
+    g = torch.Generator().manual_seed(31)
+    normalized = torch.randn(Bsz, S, H, generator=g).to(torch.bfloat16)
+    head = (torch.randn(V, H, generator=g) * 0.05).to(torch.bfloat16)
+    labels = torch.randint(0, V, (Bsz, S), generator=g)
+    labels[torch.rand(Bsz, S, generator=g) < 0.25] = -100
+    labels[:, 33:50] = -100  # a whole chunk with no supervised token is skipped
+    norm = float((labels[:, 1:] != -100).sum())
+    x = normalized.clone().requires_grad_(True)
+    loss = chunked_causal_loss(x, head, labels, normalization=norm, token_chunk=chunk)
+    (dx,) = torch.autograd.grad(loss, (x,))
+    np.savez_compressed(
+        os.path.join(HERE, "head_small.npz"), B=Bsz, S=S, H=H, V=V, token_chunk=chunk, normalization=norm,
+        normalized_bf16=bits(normalized), head_bf16=bits(head), labels=labels.numpy(),
+        loss=np.float32(loss.detach()), dnormalized_bf16=bits(dx))
+
+
+def tiny_llama_training():
+    """The reference engine on the tiny Llama (see tests/e2e_tiny.py)."""
+    import json
+    import tempfile
+    from safetensors.torch import save_file
+    from transformers.models.llama.configuration_llama import LlamaConfig
+    from ram_vram_finetune.config import TrainConfig
+    from ram_vram_finetune.training import engine
+    t = e2e_tiny
+    tmp = tempfile.mkdtemp(prefix="tiny_llama_")
+    model = os.path.join(tmp, "model")
+    os.makedirs(model)
+    cfg = LlamaConfig(vocab_size=t.VOCAB, hidden_size=t.HIDDEN, intermediate_size=t.INTER,
+                      num_hidden_layers=t.LAYERS, num_attention_heads=t.HEADS, num_key_value_heads=t.KV_HEADS,
+                      head_dim=t.HEAD_DIM, max_position_embeddings=t.MAX_POS, rms_norm_eps=t.EPS,
+                      attention_dropout=0.0, tie_word_embeddings=False, use_cache=False,
+                      rope_parameters={"rope_type": "default", "rope_theta": t.THETA})
+    with open(os.path.join(model, "config.json"), "w") as f:
+        f.write(json.dumps(cfg.to_dict(), indent=2) + "\n")
+    state = {k: v.contiguous() for k, v in t.model_state().items()}
+    save_file(state, os.path.join(model, "model.safetensors"))
+    dataset = os.path.join(tmp, "rows.jsonl")
+    with open(dataset, "w") as f:
+        for ids, labels in t.token_rows():
+            f.write(json.dumps({"input_ids": ids[0].tolist(), "labels": labels[0].tolist()}) + "\n")
+    config = TrainConfig(model=model, dataset=dataset, output=os.path.join(tmp, "out"), adapter="llama",
+                         device="cpu", steps=t.STEPS, accumulation=t.ACCUM, rank=t.RANK, alpha=t.ALPHA,
+                         learning_rate=t.LR, weight_decay=0.0, seed=t.SEED, token_chunk=t.TOKEN_CHUNK,
+                         max_sequence_length=t.SEQ, checkpoint_every=10 ** 6, quantization="int4-sym-g128")
+    out = {}
+
+    def capture(event, data):
+        adapter = data.get("adapter")
+        projs = {f"{b.index}:{name}": p for b in adapter.blocks for name, p in b.adapters.items()} if adapter else {}
+        if event == "adapter_ready":
+            for k, p in projs.items():
+                out[f"{k}/A0_sum"] = np.float64(p.A.detach().double().sum())
+                out[f"{k}/A0_head"] = p.A.detach()[0, :8].numpy().copy()
+        elif event == "step" and data["metrics"]["step"] in (1, 2):
+            st = data["metrics"]["step"]
+            for k, p in projs.items():
+                out[f"{k}/step{st}_grad_A"] = p.grad_A.numpy().copy()
+                out[f"{k}/step{st}_grad_B"] = p.grad_B.numpy().copy()
+        elif event == "training_complete":
+            for k, p in projs.items():
+                out[f"{k}/final_A"] = p.A.detach().numpy().copy()
+                out[f"{k}/final_B"] = p.B.detach().numpy().copy()
+
+    report = engine.run(config, progress_callback=capture)
+    assert report["status"] == "completed"
+    losses = np.array([m["loss"] for m in report["metrics"]], dtype=np.float64)
+    np.savez_compressed(os.path.join(HERE, "tiny_llama_train.npz"), losses=losses, **out)
+    print("tiny llama losses", losses[:3], "...", losses[-3:], file=sys.stderr)
+
+
+CASES = {"codec": codec_cases, "lora": lora_case, "moe": moe_case, "head": head_case,
+         "tiny_llama": tiny_llama_training}
+
 if __name__ == "__main__":
+    # `make_golden.py [case ...]` regenerates only the named fixtures (all by default).
     torch.set_num_threads(1)
-    codec_cases()
-    lora_case()
-    moe_case()
+    for name in sys.argv[1:] or list(CASES):
+        CASES[name]()
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")), file=sys.stderr)

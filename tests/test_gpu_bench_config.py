@@ -91,3 +91,46 @@ def test_lora_with_out_features_not_multiple_of_128(cuda_lib, M, N, K, rank):
     assert torch.equal(out, y)
     assert ol.rel_l2(gx.cpu(), rdx) <= TIGHT and ol.rel_l2(gA.cpu(), rdA) <= TIGHT
     assert ol.rel_l2(gB.cpu(), rdB) <= TIGHT
+
+
+# Stage counts per tile (reduction / 64, + 1 with a LoRA branch) whose decode-group
+# rotation used to leave one group two ring phases ahead at a tile boundary, with
+# enough tiles that every CTA pair walks several: backward 8, 9, 10, 15 stages and
+# forward 10, 16, 64 stages.  Every wait must complete (status word 0) and the
+# results must match the FP32 shadow on sampled rows.
+ROTATION_CASES = [
+    # direction, M, N, K, rank
+    ("bwd", 2048, 576, 7168, 16),
+    ("bwd", 2048, 576, 7168, 0),
+    ("bwd", 2048, 640, 7168, 0),
+    ("bwd", 4096, 512, 4096, 0),
+    ("bwd", 4096, 896, 4096, 16),
+    ("fwd", 4096, 4096, 640, 0),
+    ("fwd", 4096, 4096, 1024, 0),
+    ("fwd", 8192, 4096, 4096, 0),
+]
+
+
+@pytest.mark.parametrize("direction,M,N,K,rank", ROTATION_CASES)
+def test_stage_counts_across_tile_boundaries(cuda_lib, direction, M, N, K, rank):
+    from spilltune_b200 import _lib, ops
+    s = 2.0
+    pw, x, A, B, dy = _problem(M, N, K, max(rank, 1), seed=M + 3 * N + K, codec_name="nf4-g128")
+    if not rank:
+        A = B = None
+    pwc, xc, dyc = pw.to("cuda"), x.cuda(), dy.cuda()
+    Ac, Bc = (A.cuda(), B.cuda()) if rank else (None, None)
+    torch.cuda.synchronize()
+    assert _lib.status(reset=True) == 0
+    out = ops.fwd(xc, pwc, Ac, Bc, s) if direction == "fwd" else ops.bwd(dyc, xc, pwc, Ac, Bc, s)[0]
+    torch.cuda.synchronize()
+    assert _lib.status() == 0
+    W = _decode_cpu(pw)
+    rows = torch.arange(0, M, 97)
+    if direction == "fwd":
+        ref = x[rows].float() @ W.float().t()
+    else:
+        ref = dy[rows].float() @ W.float()
+        if rank:
+            ref = ref + s * (dy[rows].float() @ B) @ A
+    assert ol.rel_l2(out[rows.cuda()].cpu(), ref) <= TIGHT

@@ -82,3 +82,39 @@ def test_llama3_head_shape_chunk(cuda_lib):
     p[~keep[rows]] = 0
     ref_dh = p.to(torch.bfloat16).float() @ head.float()
     assert ol.rel_l2(dh[rows].cpu(), ref_dh.cpu()) <= 1e-2
+
+
+def _golden():
+    import os
+    import numpy as np
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "head_small.npz"))
+    bf = lambda a, shp: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).view(*shp)
+    B, S, H, V = (int(g[k]) for k in ("B", "S", "H", "V"))
+    return (bf(g["normalized_bf16"], (B, S, H)), bf(g["head_bf16"], (V, H)), torch.from_numpy(g["labels"]),
+            float(g["normalization"]), int(g["token_chunk"]), float(g["loss"]), bf(g["dnormalized_bf16"], (B, S, H)))
+
+
+def _chunks(labels, S, chunk):
+    return tuple((s, min(s + chunk, S - 1)) for s in range(0, S - 1, chunk)
+                 if bool((labels[:, s + 1:min(s + chunk, S - 1) + 1] != -100).any()))
+
+
+def test_oracle_matches_reference_golden():
+    """oracle/head.py against the reference's own chunked_causal_loss output
+    (tests/golden/head_small.npz, made by tests/golden/make_golden.py)."""
+    normalized, head, labels, norm, chunk, ref_loss, ref_grad = _golden()
+    loss, vjp = oh.chunked_ce(normalized, head, labels, norm, _chunks(labels, normalized.shape[1], chunk))
+    assert abs(float(loss) - ref_loss) <= 1e-6 * abs(ref_loss)
+    assert ol.rel_l2(vjp, ref_grad) <= 1e-6
+
+
+@pytest.mark.gpu
+def test_fused_head_matches_reference_golden(cuda_lib):
+    from spilltune_b200 import head as hd
+    normalized, head, labels, norm, chunk, ref_loss, ref_grad = _golden()
+    x = normalized.cuda().requires_grad_(True)
+    loss = hd.chunked_causal_loss(x, head.cuda(), labels.cuda(), normalization=norm, token_chunk=chunk,
+                                  supervised_chunks=_chunks(labels, normalized.shape[1], chunk))
+    (vjp,) = torch.autograd.grad(loss, (x,))
+    assert abs(float(loss) - ref_loss) <= 1e-3 * abs(ref_loss)
+    assert ol.rel_l2(vjp.cpu(), ref_grad) <= 1e-2

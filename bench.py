@@ -58,8 +58,9 @@ def parse():
     p.add_argument("--codec", default="nf4-g128")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--cpu-sample-tokens", type=int, default=0,
-                   help="tokens in the CPU-baseline sample (0: grow from 256 until one layer takes >= 10 s)")
+    p.add_argument("--cpu-passes", type=int, default=2,
+                   help="timed one-layer passes of the reference CPU path for this arm's cpu_baseline")
+    p.add_argument("--no-ref-gpu", action="store_true", help="reference arm: skip the reference's GPU path")
     # single-op and sweep modes (for profiling; no JSON bench line)
     p.add_argument("--op", choices=["fwd", "bwd", "dequant"], default=None,
                    help="run one frozen-linear call at --M/--N/--K instead of the training step")
@@ -278,73 +279,125 @@ def measured_peaks():
         return 1400.0, 6650.0, "fallback"
 
 
-# ---------------------------------------------------------------- CPU baseline
-def cpu_baseline(tokens, codec_name, warm=1, reps=1, threads=None):
-    """The oracle's restatement of the reference CPU path on a bounded sample:
-    one Llama-3-8B layer (7 projections) at `tokens` tokens: decode_into of
-    every matrix (forward load and backward reload, memory.py:224-229),
-    LoRAProjection.forward in the reference op order, the recomputed forward
-    and its autograd backward (recompute.py:85-127).  Scaled to 32 layers."""
-    import numpy as np
-    import oracle.codec as oc
-    import oracle.linear as ol
-    from spilltune_b200 import codec
+# ---------------------------------------------------------------- the reference's own path
+class ReferenceLayerPass:
+    """One layer of the step through the reference's own implementation of the
+    path, restated by the oracle (test infrastructure; the reference itself is
+    pure Python and does not travel to the GPU box):
+
+    * ``SlotSession.load`` (memory.py:224-229) decodes every packed matrix of
+      the layer into a BF16 slot with ``decode_into`` (quantization/codecs.py:
+      158-170; ``oracle.codec.decode_torch``, bit-exact), once for the forward
+      and again for the recompute;
+    * ``LoRAProjection.forward`` (finetune/lora.py:205-220): BF16 ``F.linear``
+      plus the two FP32 LoRA ``F.linear``s, for q, k, v, o, gate, up, down;
+    * ``StreamingBlockFunction.backward`` (training/recompute.py:85-127): the
+      recomputed forward and its autograd VJP (dX, dA, dB) per projection;
+    * the FP32 AdamW update of the layer's LoRA factors (finetune/optimizer.py).
+
+    On the CPU this is the reference's CPU path (torch with every host thread);
+    on a CUDA device it is the reference's GPU path (torch elementwise decode +
+    cuBLAS).  Weights are random packed records with the statistics of
+    NF4/int4-encoded N(0, 0.02) weights, in two alternating layer sets."""
+
+    def __init__(self, tokens, codec_name, device, seed=3, sets=2):
+        import oracle.codec as oc
+        import oracle.linear as ol
+        from spilltune_b200 import codec
+        self.oc, self.ol = oc, ol
+        self.device = torch.device(device)
+        self.tokens = tokens
+        g = torch.Generator().manual_seed(seed)
+        lut = (codec.NF4_LUT if codec_name == "nf4-g128" else codec.INT4_SYM_LUT).to(self.device)
+        self.lut = lut
+        self.sets = []
+        for _ in range(sets):
+            recs = {}
+            for name, N, K, _src in PROJ:
+                groups = N * K // 128
+                payload = torch.randint(0, 256, (groups * 64,), dtype=torch.uint8, generator=g)
+                scales = (0.02 * (2.5 + 0.3 * torch.rand(groups, generator=g))).float()
+                recs[name] = (payload.to(self.device), scales.to(self.device), N, K)
+            self.sets.append(recs)
+        self.slot = {name: torch.empty(N, K, dtype=torch.bfloat16, device=self.device) for name, N, K, _s in PROJ}
+        self.xs = {k: torch.randn(tokens, w, generator=g).to(torch.bfloat16).to(self.device)
+                   for k, w in INPUT_WIDTH.items()}
+        self.dys = {name: torch.randn(tokens, N, generator=g).to(torch.bfloat16).to(self.device)
+                    for name, N, _K, _s in PROJ}
+        self.lora = {}
+        for name, N, K, _s in PROJ:
+            A = (torch.randn(RANK, K, generator=g) * 0.01).to(self.device).requires_grad_(True)
+            B = (torch.randn(N, RANK, generator=g) * 0.01).to(self.device).requires_grad_(True)
+            self.lora[name] = (A, B, torch.zeros_like(A.detach()), torch.zeros_like(B.detach()))
+        params = [t for A, B, _a, _b in self.lora.values() for t in (A, B)]
+        self.opt = torch.optim.AdamW(params, lr=1e-4, foreach=False)
+
+    def _load(self, recs):
+        for name, (payload, scales, N, K) in recs.items():
+            self.oc.decode_torch(payload, scales, N * K, self.lut, self.slot[name])
+
+    def __call__(self, layer):
+        s = ALPHA / RANK
+        recs = self.sets[layer % len(self.sets)]
+        self._load(recs)                                        # forward load
+        with torch.no_grad():
+            for name, _N, _K, src in PROJ:
+                A, B, _ga, _gb = self.lora[name]
+                self.ol.lora_forward_reference(self.xs[src], self.slot[name], A, B, s)
+        self._load(recs)                                        # reload for the recompute
+        for name, _N, _K, src in reversed(PROJ):
+            A, B, ga, gb = self.lora[name]
+            _y, _dx, da, db = self.ol.lora_backward_reference(self.xs[src], self.slot[name], A, B, s,
+                                                              self.dys[name])
+            ga.copy_(da)
+            gb.copy_(db)
+            A.grad, B.grad = ga, gb
+        self.opt.step()
+
+
+def reference_cpu_sample(tokens, codec_name, steps, warm=1, threads=None):
+    """Time `steps` one-layer passes of the reference's CPU path (after `warm`
+    untimed ones).  Every layer of the 32-layer stack has the same shapes and
+    cost, so the stack's tokens/s is tokens / (32 x one layer pass)."""
     threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(3)
-    recs = {}
-    for name, N, K, _src in PROJ:
-        # random NF4 codes / absmax scales with the statistics of encoded N(0, 0.02) weights
-        groups = N * K // 128
-        payload = torch.randint(0, 256, (groups * 64,), dtype=torch.uint8, generator=g).numpy()
-        scales = (0.02 * (2.5 + 0.3 * torch.rand(groups, generator=g))).numpy().astype(np.float32)
-        recs[name] = (payload, scales, N, K)
-    lut = (codec.NF4_LUT if codec_name == "nf4-g128" else codec.INT4_SYM_LUT).numpy()
-    xs = {k: torch.randn(tokens, w, generator=g).to(torch.bfloat16) for k, w in INPUT_WIDTH.items()}
-    dys = {name: torch.randn(tokens, N, generator=g).to(torch.bfloat16) for name, N, _K, _s in PROJ}
-    lo = {name: (torch.randn(RANK, K, generator=g) * 0.01, torch.randn(N, RANK, generator=g) * 0.01)
-          for name, N, K, _s in PROJ}
-
-    def decode(name):
-        p, s, N, K = recs[name]
-        bits = oc.decode(p, s, N * K, lut=lut, threads=threads)
-        return torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).view(N, K)
-
-    def one_layer():
-        W = {name: decode(name) for name, *_ in PROJ}          # forward load
-        for name, _N, _K, src in PROJ:
-            A, B = lo[name]
-            ol.lora_forward_reference(xs[src], W[name], A, B, ALPHA / RANK)
-        W = {name: decode(name) for name, *_ in PROJ}          # backward reload
-        for name, _N, _K, src in reversed(PROJ):
-            A, B = lo[name]
-            ol.lora_backward_reference(xs[src], W[name], A, B, ALPHA / RANK, dys[name])
-
-    for _ in range(warm):
-        one_layer()
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        one_layer()
-    dt = (time.perf_counter() - t0) / reps
-    step_seconds = dt * 32
-    return {"value": tokens / step_seconds, "unit": "tokens/s", "cores": threads, "kind": "port", "tokens": tokens,
-            "sample": f"1 of 32 Llama-3-8B layers (7 projections, fwd + recompute + bwd, 2 decodes), "
-                      f"{tokens} tokens, scaled x32; {reps} timed rep(s) of {dt:.2f} s"}
+    run = ReferenceLayerPass(tokens, codec_name, "cpu")
+    for i in range(warm):
+        run(i)
+    times = []
+    for i in range(steps):
+        t0 = time.perf_counter()
+        run(i)
+        times.append(time.perf_counter() - t0)
+    layer_s = statistics.median(times)
+    return {"value": tokens / (32 * layer_s), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "layer_seconds": times, "tokens": tokens,
+            "sample": f"{steps} timed one-layer passes ({tokens} tokens, 7 projections, 2 decode_into loads, "
+                      f"fwd + recompute + bwd + AdamW) of the 32-layer stack, median {layer_s:.2f} s; "
+                      f"tokens/s = tokens / (32 x median layer pass)"}
 
 
-def cpu_baseline_adaptive(tokens, codec_name, target_s=10.0, cap=8192):
-    """Pick the sample size: double the token count (from 256) until one
-    layer-pass of the oracle takes at least `target_s` seconds or reaches the
-    GPU micro-batch (8192 tokens); then time that sample."""
-    if tokens:
-        return cpu_baseline(tokens, codec_name)
-    t = 256
-    while True:
-        info = cpu_baseline(t, codec_name, warm=0 if t > 256 else 1)
-        layer_s = t / info["value"] / 32
-        if layer_s >= target_s or t >= cap:
-            return info
-        t = min(cap, max(2 * t, int(t * target_s / max(layer_s, 1e-3))))
+def reference_gpu_torch(tokens, codec_name, steps, warmup, layers=32):
+    """The reference's GPU path (torch decode_into on the device, cuBLAS BF16
+    F.linear, FP32 LoRA F.linears, autograd VJP, AdamW) over the whole
+    `layers`-layer step on cuda:0, timed with CUDA events: the comparator the
+    fused kernels replace."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    run = ReferenceLayerPass(tokens, codec_name, dev)
+    step = lambda: [run(l) for l in range(layers)]
+    for _ in range(max(1, warmup)):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    return {"value": tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "what": f"reference GPU path restated (torch decode_into + cuBLAS + FP32 LoRA + autograd + AdamW), "
+                    f"{layers} layers x 7 projections, {tokens} tokens, weights resident packed in HBM"}
 
 
 def bench_config(args, world):
@@ -357,32 +410,34 @@ def bench_config(args, world):
 
 
 def run_reference(args, world, rank):
+    """The reference arm: each step is one measured one-layer pass of the
+    reference's CPU path at the full config (8192 tokens, 7 projections);
+    ms_per_step is that pass's wall time and value the stack's tokens/s
+    (tokens / (32 x median pass)).  Adds the reference's GPU path on cuda:0
+    (ref_gpu_torch) when a GPU is present."""
     if rank != 0:
         return 0
-    steps, warm = max(1, args.steps), max(0, args.warmup)
-    # Each step is one bounded sample; keep the whole run within a few minutes.
-    warm = min(warm, 1)
-    vals = []
-    info = None
-    for i in range(steps):
-        if i == 0:
-            info = cpu_baseline_adaptive(args.cpu_sample_tokens, args.codec)
-            tokens = info["tokens"]
-        else:
-            info = cpu_baseline(tokens, args.codec, warm=0, reps=1)
-        vals.append(info["value"])
-    value = statistics.median(vals)
+    steps = max(1, args.steps)
+    info = reference_cpu_sample(args.tokens, args.codec, steps, warm=min(1, max(0, args.warmup)))
+    value = info["value"]
+    layer_ms = 1e3 * statistics.median(info["layer_seconds"])
+    gpu = None
+    if torch.cuda.is_available() and not args.no_ref_gpu:
+        gpu = reference_gpu_torch(args.tokens, args.codec, steps=min(steps, 3), warmup=1)
     line = {"metric": "train tokens/s (8B NF4 LoRA frozen-linear stack)", "value": value, "unit": "tokens/s",
             "impl": "reference", "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * args.tokens / value, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": layer_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": bench_config(args, world),
+            "step_is": {"layers_timed_per_step": 1, "layers_in_model": 32, "tokens_per_step": args.tokens,
+                        "timed_passes": steps,
+                        "value_formula": "tokens_per_step / (32 x median one-layer pass seconds)"},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
                              "sample": info["sample"]},
-            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "ref_gpu_torch": gpu}
     print(json.dumps(line), flush=True)
     return 0
-
 
 
 # ---------------------------------------------------------------- single-op and sweep modes
@@ -616,7 +671,8 @@ def main():
         achieved = fl / (kern_ms / 1e3) / 1e12
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline_adaptive(args.cpu_sample_tokens, args.codec)
+            cpu = reference_cpu_sample(args.tokens, args.codec, args.cpu_passes)
+            cpu.pop("layer_seconds", None)
         total_flops = step_flops(M, L)
         line = {
             "metric": "train tokens/s (8B NF4 LoRA frozen-linear stack)",

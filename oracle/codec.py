@@ -12,6 +12,7 @@ import os
 import subprocess
 
 import numpy as np
+import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
@@ -180,4 +181,29 @@ def nf4dq_decode(packed, absmax_f32, numel, quant_map=NF4_LUT):
     quant_map = np.ascontiguousarray(quant_map, dtype=np.float32)
     out = np.empty(numel, np.uint16)
     lib().oracle_nf4dq_decode(_ptr(packed), _ptr(absmax_f32), _ptr(quant_map), numel, _ptr(out))
+    return out
+
+
+DECODE_CHUNK_GROUPS = 8192  # codecs.py CHUNK_GROUPS: <= 1,048,576 elements per FP32 chunk
+
+
+def decode_torch(payload, scales, numel, lut, out):
+    """The reference's ``decode_into`` (quantization/codecs.py:158-170) as torch
+    ops, on whatever device the tensors live on: per chunk of 8192 groups,
+    unpack the two codes of every byte (low nibble first, ``unpack_codes``
+    :55-64), map them through the 16-entry codebook (``c - 8`` for int4-sym,
+    exactly the reference's ``.float() - 8``; the NF4 table for nf4-g128),
+    multiply by the group scale in FP32 and round into the BF16 destination.
+    ``out`` is a BF16 tensor of ``numel`` elements (any shape, contiguous).
+    This is the reference's CPU path when run on the CPU, and its GPU path
+    (``SlotSession.load`` decodes on the device, memory.py:224-229) on CUDA."""
+    flat = out.view(-1)
+    groups = (numel + GROUP - 1) // GROUP
+    for g in range(0, groups, DECODE_CHUNK_GROUPS):
+        end = min(g + DECODE_CHUNK_GROUPS, groups)
+        raw = payload[g * 64:end * 64]
+        codes = torch.stack((raw & 15, raw >> 4), 1).flatten().long()
+        values = lut[codes].view(-1, GROUP) * scales[g:end, None]
+        valid = min(end * GROUP, numel) - g * GROUP
+        flat[g * GROUP:g * GROUP + valid].copy_(values.flatten()[:valid])
     return out

@@ -41,8 +41,10 @@ def test_opcheck_frozen_lora_linear(cuda_lib, M, N, K, rank):
     torch.library.opcheck(torch.ops.spilltune_b200.frozen_lora_linear.default, args, **TOL)
     y, ts = torch.ops.spilltune_b200.frozen_lora_linear(*args)
     dy = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+    # The backward op has no autograd formula of its own (no double backward):
+    # its inputs are plain tensors.
     bargs = (dy, xc.detach(), pwc.payload, pwc.scales, pwc.lut, 0,
-             None if Ac is None else Ac.detach(), None if Bc is None else Bc.detach(), 2.0, ts)
+             None if Ac is None else Ac.detach(), None if Bc is None else Bc.detach(), 2.0, ts.detach())
     torch.library.opcheck(torch.ops.spilltune_b200.frozen_lora_linear_backward.default, bargs, **TOL)
 
 

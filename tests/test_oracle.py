@@ -104,3 +104,16 @@ def test_lora_oracle_matches_reference_golden():
     dx32, da32, db32 = ol.lora_backward_fp32(x, W, A, B, alpha / r, dY)
     assert ol.rel_l2(dx, dx32) < 1e-2 and ol.rel_l2(da, da32) < 1e-5 and ol.rel_l2(db, db32) < 1e-5
     assert ol.rel_l2(y, ol.lora_forward_fp32(x, W, A, B, alpha / r)) < 1e-2
+
+
+def test_torch_decode_matches_reference_golden():
+    """oracle.codec.decode_torch (the reference's decode_into as torch ops, used
+    as the reference path in bench.py) gives the reference's own decoded bits."""
+    import torch
+    g = _load("codec_int4.npz")
+    for name in ("len128", "len129", "len257", "kat", "mat32x256"):
+        x = g[f"{name}/input"]
+        out = torch.empty(x.size, dtype=torch.bfloat16)
+        oc.decode_torch(torch.from_numpy(g[f"{name}/payload"]), torch.from_numpy(g[f"{name}/scales"]), x.size,
+                        torch.arange(16, dtype=torch.float32) - 8.0, out)
+        assert np.array_equal(out.view(torch.int16).numpy().view(np.uint16), g[f"{name}/decoded_bf16"]), name

@@ -170,7 +170,11 @@ def test_fused_path_trains_like_reference(cuda_lib):
     torch.cuda.synchronize()
     assert _lib.status() == 0
     worst, errs = _compare(fx, got, blocks, loss_atol=1e-2, grad_tol=dict(rtol=0.06, atol=3e-3), update_rel=5e-2)
-    # Streaming really happened: two loads per layer per micro-batch (forward and recompute).
-    assert session.uploads + session.hits == 2 * t.LAYERS * t.ACCUM * t.STEPS
+    # Every block borrowed its layer twice per micro-batch (forward, recompute);
+    # with two slots for two layers only the first borrow loads on demand (the
+    # second layer is prefetched) and both stay resident (eviction and reload
+    # are covered by tests/test_gpu_streaming.py).
+    assert session.hits == 2 * t.LAYERS * t.ACCUM * t.STEPS - 1
+    assert session.uploads == t.LAYERS
     session.close()
     print(f"worst |loss - reference| over {t.STEPS} steps: {worst:.2e}; LoRA update rel-L2 (A, B): {errs}")

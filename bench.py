@@ -3,7 +3,9 @@
 
 One step = one training pass of the 32-layer frozen-linear stack over one
 micro-batch (micro-batch 4 x seq 2048 = 8192 tokens per GPU):
-  forward        : for each layer, q,k,v,o,gate,up,down  Y = X.W^T + s.(X.A^T).B^T
+  forward        : for each layer, q,k,v,o,gate,up,down  Y = X.W^T + s.(X.A^T).B^T, as four
+                   calls: q/k/v fused and gate/up fused (they share their input and
+                   sit back to back in the layer image), o, down
   recompute+bwd  : for each layer in reverse, the recomputed forward of every
                    projection (StreamingBlockFunction.backward reruns the block,
                    ram_vram_finetune/training/recompute.py:85-105) and its
@@ -44,7 +46,6 @@ PROJ = [("q_proj", HIDDEN, HIDDEN, "attn"), ("k_proj", KV, HIDDEN, "attn"), ("v_
         ("down_proj", HIDDEN, INTER, "down")]
 INPUT_WIDTH = {"attn": HIDDEN, "o": HIDDEN, "mlp": HIDDEN, "down": INTER}
 RANK, ALPHA = 16, 32.0
-DOMINANT = "gate_proj"
 
 
 def parse():
@@ -160,24 +161,62 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- model
+# Projections that share their input run as one fused call over adjacent
+# records (q, k, v; gate, up): name, member projections, input buffer.
+GROUPS = [("qkv", ("q_proj", "k_proj", "v_proj"), "attn"), ("o", ("o_proj",), "o"),
+          ("gate_up", ("gate_proj", "up_proj"), "mlp"), ("down", ("down_proj",), "down")]
+SHAPE = {name: (N, K) for name, N, K, _src in PROJ}
+DOMINANT_GROUP = "gate_up"
+
+
+class GroupLoRA:
+    """The LoRA factors of one fused group as one branch: A = [A_1; A_2; ...]
+    ([n r, K]) and B = blockdiag(B_1, B_2, ...) ([sum N_i, n r]); every member
+    keeps its own rank-16 factors (views of the diagonal blocks).  The
+    off-diagonal blocks of B start at zero and their gradient is masked to zero
+    after every backward, so AdamW (element-wise) keeps them at zero: the same
+    update as separate per-projection factors."""
+
+    def __init__(self, members, g, device):
+        K = SHAPE[members[0]][1]
+        Ns = [SHAPE[m][0] for m in members]
+        n = len(members)
+        self.A = (torch.randn(n * RANK, K, generator=g, device=device) * 0.01).requires_grad_(True)
+        B = torch.zeros(sum(Ns), n * RANK, device=device)
+        self.mask = torch.zeros_like(B) if n > 1 else None
+        row = 0
+        for i, N in enumerate(Ns):
+            B[row:row + N, i * RANK:(i + 1) * RANK] = torch.randn(N, RANK, generator=g, device=device) * 0.01
+            if self.mask is not None:
+                self.mask[row:row + N, i * RANK:(i + 1) * RANK] = 1.0
+            row += N
+        self.B = B.requires_grad_(True)
+        self.A.grad = torch.zeros_like(self.A)
+        self.B.grad = torch.zeros_like(self.B)
+
+    def params(self):
+        return (self.A, self.B)
+
+
 def build_model(layers, codec_name, device, seed):
-    from spilltune_b200 import codec
+    """Per layer: the seven records packed into one device buffer laid out like
+    a slot image (so q/k/v and gate/up are adjacent), and one GroupLoRA per
+    group.  Returns (buffers, host-order records {name: PackedWeight view}, loras)."""
+    from spilltune_b200 import codec, streaming
     g = torch.Generator(device=device).manual_seed(seed)
-    weights, loras = [], []
+    bufs, weights, loras = [], [], []
     for _ in range(layers):
-        lw, ll = {}, {}
+        layer = {}
         for name, N, K, _src in PROJ:
             w = torch.randn(N, K, generator=g, device=device) * 0.02
-            lw[name] = codec.encode(w, codec_name)
+            layer[name] = codec.encode(w, codec_name)
             del w
-            A = (torch.randn(RANK, K, generator=g, device=device) * 0.01).requires_grad_(True)
-            B = (torch.randn(N, RANK, generator=g, device=device) * 0.01).requires_grad_(True)
-            A.grad = torch.zeros_like(A)
-            B.grad = torch.zeros_like(B)
-            ll[name] = (A, B)
-        weights.append(lw)
-        loras.append(ll)
-    return weights, loras
+        buf, views = streaming.pack_layer(layer, device)
+        del layer
+        bufs.append(buf)
+        weights.append(views)
+        loras.append({gname: GroupLoRA(members, g, device) for gname, members, _src in GROUPS})
+    return bufs, weights, loras
 
 
 def make_buffers(tokens, device, seed):
@@ -185,15 +224,18 @@ def make_buffers(tokens, device, seed):
     sets = []
     for _ in range(2):
         x = {k: torch.randn(tokens, w, generator=g, device=device).to(torch.bfloat16) for k, w in INPUT_WIDTH.items()}
-        dy = {name: torch.randn(tokens, N, generator=g, device=device).to(torch.bfloat16) for name, N, _K, _s in PROJ}
+        dy = {gname: torch.randn(tokens, sum(SHAPE[m][0] for m in members), generator=g,
+                                 device=device).to(torch.bfloat16) for gname, members, _s in GROUPS}
         sets.append((x, dy))
     return sets
 
 
 class Step:
-    """One training step of the frozen-linear stack (see module docstring)."""
+    """One training step of the frozen-linear stack (see module docstring):
+    per layer four calls (q/k/v fused, o, gate/up fused, down), forward, then
+    recompute + backward in reverse layer order, then AdamW."""
 
-    def __init__(self, weights_for, loras, bufs, world, optimizer, timed_name=DOMINANT):
+    def __init__(self, weights_for, loras, bufs, world, optimizer, timed_name=DOMINANT_GROUP):
         from spilltune_b200 import ops
         self.ops = ops
         self.weights_for = weights_for
@@ -207,15 +249,23 @@ class Step:
         self.events = []
         self.launches = 0
 
-    def _fwd(self, x, w, A, B, name, return_ts=False):
+    def _record(self, W, members):
+        if len(members) == 1:
+            return W[members[0]]
+        cat = self.ops.concat_records([W[m] for m in members])
+        if cat is None:
+            raise RuntimeError("fused group records are not adjacent in the layer image")
+        return cat
+
+    def _fwd(self, x, w, lora, name, return_ts=False):
         if self.record and name == self.timed_name:
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
-            out = self.ops.fwd(x, w, A, B, self.scale, return_ts=return_ts)
+            out = self.ops.fwd(x, w, lora.A, lora.B, self.scale, return_ts=return_ts)
             e.record()
             self.events.append((s, e))
         else:
-            out = self.ops.fwd(x, w, A, B, self.scale, return_ts=return_ts)
+            out = self.ops.fwd(x, w, lora.A, lora.B, self.scale, return_ts=return_ts)
         # Kernels of one fl_fwd call at these sizes: factor prepass, lora_down, GEMM.
         self.launches += 3
         return out
@@ -225,26 +275,28 @@ class Step:
         for l in range(L):
             x, _ = self.bufs[l % 2]
             with self.weights_for(l, "forward") as W:
-                for name, _N, _K, src in PROJ:
-                    A, B = self.loras[l][name]
-                    self._fwd(x[src], W[name], A, B, name)
+                for gname, members, src in GROUPS:
+                    self._fwd(x[src], self._record(W, members), self.loras[l][gname], gname)
         from spilltune_b200.dp import LoRAGradReducer
         reducer = LoRAGradReducer(average=True)
         for l in reversed(range(L)):
             x, dy = self.bufs[l % 2]
             with self.weights_for(l, "backward") as W:
-                for name, _N, _K, src in reversed(PROJ):
-                    A, B = self.loras[l][name]
+                for gname, members, src in reversed(GROUPS):
+                    lora = self.loras[l][gname]
+                    w = self._record(W, members)
                     # Recompute; the backward reuses its Ts = bf16(s * x . A^T)
                     # as the reference's autograd reuses F.linear(x, A).
-                    _y, ts = self._fwd(x[src], W[name], A, B, name, return_ts=True)
-                    self.ops.bwd(dy[name], x[src], W[name], A, B, self.scale, dA=A.grad, dB=B.grad,
-                                 accumulate=False, ts=ts)
+                    _y, ts = self._fwd(x[src], w, lora, gname, return_ts=True)
+                    self.ops.bwd(dy[gname], x[src], w, lora.A, lora.B, self.scale, dA=lora.A.grad,
+                                 dB=lora.B.grad, accumulate=False, ts=ts)
                     # prepass(B), lora_down(Us), backward GEMM, lora_grad x 2
                     self.launches += 5
+                    if lora.mask is not None:
+                        lora.B.grad.mul_(lora.mask)  # no gradient for the zero blocks
             # Data parallel: this layer's LoRA gradients are final; all-reduce
             # them on a side stream while the next layer recomputes.
-            reducer.reduce([t.grad for name, _N, _K, _s in PROJ for t in self.loras[l][name]])
+            reducer.reduce([t.grad for gname, _m, _s in GROUPS for t in self.loras[l][gname].params()])
         reducer.finish()
         self.opt.step()
 
@@ -576,9 +628,9 @@ def main():
     build.build()
     dev = torch.device("cuda", local)
     M, L = args.tokens, args.layers
-    weights, loras = build_model(L, args.codec, dev, seed=1234)  # same weights on every rank
-    bufs = make_buffers(M, dev, seed=100 + rank)                 # rank-local micro-batch
-    params = [t for ll in loras for name, *_ in PROJ for t in ll[name]]
+    layer_bufs, weights, loras = build_model(L, args.codec, dev, seed=1234)  # same weights on every rank
+    bufs = make_buffers(M, dev, seed=100 + rank)                             # rank-local micro-batch
+    params = [t for ll in loras for gname, *_ in GROUPS for t in ll[gname].params()]
     opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
 
     @contextlib.contextmanager
@@ -617,6 +669,7 @@ def main():
         host_layers = [{k: w.to("cpu").pin_memory() for k, w in lw.items()} for lw in weights]
         for lw in weights:
             lw.clear()
+        layer_bufs.clear()
         torch.cuda.empty_cache()
         # N > 1: each rank copies its 1/N of every layer from the host and the
         # slot is all-gathered over NVLink on a communicator of its own.
@@ -666,8 +719,10 @@ def main():
     # ------------------------------------------------------------ report
     if rank == 0:
         peak, hbm, peak_kind = measured_peaks()
-        Ndom = dict((n, N) for n, N, _K, _s in PROJ)[DOMINANT]
-        fl = algorithmic_fwd_flops(M, Ndom, HIDDEN, RANK)
+        # Algorithmic work of the dominant call (gate and up, rank 16 each; the
+        # zero blocks of the combined LoRA factor are not counted).
+        fl = sum(algorithmic_fwd_flops(M, SHAPE[m][0], SHAPE[m][1], RANK)
+                 for m in dict((g[0], g[1]) for g in GROUPS)[DOMINANT_GROUP])
         achieved = fl / (kern_ms / 1e3) / 1e12
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -681,7 +736,8 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": bench_config(args, world),
             "step_tflops": total_flops / (ms / 1e3) / 1e12,
-            "roofline": {"bound": "tensor", "kernel": "fl_fwd (fused dequant-GEMM + LoRA) gate_proj 8192x14336x4096",
+            "roofline": {"bound": "tensor",
+                         "kernel": "fl_fwd (fused dequant-GEMM + LoRA) gate+up 8192x28672x4096, rank 16 each",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_kind": f"{peak_kind} bf16 sustained", "traffic": load_profile_traffic(),
                          "launch_ms": kern_ms},

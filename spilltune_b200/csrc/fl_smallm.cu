@@ -125,6 +125,12 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c4 = lane & 3;
+  // MMA row g of a 16-row tile holds weight row pg (and g + 8 row pg + 8): the
+  // two rows of an 8-lane shared-memory phase (g = 2i, 2i + 1) are then four
+  // rows apart, so their code chunks fall in opposite halves of the 128-byte
+  // swizzle and the 16-byte loads are conflict-free.  The scales and the
+  // partial sums use the same map.
+  const int pg = (g >> 1) | ((g & 1) << 2);
   const int grp = warp & (kGroups - 1);  // scale group of every chunk
   const int half = warp / kGroups;       // tiles [half * TW, half * TW + TW) of the CTA
   const int split = args.split;
@@ -235,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
       for (int t = 0; t < TW; ++t)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int r = 16 * (half * TW + t) + g + 8 * h;
+          const int r = 16 * (half * TW + t) + pg + 8 * h;
           q[t][h] = *reinterpret_cast<const uint4*>(cbox + r * 128 + ((j ^ (r & 7)) << 4));
         }
       float part[PS][TW][NT][4];
@@ -271,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
       }
 #pragma unroll
       for (int t = 0; t < TW; ++t) {
-        const int r0 = 16 * (half * TW + t) + g, r1 = r0 + 8;
+        const int r0 = 16 * (half * TW + t) + pg, r1 = r0 + 8;
         const float s0 = scl[r0 * 4 + grp], s1 = scl[r1 * 4 + grp];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -294,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
   // Warp partials -> red[group][row][token] in the ring's space, once every
   // copy into the ring has landed (the consumers waited for each chunk; the
   // producer drained what an abort left in flight): accumulator element i of
-  // tile t: row 16 (half TW + t) + g + 8*(i >> 1), token 8*nt + 2*c4 + (i & 1).
+  // tile t: row 16 (half TW + t) + pg + 8*(i >> 1), token 8*nt + 2*c4 + (i & 1).
   __syncthreads();
   if (warp < kWarps)
 #pragma unroll
@@ -303,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        red[(grp * rows + 16 * (half * TW + t) + g + 8 * (i >> 1)) * 16 + 8 * nt + 2 * c4 + (i & 1)] = acc[t][nt][i];
+        red[(grp * rows + 16 * (half * TW + t) + pg + 8 * (i >> 1)) * 16 + 8 * nt + 2 * c4 + (i & 1)] = acc[t][nt][i];
   }
   __syncthreads();
   // Sum the four groups into red[0] (tokens past 8*NT stay unused).

@@ -62,17 +62,22 @@ def rms(hidden, weight, eps):
 
 
 def block_forward(hidden_states, position_embeddings, attention_mask, linear, weights, *, heads, kv_heads,
-                  head_dim, eps, qk_norm=False, feed_forward=None):
+                  head_dim, eps, qk_norm=False, feed_forward=None, fused=None):
     """The dense block's math (adapters/dense.py:120-153) with the projections
     supplied by ``linear(x, path)``: RMSNorm, GQA attention with full RoPE and
     an additive mask (softmax in FP32), residuals, SwiGLU MLP.  The op order
-    follows the reference so BF16 roundings match."""
+    follows the reference so BF16 roundings match.  ``fused(x, paths)``, when
+    given, computes projections that share their input (q, k, v; gate, up)
+    together and returns their outputs in order."""
+    if fused is None:
+        fused = lambda x, paths: [linear(x, p) for p in paths]  # noqa: E731
     residual = hidden_states
     x = rms(hidden_states, weights["input_layernorm.weight"], eps)
     shape = (*x.shape[:-1], -1, head_dim)
-    q = linear(x, "self_attn.q_proj").view(shape)
-    k = linear(x, "self_attn.k_proj").view(shape)
-    v = linear(x, "self_attn.v_proj").view(shape).transpose(1, 2)
+    q, k, v = fused(x, ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"))
+    q = q.view(shape)
+    k = k.view(shape)
+    v = v.view(shape).transpose(1, 2)
     if qk_norm:
         q = rms(q, weights["self_attn.q_norm.weight"], eps)
         k = rms(k, weights["self_attn.k_norm.weight"], eps)
@@ -98,7 +103,8 @@ def block_forward(hidden_states, position_embeddings, attention_mask, linear, we
     x = rms(x, weights["post_attention_layernorm.weight"], eps)
     if feed_forward is not None:
         return residual + feed_forward(x, weights)
-    return residual + linear(F.silu(linear(x, "mlp.gate_proj")) * linear(x, "mlp.up_proj"), "mlp.down_proj")
+    gate, up = fused(x, ("mlp.gate_proj", "mlp.up_proj"))
+    return residual + linear(F.silu(gate) * up, "mlp.down_proj")
 
 
 def packed_dense_block(hidden_states, position_embeddings, attention_mask, *, heads, kv_heads, head_dim, eps,
@@ -118,18 +124,36 @@ def packed_dense_block(hidden_states, position_embeddings, attention_mask, *, he
                 "self_attn.o_proj": lora_o, "mlp.gate_proj": lora_gate, "mlp.up_proj": lora_up,
                 "mlp.down_proj": lora_down}
 
-    def linear(x, path):
-        name = path + ".weight"
+    def record(x, path):
         if weights.get(path + ".bias") is not None:
             raise ValueError("unsupported_capability: fused frozen linear has no bias term")
-        pw = packed_weight(weights, name, x.shape[-1], codec_name)
+        return packed_weight(weights, path + ".weight", x.shape[-1], codec_name)
+
+    def linear(x, path):
+        pw = record(x, path)
         proj = adapters.get(path)
         if proj is not None:
             return ops.lora_projection_forward(proj, x, pw)
         return ops.frozen_lora_linear(x, pw)
 
+    def fused(x, paths):
+        """Projections of one input as one call when the slot holds them back
+        to back and their LoRA branches share one scale (q, k, v; gate, up);
+        each adapted projection is checked like LoRAProjection.forward."""
+        pws = [record(x, p) for p in paths]
+        projs = [adapters.get(p) for p in paths]
+        for p, pw in zip(projs, pws):
+            if p is not None:
+                ops.check_projection(p, x, pw)
+        scales = {p.scale for p in projs if p is not None}
+        if len(scales) <= 1:
+            factors = [(p.A, p.B) if p is not None else None for p in projs]
+            return ops.fused_lora_linears(x, pws, factors, scales.pop() if scales else 0.0)
+        return [linear(x, p) for p in paths]
+
     return block_forward(hidden_states, position_embeddings, attention_mask, linear, weights, heads=heads,
-                         kv_heads=kv_heads, head_dim=head_dim, eps=eps, qk_norm=qk_norm, feed_forward=feed_forward)
+                         kv_heads=kv_heads, head_dim=head_dim, eps=eps, qk_norm=qk_norm, feed_forward=feed_forward,
+                         fused=fused)
 
 
 class PackedBlockReloader:

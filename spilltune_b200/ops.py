@@ -188,13 +188,77 @@ def frozen_lora_linear(x, weight: PackedWeight, A=None, B=None, scale=0.0):
     return library.frozen_linear(x, weight.payload, weight.scales, weight.lut, N, K, 0, A, B, scale)
 
 
-def lora_projection_forward(proj, x, weight: PackedWeight, base_bias=None):
-    """``LoRAProjection.forward(x, base_weight, base_bias)`` with a packed base weight.
+def concat_records(weights):
+    """One stacked record over matrices that share their input and sit back to
+    back in memory (a slot image or ``streaming.pack_layer`` places a layer's
+    payloads contiguously, then its scales): the view [sum N_i, K] whose rows
+    are the matrices' rows in order, or None when the parts are not adjacent,
+    the input widths or codebooks differ, or a record is not a plain [N, K]
+    matrix.  No copy."""
+    if len(weights) < 2:
+        return None
+    first = weights[0]
+    K = first.shape[-1]
+    for w in weights:
+        if len(w.shape) != 2 or w.shape[1] != K or w.codec != first.codec or w.lut.data_ptr() == 0:
+            return None
+    for a, b in zip(weights, weights[1:]):
+        if a.payload.untyped_storage().data_ptr() != b.payload.untyped_storage().data_ptr():
+            return None
+        if a.payload.data_ptr() + a.payload.numel() != b.payload.data_ptr():
+            return None
+        if a.scales.data_ptr() + 4 * a.scales.numel() != b.scales.data_ptr():
+            return None
+        if not torch.equal(a.lut, b.lut):
+            return None
+    N = sum(w.shape[0] for w in weights)
+    payload = first.payload.as_strided((N * K // 2,), (1,))
+    scales = first.scales.as_strided((N * K // 128,), (1,))
+    return PackedWeight(payload, scales, first.lut, (N, K), first.codec)
 
-    Same argument meaning and error behaviour as finetune/lora.py:205-220
-    (shape checks raise ValueError); bias-carrying projections are rejected
-    because the fused kernels have no bias term.
-    """
+
+def concat_lora(factors, out_features):
+    """The LoRA factors of several projections over one input as one branch:
+    A = [A_1; A_2; ...] ([sum r_i, K]) and B = blockdiag(B_1, B_2, ...)
+    ([sum N_i, sum r_i]; a projection without LoRA contributes rows of zeros).
+    Built with differentiable torch ops, so gradients reach every A_i and B_i
+    and the zero blocks receive none.  `factors` is [(A_i, B_i) or None] in
+    record order, `out_features` the N_i.  Returns (A, B) or (None, None)."""
+    As, Bs = [], []
+    for f, n in zip(factors, out_features):
+        if f is None:
+            continue
+        As.append(f[0])
+    if not As:
+        return None, None
+    for f, n in zip(factors, out_features):
+        if f is None:
+            Bs.append(As[0].new_zeros((n, 0)))
+        else:
+            Bs.append(f[1])
+    return torch.cat(As, 0), torch.block_diag(*Bs)
+
+
+def fused_lora_linears(x, weights, factors=None, scale=0.0):
+    """Projections of one input x as one fused call when their records are
+    adjacent (``concat_records``) and their LoRA branches share `scale`:
+    returns the list of outputs, each x . W_i^T + scale * (x . A_i^T) . B_i^T,
+    autograd-capable in x and every A_i, B_i.  Otherwise one call each.  The
+    combined rank (sum of r_i) must be <= 64."""
+    factors = factors or [None] * len(weights)
+    outs = [w.shape[0] for w in weights]
+    cat = concat_records(weights)
+    ranks = sum(f[0].shape[0] for f in factors if f is not None)
+    if cat is None or ranks > FL_MAX_RANK:
+        return [frozen_lora_linear(x, w, *(f if f is not None else (None, None)), scale)
+                for w, f in zip(weights, factors)]
+    A, B = concat_lora(factors, outs)
+    y = frozen_lora_linear(x, cat, A, B, scale)
+    return list(y.split(outs, dim=-1))
+
+
+def check_projection(proj, x, weight: PackedWeight):
+    """The shape checks of LoRAProjection.forward (finetune/lora.py:207-216), same messages."""
     if tuple(weight.shape) != tuple(proj.base_weight_shape):
         raise ValueError(
             f"{proj.target_path} base weight shape mismatch: expected "
@@ -202,6 +266,16 @@ def lora_projection_forward(proj, x, weight: PackedWeight, base_bias=None):
     if x.shape[-1] != proj.in_features:
         raise ValueError(
             f"{proj.target_path} input width mismatch: expected {proj.in_features}, got {x.shape[-1]}")
+
+
+def lora_projection_forward(proj, x, weight: PackedWeight, base_bias=None):
+    """``LoRAProjection.forward(x, base_weight, base_bias)`` with a packed base weight.
+
+    Same argument meaning and error behaviour as finetune/lora.py:205-220
+    (shape checks raise ValueError); bias-carrying projections are rejected
+    because the fused kernels have no bias term.
+    """
+    check_projection(proj, x, weight)
     if base_bias is not None:
         raise ValueError("unsupported_capability: fused frozen linear has no bias term")
     return frozen_lora_linear(x, weight, proj.A, proj.B, proj.scale)

@@ -32,34 +32,61 @@ import torch
 
 from .codec import PackedWeight, validate
 
-_ALIGN = 256
+_ALIGN = 256   # slot buffers and shard boundaries
+_PART = 16     # parts inside a layer image (the kernels' operand alignment)
 
 
-def _align(n):
-    return (n + _ALIGN - 1) // _ALIGN * _ALIGN
+def _align(n, a=_ALIGN):
+    return (n + a - 1) // a * a
+
+
+def _layout(layer):
+    """Slot-image layout of one layer (dict name -> PackedWeight), in order:
+    every matrix's payload, then every matrix's scales, then every codebook,
+    each part 16-byte aligned.  Group-128 records with K % 128 == 0 have
+    payloads of N * K / 2 and scales of N * K / 32 bytes (multiples of 16), so
+    matrices that follow each other in the layer (q, k, v; gate, up) sit back to
+    back: their concatenation is itself a valid stacked record [N1 + N2 + ..., K]
+    that one fused call can read (``ops.concat_records``).
+    Returns [(name, part, offset, tensor)] and the image size (256-aligned)."""
+    out, off = [], 0
+    for part in ("payload", "scales", "lut"):
+        for name, w in layer.items():
+            t = getattr(w, part)
+            off = _align(off, _PART)
+            out.append((name, part, off, t))
+            off += t.numel() * t.element_size()
+    return out, _align(off)
 
 
 def layer_bytes(layer):
-    """Slot bytes for one layer (dict name -> PackedWeight), 256-byte aligned parts."""
-    total = 0
-    for w in layer.values():
-        total = _align(total) + w.payload.numel()
-        total = _align(total) + 4 * w.scales.numel()
-        total = _align(total) + 64
-    return _align(total)
+    """Slot bytes for one layer (dict name -> PackedWeight)."""
+    return _layout(layer)[1]
 
 
 def _parts(layer):
     """(slot offset, byte view) of every part of a layer, in slot-image order."""
-    out = []
-    off = 0
-    for w in layer.values():
-        for t in (w.payload, w.scales, w.lut):
-            off = _align(off)
-            b = t.reshape(-1).view(torch.uint8)
-            out.append((off, b))
-            off += b.numel()
-    return out
+    return [(off, t.reshape(-1).view(torch.uint8)) for _name, _part, off, t in _layout(layer)[0]]
+
+
+def layer_views(buf, layer):
+    """{name: PackedWeight} views of a layer image in `buf` (uint8, any device)."""
+    parts = {}
+    for name, part, off, t in _layout(layer)[0]:
+        n = t.numel() * t.element_size()
+        parts.setdefault(name, {})[part] = buf.narrow(0, off, n).view(t.dtype)
+    return {name: PackedWeight(parts[name]["payload"], parts[name]["scales"], parts[name]["lut"], w.shape, w.codec)
+            for name, w in layer.items()}
+
+
+def pack_layer(layer, device):
+    """One layer copied into a single device buffer laid out like a slot image;
+    returns (buffer, {name: PackedWeight views}).  Resident layers packed this
+    way can run fused calls over adjacent matrices, like streamed slots."""
+    buf = torch.empty(layer_bytes(layer), dtype=torch.uint8, device=device)
+    for off, b in _parts(layer):
+        buf.narrow(0, off, b.numel()).copy_(b, non_blocking=True)
+    return buf, layer_views(buf, layer)
 
 
 def shard_image(layer, start, size, out=None):
@@ -129,19 +156,7 @@ class PackedSlotSession:
 
     # -------------------------------------------------------------- internals
     def _views(self, slot, idx):
-        buf = slot["buffer"]
-        out = {}
-        off = 0
-        for name, w in self.layers[idx].items():
-            off = _align(off)
-            payload = buf.narrow(0, off, w.payload.numel())
-            off = _align(off + w.payload.numel())
-            scales = buf.narrow(0, off, 4 * w.scales.numel()).view(torch.float32)
-            off = _align(off + 4 * w.scales.numel())
-            lut = buf.narrow(0, off, 64).view(torch.float32)
-            off += 64
-            out[name] = PackedWeight(payload, scales, lut, w.shape, w.codec)
-        return out
+        return layer_views(slot["buffer"], self.layers[idx])
 
     def _find(self, idx):
         return next((s for s in self.slots if s["layer"] == idx), None)
@@ -174,12 +189,10 @@ class PackedSlotSession:
                 # In place: every rank's chunk of the slot -> the whole slot on every rank.
                 dist.all_gather_into_tensor(buf, mine, group=self.group, async_op=True).wait()
             else:
-                for name, w in src.items():
-                    v = views[name]
-                    v.payload.copy_(w.payload, non_blocking=True)
-                    v.scales.copy_(w.scales, non_blocking=True)
-                    v.lut.copy_(w.lut, non_blocking=True)
-                    nbytes += w.payload.numel() + 4 * w.scales.numel() + 64
+                buf = slot["buffer"]
+                for off, b in _parts(src):
+                    buf.narrow(0, off, b.numel()).copy_(b, non_blocking=True)
+                    nbytes += b.numel()
             end.record(self.copy_stream)
         slot.update(layer=idx, ready=end, views=views)
         self.copy_events.append((start, end, nbytes))

@@ -82,8 +82,9 @@ int fl_dequant(const uint8_t* payload, const float* scales, const float* lut16, 
 
 /* Scratch bytes fl_fwd needs: the scaled low-rank activations
  * Ts = bf16(s * X.A^T) (M x 64 bf16) and A converted to a bf16 hi/lo pair
- * (4 * rank' * K bytes, rank' = rank rounded up to 16, 32 or 64); 0 when
- * rank == 0. */
+ * (4 * rank' * K bytes, rank' = rank rounded up to 16, 32 or 64) with one
+ * 32-bit mask of its nonzero 8-column groups per 64 columns (4 * K / 64 bytes,
+ * padded to 16); 0 when rank == 0. */
 size_t fl_fwd_workspace_bytes(int64_t M, int64_t K, int rank);
 
 /*
@@ -108,7 +109,10 @@ int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, cons
            void* workspace, size_t workspace_bytes, void* stream);
 
 /* Scratch bytes fl_bwd needs: Us = bf16(s * dY.B) and Ts (M x 64 bf16 each)
- * and the converted factors (4 * rank' * (N + K) bytes); 0 when rank == 0. */
+ * and the converted factors with their masks (as for fl_fwd, over N and over
+ * K); 0 when rank == 0.  A factor whose 8-column groups are zero over whole
+ * 64-row units (the block-diagonal B of projections stacked over one input)
+ * costs correspondingly less low-rank work. */
 size_t fl_bwd_workspace_bytes(int64_t M, int64_t N, int64_t K, int rank);
 
 /*

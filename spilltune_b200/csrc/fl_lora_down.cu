@@ -64,10 +64,15 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Prepass: qc[e][plane][u][j][c][16] (bf16) from Q(j, r) = q[e*q_es + j*q_sj + r*q_sr].
-// One thread per (e, j, 8 consecutive r).
+// Prepass: qc[e][plane][u][j][c][16] (bf16) from Q(j, r) = q[e*q_es + j*q_sj + r*q_sr],
+// one thread per (e, j, 8 consecutive r); then, after expert e's two planes,
+// one 32-bit mask per 64-wide unit u: bit n set when some Q(j, r) with
+// 8n <= j < 8n + 8, r in the unit, is nonzero (one warp per unit).  A
+// block-diagonal factor (the LoRA branches of several projections over one
+// input, stacked) leaves most 8-column groups of a unit zero; lora_down skips
+// their MMAs.  qc_es: elements from one expert's block to the next.
 __global__ void prep_kernel(const float* __restrict__ q, int64_t q_sj, int64_t q_sr, int64_t q_es, int rank, int R,
-                            int nq, int experts, __nv_bfloat16* __restrict__ qc) {
+                            int nq, int experts, __nv_bfloat16* __restrict__ qc, int64_t qc_es) {
   // lora_down follows at once (programmatic dependent launch) and starts
   // streaming its activations; it waits for this grid before reading qc.
   griddep_launch_dependents();
@@ -105,9 +110,28 @@ __global__ void prep_kernel(const float* __restrict__ q, int64_t q_sj, int64_t q
     }
     const int u = r0 >> 6, c = (r0 & 63) >> 4, w = r0 & 15;
     const int64_t off = ((static_cast<int64_t>(u) * nq + j) * 4 + c) * 16 + w;
-    __nv_bfloat16* base = qc + static_cast<int64_t>(e) * 2 * plane;
+    __nv_bfloat16* base = qc + static_cast<int64_t>(e) * qc_es;
     *reinterpret_cast<uint4*>(base + off) = make_uint4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<uint4*>(base + plane + off) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+  // Unit masks: warp `wid` takes unit u of expert e; lane l looks at r = 64u + l
+  // and 64u + 32 + l for every j < rank.
+  const int units = R / 64;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t wid = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+       wid < static_cast<int64_t>(experts) * units; wid += warps) {
+    const int u = static_cast<int>(wid % units);
+    const int e = static_cast<int>(wid / units);
+    const float* src = q + e * q_es + static_cast<int64_t>(64 * u + lane) * q_sr;
+    uint32_t mask = 0;
+    for (int n = 0; n < nq / 8; ++n) {
+      bool any = false;
+      for (int j = 8 * n; j < 8 * n + 8 && j < rank; ++j)
+        any |= (__ldg(src + j * q_sj) != 0.f) | (__ldg(src + j * q_sj + 32 * q_sr) != 0.f);
+      if (__any_sync(0xffffffffu, any)) mask |= 1u << n;
+    }
+    if (lane == 0) reinterpret_cast<uint32_t*>(qc + static_cast<int64_t>(e) * qc_es + 2 * plane)[u] = mask;
   }
   // Launched as a dependent itself (the second factor of a backward): finish
   // no earlier than the launch before, so completion stays ordered.
@@ -153,6 +177,8 @@ __global__ void __launch_bounds__(kThreads)
   }
   const int64_t plane = static_cast<int64_t>(NQ) * R;
   const int units = R / 64;
+  // Per 64-wide unit: which 8-column groups of the factor are nonzero (the prepass).
+  const uint32_t* umask = reinterpret_cast<const uint32_t*>(qc + 2 * plane);
   const int u0 = kslice * units / split;
   const int u1 = (kslice + 1) * units / split;
   const int n_units = u1 - u0;
@@ -209,8 +235,12 @@ __global__ void __launch_bounds__(kThreads)
     }
   } else {
     // ------------------------------------------------------------ consumers
+    // The unit masks are the prepass grid's output, like qc: wait for that grid
+    // (the producer does the same before loading qc).
+    griddep_wait();
     for (int k = 0; k < n_units; ++k) {
       const int st = k % kStages;
+      const uint32_t um = umask[u0 + k];
       if (!mbar_wait_short_warp(&full[st], (k / kStages) & 1, abort_word, status, kStatusTimeoutFull)) break;
       const uint8_t* stage = smem + st * C::kStage;
       // Thread (g, c) needs chunk 2c + e of rows 32w + 16t + 8h + g; under the
@@ -229,6 +259,7 @@ __global__ void __launch_bounds__(kThreads)
       const uint8_t* qb = stage + kXBytes + ((g * 4 + c) * 16) * 2;
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
+        if (((um >> n) & 1u) == 0) continue;  // this unit's 8 factor columns are all zero
         const uint4* hp = reinterpret_cast<const uint4*>(qb + n * 8 * 64 * 2);
         const uint4* lp = reinterpret_cast<const uint4*>(qb + C::kQPlane + n * 8 * 64 * 2);
         const uint4 h0 = hp[0], h1 = hp[1];
@@ -600,7 +631,11 @@ int launch_lora_parts(const void* P, int M, int R, const float* q, int64_t q_sj,
 
 int lora_nq(int rank) { return rank <= 16 ? 16 : rank <= 32 ? 32 : 64; }
 
-size_t lora_factor_bytes(int64_t R, int rank) { return 4u * static_cast<size_t>(lora_nq(rank)) * R; }
+// Per expert: the hi and lo planes (2 x nq x R bf16) and the unit masks (R / 64
+// uint32, padded to 16 bytes).
+size_t lora_factor_bytes(int64_t R, int rank) {
+  return 4u * static_cast<size_t>(lora_nq(rank)) * R + static_cast<size_t>((R / 64 * 4 + 15) / 16 * 16);
+}
 
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank, float s,
                      void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles, const int* tile_count,
@@ -620,7 +655,10 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
   {
     const int64_t total = static_cast<int64_t>(experts) * nq * (R / 8);
     const int threads = 256;
-    const int64_t want = (total + threads - 1) / threads;
+    // Enough threads for the conversion and one warp per unit for the masks.
+    const int64_t items = total > static_cast<int64_t>(experts) * (R / 64) * 32 ? total
+                                                                                : static_cast<int64_t>(experts) * (R / 64) * 32;
+    const int64_t want = (items + threads - 1) / threads;
     const int grid = static_cast<int>(want < 4096 ? want : 4096);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -631,10 +669,12 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, ld::prep_kernel, q, q_sj, q_sr, q_expert_stride, rank, R, nq, experts, qc);
+    const int64_t qc_es = static_cast<int64_t>(lora_factor_bytes(R, rank) / 2);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, ld::prep_kernel, q, q_sj, q_sr, q_expert_stride, rank, R, nq, experts, qc,
+                                       qc_es);
     if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down prepass: %s", cudaGetErrorString(e));
   }
-  const int64_t qc_es = 2 * static_cast<int64_t>(nq) * R;
+  const int64_t qc_es = static_cast<int64_t>(lora_factor_bytes(R, rank) / 2);
   if (nq == 16) return ld::launch_nq<16>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
   if (nq == 32) return ld::launch_nq<32>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
   return ld::launch_nq<64>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);

@@ -199,8 +199,11 @@ def concat_records(weights):
         return None
     first = weights[0]
     K = first.shape[-1]
+    # Host-side checks only (pointers, shapes, codec names): nothing here may
+    # touch the device, which would synchronise the stream on every call.  The
+    # codebook follows from the codec name.
     for w in weights:
-        if len(w.shape) != 2 or w.shape[1] != K or w.codec != first.codec or w.lut.data_ptr() == 0:
+        if len(w.shape) != 2 or w.shape[1] != K or w.codec != first.codec:
             return None
     for a, b in zip(weights, weights[1:]):
         if a.payload.untyped_storage().data_ptr() != b.payload.untyped_storage().data_ptr():
@@ -208,8 +211,6 @@ def concat_records(weights):
         if a.payload.data_ptr() + a.payload.numel() != b.payload.data_ptr():
             return None
         if a.scales.data_ptr() + 4 * a.scales.numel() != b.scales.data_ptr():
-            return None
-        if not torch.equal(a.lut, b.lut):
             return None
     N = sum(w.shape[0] for w in weights)
     payload = first.payload.as_strided((N * K // 2,), (1,))

@@ -44,11 +44,13 @@ def test_python_binding_covers_header():
 
 def test_version_and_workspace_sizes(lib):
     assert lib.fl_version() >= 200  # 0.2.0 adds fl_bwd_ts and fl_bwd_nf4dq_ts
-    # Ts (M x 64 bf16) + the factor converted to a bf16 hi/lo pair (4 * rank' * K).
-    assert lib.fl_fwd_workspace_bytes(8192, 4096, 16) == 8192 * 128 + 4 * 16 * 4096
-    assert lib.fl_fwd_workspace_bytes(8192, 4096, 20) == 8192 * 128 + 4 * 32 * 4096
+    # Ts (M x 64 bf16) + the factor converted to a bf16 hi/lo pair (4 * rank' * K) and its
+    # per-64-unit masks (4 * K / 64 bytes, padded to 16).
+    mask = lambda R: (R // 64 * 4 + 15) // 16 * 16
+    assert lib.fl_fwd_workspace_bytes(8192, 4096, 16) == 8192 * 128 + 4 * 16 * 4096 + mask(4096)
+    assert lib.fl_fwd_workspace_bytes(8192, 4096, 20) == 8192 * 128 + 4 * 32 * 4096 + mask(4096)
     assert lib.fl_fwd_workspace_bytes(8192, 4096, 0) == 0
-    assert lib.fl_bwd_workspace_bytes(100, 384, 256, 8) == 100 * 256 + 4 * 16 * (384 + 256)
+    assert lib.fl_bwd_workspace_bytes(100, 384, 256, 8) == 100 * 256 + 4 * 16 * (384 + 256) + mask(384) + mask(256)
 
 
 def _fwd(lib, M=16, K=256, N=128, rank=0, ptr=1024, ws=0):

@@ -54,6 +54,8 @@ def parse():
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["llama3-8b", "qwen3-30b-a3b"], default="llama3-8b",
+                   help="llama3-8b: the headline step (BASELINE config 3); qwen3-30b-a3b: config 4's MoE stack")
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--tokens", type=int, default=8192, help="tokens per GPU per step (micro-batch 4 x seq 2048)")
     p.add_argument("--codec", default="nf4-g128")
@@ -608,9 +610,135 @@ def probe_op(a):
                       "tflops": flops / us / 1e6 if flops else None}))
 
 
+# ---------------------------------------------------------------- Qwen3-30B-A3B
+MOE = {"layers": 48, "hidden": 2048, "q": 4096, "kv": 512, "experts": 128, "top_k": 8, "inter": 768, "rank": 8,
+       "alpha": 16.0, "tokens": 8192}
+
+
+def run_moe(args, world, rank, local):
+    """The frozen-linear stack of a Qwen3-30B-A3B-shaped model (BASELINE
+    config 4: 48 layers, hidden 2048, 32 x 128 query heads, 4 KV heads, 128
+    experts top-8 with expert intermediate 768; NF4 group-128 records; LoRA
+    rank 8 on the attention projections and per expert on gate_up / down;
+    seq 4096 x micro-batch 2 = 8192 tokens per GPU).  Per layer: q/k/v fused
+    (N = 4096 + 512 + 512), o, and the two grouped expert projections over
+    the 65536 routed rows (fl_grouped_fwd / fl_grouped_bwd: expert
+    gate_up [128, 1536, 2048], down [128, 2048, 768]); routing from random
+    router weights (near-uniform load), sorted by expert on the device as
+    moe.expert_segments does.  Step = forward, recomputed forward and backward
+    of every call, then AdamW.  Inputs and upstream gradients are synthetic
+    per-call buffers in two alternating sets (the router, gather, SiLU and
+    combine are outside the frozen-linear stack, as attention is for the
+    dense workload).  Weights resident in HBM (15.9 GB packed)."""
+    from spilltune_b200 import build, codec, moe, ops, streaming
+    build.build()
+    dev = torch.device("cuda", local)
+    c = MOE
+    T, H, E, k, I, r = args.tokens, c["hidden"], c["experts"], c["top_k"], c["inter"], c["rank"]
+    L = args.layers if args.layers != 32 else c["layers"]
+    scale = c["alpha"] / r
+    rows = T * k
+    g = torch.Generator(device=dev).manual_seed(1234)
+
+    def lora(n_experts, N, K, rk):
+        shape_a = (n_experts, rk, K) if n_experts else (rk, K)
+        shape_b = (n_experts, N, rk) if n_experts else (N, rk)
+        A = (torch.randn(*shape_a, generator=g, device=dev) * 0.01).requires_grad_(True)
+        B = (torch.randn(*shape_b, generator=g, device=dev) * 0.01).requires_grad_(True)
+        A.grad, B.grad = torch.zeros_like(A), torch.zeros_like(B)
+        return A, B
+
+    layers = []
+    for _ in range(L):
+        attn = {n: codec.encode(torch.randn(N, K, generator=g, device=dev) * 0.02, args.codec)
+                for n, N, K in (("q", c["q"], H), ("k", c["kv"], H), ("v", c["kv"], H), ("o", H, c["q"]))}
+        buf, views = streaming.pack_layer(attn, dev)
+        del attn
+        qkv = ops.concat_records([views["q"], views["k"], views["v"]])
+        gate_up = codec.encode(torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02, args.codec)
+        down = codec.encode(torch.randn(E, H, I, generator=g, device=dev) * 0.02, args.codec)
+        router = torch.randn(E, H, generator=g, device=dev) * 0.02
+        logits = torch.randn(T, H, generator=g, device=dev) @ router.t()
+        segs = moe.expert_segments(torch.topk(logits.softmax(-1), k, dim=-1)[1], E)
+        A_qkv = (torch.randn(3 * r, H, generator=g, device=dev) * 0.01).requires_grad_(True)
+        B_qkv = torch.zeros(c["q"] + 2 * c["kv"], 3 * r, device=dev)
+        mask = torch.zeros_like(B_qkv)
+        row = 0
+        for i, N in enumerate((c["q"], c["kv"], c["kv"])):
+            B_qkv[row:row + N, i * r:(i + 1) * r] = torch.randn(N, r, generator=g, device=dev) * 0.01
+            mask[row:row + N, i * r:(i + 1) * r] = 1.0
+            row += N
+        B_qkv.requires_grad_(True)
+        A_qkv.grad, B_qkv.grad = torch.zeros_like(A_qkv), torch.zeros_like(B_qkv)
+        layers.append({"buf": buf, "qkv": qkv, "o": views["o"], "gate_up": gate_up, "down": down, "segs": segs,
+                       "lora": {"qkv": (A_qkv, B_qkv), "o": lora(0, H, c["q"], r),
+                                "gate_up": lora(E, 2 * I, H, r), "down": lora(E, H, I, r)},
+                       "mask": mask})
+    gi = torch.Generator(device=dev).manual_seed(100 + rank)
+    rnd = lambda *shape: torch.randn(*shape, generator=gi, device=dev).to(torch.bfloat16)  # noqa: E731
+    bufs = [{"attn": rnd(T, H), "o": rnd(T, c["q"]), "xs": rnd(rows, H), "act": rnd(rows, I),
+             "d_qkv": rnd(T, c["q"] + 2 * c["kv"]), "d_o": rnd(T, H), "d_gu": rnd(rows, 2 * I), "d_dn": rnd(rows, H)}
+            for _ in range(2)]
+    params = [t for lay in layers for AB in lay["lora"].values() for t in AB]
+    opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
+    counts = {"launches": 0}
+
+    def step():
+        for li, lay in enumerate(layers):
+            b = bufs[li % 2]
+            ops.fwd(b["attn"], lay["qkv"], *lay["lora"]["qkv"], scale)
+            ops.fwd(b["o"], lay["o"], *lay["lora"]["o"], scale)
+            moe.grouped_fwd(b["xs"], lay["segs"], lay["gate_up"], *lay["lora"]["gate_up"], scale)
+            moe.grouped_fwd(b["act"], lay["segs"], lay["down"], *lay["lora"]["down"], scale)
+        for li in reversed(range(len(layers))):
+            lay, b = layers[li], bufs[li % 2]
+            for name, x, d in (("down", b["act"], b["d_dn"]), ("gate_up", b["xs"], b["d_gu"])):
+                A, B = lay["lora"][name]
+                moe.grouped_fwd(x, lay["segs"], lay[name], A, B, scale)  # recompute
+                moe.grouped_bwd(d, x, lay["segs"], lay[name], A, B, scale, dA=A.grad, dB=B.grad)
+            for name, x, d in (("o", b["o"], b["d_o"]), ("qkv", b["attn"], b["d_qkv"])):
+                A, B = lay["lora"][name]
+                _y, ts = ops.fwd(x, lay[name], A, B, scale, return_ts=True)  # recompute
+                ops.bwd(d, x, lay[name], A, B, scale, dA=A.grad, dB=B.grad, ts=ts)
+            lay["lora"]["qkv"][1].grad.mul_(lay["mask"])
+        opt.step()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    # Algorithmic work per token per layer: forward 2 x (attention weights + top_k expert weights),
+    # backward (dX) the same, the recompute once more; LoRA terms are small and not counted here.
+    w_tok = c["q"] * H + 2 * c["kv"] * H + H * c["q"] + k * (2 * I * H + H * I)
+    step_flops = 3 * 2.0 * w_tok * T * L
+    line = {"metric": "train tokens/s (Qwen3-30B-A3B NF4 LoRA frozen-linear stack)", "value": T / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"qwen3-30b-a3b frozen-linear stack: {L} layers x (q/k/v fused, o, grouped experts "
+                                   "gate_up and down over 65536 routed rows), fwd + recompute + bwd + AdamW",
+                       "layers": L, "tokens_per_gpu": T, "micro_batch": 2, "seq_len": 4096, "experts": E,
+                       "top_k": k, "expert_inter": I, "rank": r, "alpha": c["alpha"], "codec": args.codec,
+                       "parallelism": "dp1", "weights": "resident in HBM (no e2e streaming in this mode)"},
+            "step_tflops": step_flops / (ms / 1e3) / 1e12, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- main
 def main():
     args = parse()
+    if args.workload == "qwen3-30b-a3b":
+        world, rank, local = init_dist()
+        if world > 1:
+            raise SystemExit("the qwen3-30b-a3b workload runs on one GPU")
+        return run_moe(args, world, rank, local)
     if args.op or args.sweep:
         from spilltune_b200 import build
         build.build()

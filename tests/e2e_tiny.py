@@ -38,6 +38,8 @@ SEQ, ROWS, STEPS, ACCUM = 128, 16, 50, 2
 RANK, ALPHA, LR, SEED, TOKEN_CHUNK = 8, 16.0, 1e-4, 42, 64
 MODEL_SEED, DATA_SEED = 1234, 99
 TARGETS = ("self_attn.q_proj", "self_attn.v_proj", "self_attn.o_proj")  # reference adapters/targets.py:3-9
+ALL7 = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj", "mlp.gate_proj",
+        "mlp.up_proj", "mlp.down_proj")  # LoRA on every projection
 MATRICES = {"self_attn.q_proj": (HEADS * HEAD_DIM, HIDDEN), "self_attn.k_proj": (KV_HEADS * HEAD_DIM, HIDDEN),
             "self_attn.v_proj": (KV_HEADS * HEAD_DIM, HIDDEN), "self_attn.o_proj": (HIDDEN, HEADS * HEAD_DIM),
             "mlp.gate_proj": (INTER, HIDDEN), "mlp.up_proj": (INTER, HIDDEN), "mlp.down_proj": (HIDDEN, INTER)}
@@ -94,7 +96,7 @@ class Projection:
         self.grad_B.zero_()
 
 
-def make_adapters(device):
+def make_adapters(device, targets=TARGETS):
     """Per block, {target path: Projection}, with A drawn exactly as the
     reference's run does: torch.manual_seed(seed) at the start of
     engine.run, then randn(rank, in).mul_(0.02) block by block, target by
@@ -103,7 +105,7 @@ def make_adapters(device):
     blocks = []
     for _ in range(LAYERS):
         d = {}
-        for t in TARGETS:
+        for t in targets:
             N, K = MATRICES[t]
             A = torch.randn(RANK, K, dtype=torch.float32).mul_(0.02)
             d[t] = Projection(t, N, K, A, device)

@@ -31,6 +31,8 @@ reference; they only read these committed vectors.
   losses, every LoRA projection's gradients after steps 1 and 2, its A and B
   after step 50, and checksums of the initial A (to confirm the tests draw the
   same initial state).
+* ``tiny_llama_train_all7.npz`` — the same with LoRA on all seven projections
+  through a registered adapter (``_all7_factory``).
 """
 import os
 import sys
@@ -159,8 +161,68 @@ def head_case():
         loss=np.float32(loss.detach()), dnormalized_bf16=bits(dx))
 
 
-def tiny_llama_training():
-    """The reference engine on the tiny Llama (see tests/e2e_tiny.py)."""
+def _all7_factory():
+    """A registered adapter (the reference's extension API, adapters/registry.py:6-14)
+    that is the stock Llama adapter with LoRA on all seven projections: the
+    reference's target list is switched to the seven targets while the adapter
+    builds its blocks (create_lora_for_block, finetune/lora.py:319-388), and each
+    block's functional becomes a restatement of dense_block (adapters/dense.py:
+    120-153) that routes every projection through its LoRAProjection.forward."""
+    import torch.nn.functional as F
+    from ram_vram_finetune.adapters import targets as tg
+    from ram_vram_finetune.adapters.dense import LlamaAdapter, rms
+
+    def block7(hidden_states, position_embeddings, attention_mask, *, heads, kv_heads, head_dim, eps, lora_q,
+               lora_k, lora_v, lora_o, lora_gate, lora_up, lora_down, qk_norm=False, **weights):
+        def linear(x, path, lora):
+            return lora.forward(x, weights[path + ".weight"], weights.get(path + ".bias"))
+        residual = hidden_states
+        x = rms(hidden_states, weights["input_layernorm.weight"], eps)
+        shape = (*x.shape[:-1], -1, head_dim)
+        q = linear(x, "self_attn.q_proj", lora_q).view(shape)
+        k = linear(x, "self_attn.k_proj", lora_k).view(shape)
+        v = linear(x, "self_attn.v_proj", lora_v).view(shape).transpose(1, 2)
+        q, k = q.transpose(1, 2), k.transpose(1, 2)
+        cos, sin = (value.unsqueeze(1) for value in position_embeddings)
+
+        def rotate(t):
+            left, right = t.chunk(2, dim=-1)
+            return t * cos + torch.cat((-right, left), dim=-1) * sin
+        q, k = rotate(q), rotate(k)
+
+        def repeat(t):
+            b, h, s_, d = t.shape
+            return t[:, :, None].expand(b, h, heads // kv_heads, s_, d).reshape(b, heads, s_, d)
+        k, v = repeat(k), repeat(v)
+        scores = (q @ k.transpose(-2, -1)) * head_dim ** -0.5
+        probabilities = torch.softmax(scores + attention_mask, dim=-1, dtype=torch.float32).to(q.dtype)
+        attended = (probabilities @ v).transpose(1, 2).contiguous().reshape(*x.shape[:-1], heads * head_dim)
+        x = residual + linear(attended, "self_attn.o_proj", lora_o)
+        residual = x
+        x = rms(x, weights["post_attention_layernorm.weight"], eps)
+        return residual + linear(F.silu(linear(x, "mlp.gate_proj", lora_gate)) * linear(x, "mlp.up_proj", lora_up),
+                                 "mlp.down_proj", lora_down)
+
+    def factory(path, **kwargs):
+        saved = tg.ATTENTION_TARGETS["full_attention"]
+        tg.ATTENTION_TARGETS["full_attention"] = e2e_tiny.ALL7
+        try:
+            adapter = LlamaAdapter(path, **kwargs)
+        finally:
+            tg.ATTENTION_TARGETS["full_attention"] = saved
+        for block in adapter.blocks:
+            block.functional = block7
+            for key, path_ in (("lora_k", "self_attn.k_proj"), ("lora_gate", "mlp.gate_proj"),
+                               ("lora_up", "mlp.up_proj"), ("lora_down", "mlp.down_proj")):
+                block.kwargs[key] = block.adapters[path_]
+        return adapter
+    return factory
+
+
+def tiny_llama_training(targets="qvo"):
+    """The reference engine on the tiny Llama (see tests/e2e_tiny.py); targets
+    "qvo" uses the stock llama adapter (LoRA on q, v, o), "all7" a registered
+    adapter with LoRA on all seven projections."""
     import json
     import tempfile
     from safetensors.torch import save_file
@@ -184,7 +246,12 @@ def tiny_llama_training():
     with open(dataset, "w") as f:
         for ids, labels in t.token_rows():
             f.write(json.dumps({"input_ids": ids[0].tolist(), "labels": labels[0].tolist()}) + "\n")
-    config = TrainConfig(model=model, dataset=dataset, output=os.path.join(tmp, "out"), adapter="llama",
+    adapter_name = "llama"
+    if targets == "all7":
+        from ram_vram_finetune.adapters.registry import register
+        adapter_name = "tiny_llama_all7"
+        register(adapter_name, _all7_factory())
+    config = TrainConfig(model=model, dataset=dataset, output=os.path.join(tmp, "out"), adapter=adapter_name,
                          device="cpu", steps=t.STEPS, accumulation=t.ACCUM, rank=t.RANK, alpha=t.ALPHA,
                          learning_rate=t.LR, weight_decay=0.0, seed=t.SEED, token_chunk=t.TOKEN_CHUNK,
                          max_sequence_length=t.SEQ, checkpoint_every=10 ** 6, quantization="int4-sym-g128")
@@ -210,12 +277,13 @@ def tiny_llama_training():
     report = engine.run(config, progress_callback=capture)
     assert report["status"] == "completed"
     losses = np.array([m["loss"] for m in report["metrics"]], dtype=np.float64)
-    np.savez_compressed(os.path.join(HERE, "tiny_llama_train.npz"), losses=losses, **out)
-    print("tiny llama losses", losses[:3], "...", losses[-3:], file=sys.stderr)
+    name = "tiny_llama_train.npz" if targets == "qvo" else "tiny_llama_train_all7.npz"
+    np.savez_compressed(os.path.join(HERE, name), losses=losses, **out)
+    print("tiny llama", targets, "losses", losses[:3], "...", losses[-3:], file=sys.stderr)
 
 
 CASES = {"codec": codec_cases, "lora": lora_case, "moe": moe_case, "head": head_case,
-         "tiny_llama": tiny_llama_training}
+         "tiny_llama": tiny_llama_training, "tiny_llama_all7": lambda: tiny_llama_training("all7")}
 
 if __name__ == "__main__":
     # `make_golden.py [case ...]` regenerates only the named fixtures (all by default).

@@ -34,11 +34,23 @@ import e2e_tiny as t
 import oracle.codec as oc
 import oracle.linear as ol
 
-GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "tiny_llama_train.npz")
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+# LoRA targets of each fixture: the reference's default dense targets, and all seven
+# projections through a registered adapter.
+PLANS = {"qvo": ("tiny_llama_train.npz", t.TARGETS), "all7": ("tiny_llama_train_all7.npz", t.ALL7)}
+KWARG = {"self_attn.q_proj": "lora_q", "self_attn.k_proj": "lora_k", "self_attn.v_proj": "lora_v",
+         "self_attn.o_proj": "lora_o", "mlp.gate_proj": "lora_gate", "mlp.up_proj": "lora_up",
+         "mlp.down_proj": "lora_down"}
 
 
-def _fixture():
-    return dict(np.load(GOLDEN))
+def _fixture(plan):
+    return dict(np.load(os.path.join(GOLDEN, PLANS[plan][0])))
+
+
+def _lora_kwargs(adapters):
+    kw = {"lora_q": None, "lora_v": None, "lora_o": None}
+    kw.update({KWARG[path]: proj for path, proj in adapters.items()})
+    return kw
 
 
 def _packed_layers():
@@ -75,7 +87,7 @@ def _snapshot(store):
     return on_step
 
 
-def _compare(fx, got, blocks, loss_atol, grad_tol, update_rel):
+def _compare(fx, got, blocks, loss_atol, grad_tol, update_rel, targets):
     """Losses (absolute), step-1/2 LoRA gradients (assert_close tolerances) and
     the 50-step LoRA updates: rel-L2 of A_final - A_0 and of B_final (B_0 = 0)
     against the reference's.  Returns the worst loss error and update errors."""
@@ -87,7 +99,7 @@ def _compare(fx, got, blocks, loss_atol, grad_tol, update_rel):
         if key == "losses":
             continue
         torch.testing.assert_close(val, torch.from_numpy(fx[key]), **grad_tol, msg=key)
-    init = t.make_adapters("cpu")
+    init = t.make_adapters("cpu", targets)
     errs = {}
     for i, b in enumerate(blocks):
         for name, p in b.adapters.items():
@@ -100,12 +112,12 @@ def _compare(fx, got, blocks, loss_atol, grad_tol, update_rel):
     return worst, errs
 
 
-def _cpu_blocks(layers, raw):
+def _cpu_blocks(layers, raw, targets):
     """Blocks whose projections run the oracle: decode_into's bits (oracle C
     decoder) and LoRAProjection.forward's op order."""
     from spilltune_b200.dense import block_forward
     blocks = []
-    adapters = t.make_adapters("cpu")
+    adapters = t.make_adapters("cpu", targets)
     for i in range(t.LAYERS):
         decoded = {}
         for name, pw in layers[i].items():
@@ -113,8 +125,8 @@ def _cpu_blocks(layers, raw):
             decoded[name] = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).view(*pw.shape)
         weights = {**decoded, **raw[i]}
 
-        def functional(hidden_states, position_embeddings, attention_mask, *, lora_q, lora_v, lora_o, **w):
-            lora = {"self_attn.q_proj": lora_q, "self_attn.v_proj": lora_v, "self_attn.o_proj": lora_o}
+        def functional(hidden_states, position_embeddings, attention_mask, **w):
+            lora = {path: w.pop(key, None) for path, key in KWARG.items()}
 
             def linear(x, path):
                 W = w[path + ".weight"]
@@ -124,41 +136,44 @@ def _cpu_blocks(layers, raw):
             return block_forward(hidden_states, position_embeddings, attention_mask, linear, w, heads=t.HEADS,
                                  kv_heads=t.KV_HEADS, head_dim=t.HEAD_DIM, eps=t.EPS)
 
-        kw = {"lora_q": adapters[i]["self_attn.q_proj"], "lora_v": adapters[i]["self_attn.v_proj"],
-              "lora_o": adapters[i]["self_attn.o_proj"]}
-        blocks.append(t.Block(i, functional, kw, (lambda w=weights: w), adapters[i]))
+        blocks.append(t.Block(i, functional, _lora_kwargs(adapters[i]), (lambda w=weights: w), adapters[i]))
     return blocks
 
 
-def test_restated_engine_reproduces_reference_on_cpu():
-    fx = _fixture()
+@pytest.mark.parametrize("plan", sorted(PLANS))
+def test_restated_engine_reproduces_reference_on_cpu(plan):
+    fx = _fixture(plan)
+    targets = PLANS[plan][1]
     layers, raw, boundary = _packed_layers()
-    blocks = _cpu_blocks(layers, raw)
+    blocks = _cpu_blocks(layers, raw, targets)
     _check_initial_state(fx, blocks)
     got = {}
     got["losses"] = t.train(blocks, boundary["model.embed_tokens.weight"], boundary["model.norm.weight"],
                             boundary["lm_head.weight"], device=torch.device("cpu"),
                             terminal=t.reference_terminal, on_step=_snapshot(got))
-    _compare(fx, got, blocks, loss_atol=1e-5, grad_tol=dict(rtol=1e-3, atol=1e-6), update_rel=1e-4)
+    _compare(fx, got, blocks, loss_atol=1e-5, grad_tol=dict(rtol=1e-3, atol=1e-6), update_rel=1e-4, targets=targets)
 
 
 @pytest.mark.gpu
-def test_fused_path_trains_like_reference(cuda_lib):
-    """50 steps through the fused path on the GPU, streamed from pinned host memory."""
+@pytest.mark.parametrize("plan", sorted(PLANS))
+def test_fused_path_trains_like_reference(cuda_lib, plan):
+    """50 steps through the fused path on the GPU, streamed from pinned host memory
+    (with all seven targets, q/k/v and gate/up each run as one call with a
+    block-diagonal LoRA branch)."""
     from spilltune_b200 import _lib
     from spilltune_b200.dense import PackedBlockReloader, packed_dense_block
     from spilltune_b200.streaming import PackedSlotSession
-    fx = _fixture()
+    fx = _fixture(plan)
+    targets = PLANS[plan][1]
     dev = torch.device("cuda")
     layers, raw, boundary = _packed_layers()
     host = [{k: w.pin_memory() for k, w in layer.items()} for layer in layers]
     session = PackedSlotSession(host, dev, slots=2)
-    adapters = t.make_adapters(dev)
+    adapters = t.make_adapters(dev, targets)
     blocks = []
     for i in range(t.LAYERS):
         kw = {"heads": t.HEADS, "kv_heads": t.KV_HEADS, "head_dim": t.HEAD_DIM, "eps": t.EPS,
-              "lora_q": adapters[i]["self_attn.q_proj"], "lora_v": adapters[i]["self_attn.v_proj"],
-              "lora_o": adapters[i]["self_attn.o_proj"]}
+              **_lora_kwargs(adapters[i])}
         reloader = PackedBlockReloader(session, i, raw={k: v.to(dev) for k, v in raw[i].items()})
         blocks.append(t.Block(i, packed_dense_block, kw, reloader, adapters[i]))
     _check_initial_state(fx, blocks)
@@ -169,7 +184,8 @@ def test_fused_path_trains_like_reference(cuda_lib):
                             on_step=_snapshot(got))
     torch.cuda.synchronize()
     assert _lib.status() == 0
-    worst, errs = _compare(fx, got, blocks, loss_atol=1e-2, grad_tol=dict(rtol=0.06, atol=3e-3), update_rel=5e-2)
+    worst, errs = _compare(fx, got, blocks, loss_atol=1e-2, grad_tol=dict(rtol=0.06, atol=3e-3), update_rel=5e-2,
+                           targets=targets)
     # Every block borrowed its layer twice per micro-batch (forward, recompute);
     # with two slots for two layers only the first borrow loads on demand (the
     # second layer is prefetched) and both stay resident (eviction and reload

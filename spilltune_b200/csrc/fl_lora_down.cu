@@ -126,9 +126,18 @@ __global__ void prep_kernel(const float* __restrict__ q, int64_t q_sj, int64_t q
     const float* src = q + e * q_es + static_cast<int64_t>(64 * u + lane) * q_sr;
     uint32_t mask = 0;
     for (int n = 0; n < nq / 8; ++n) {
+      // The group's 16 loads go out together (unrolled, predicated), so a unit
+      // costs one memory round trip per group instead of one per column.
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int j = 8 * n + i;
+        v[2 * i] = j < rank ? __ldg(src + j * q_sj) : 0.f;
+        v[2 * i + 1] = j < rank ? __ldg(src + j * q_sj + 32 * q_sr) : 0.f;
+      }
       bool any = false;
-      for (int j = 8 * n; j < 8 * n + 8 && j < rank; ++j)
-        any |= (__ldg(src + j * q_sj) != 0.f) | (__ldg(src + j * q_sj + 32 * q_sr) != 0.f);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) any |= v[i] != 0.f;
       if (__any_sync(0xffffffffu, any)) mask |= 1u << n;
     }
     if (lane == 0) reinterpret_cast<uint32_t*>(qc + static_cast<int64_t>(e) * qc_es + 2 * plane)[u] = mask;

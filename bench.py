@@ -506,60 +506,67 @@ def run_reference(args, world, rank):
 # LoRA pair per expert.  `python bench.py --sweep` runs the kernel sweep: forward
 # and backward (LoRA rank 16, s = 2) of NF4-g128 weights N x K in {4096x4096,
 # 1024x4096, 14336x4096, 4096x14336} at M in {1, 16, 256, 2048, 8192}, one JSON
-# line each; each timing replays a CUDA graph of ten (256 MB buffer write + call)
-# pairs minus a graph of the ten writes alone, so the weights come from HBM and
-# host launch overhead is excluded.
-def _graph_us(fn, flush, reps=10):
-    """Device time of fn() per call: graph of (flush, fn) pairs minus graph of flushes."""
-    def timed(body):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for _ in range(reps):
-                body()
+# line each.  Each timing replays a CUDA graph of calls that rotate over C copies
+# of the weights and activations, C chosen so the copies together exceed three
+# L2s: every call reads cold weights from HBM, back to back as in a model step,
+# and host launch overhead is excluded.  (Writing a 256 MB buffer between calls
+# instead leaves dirty L2 lines whose write-back overlaps the next call; that
+# added 1.5-4 us to a decode-step call.)
+def _graph_us(fns, rounds=4):
+    """Device time per call of a CUDA graph of `rounds` passes over fns."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(rounds):
+            for fn in fns:
+                fn()
+    g.replay()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(3):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
         g.replay()
+        e.record()
         torch.cuda.synchronize()
-        best = float("inf")
-        for _ in range(3):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            g.replay()
-            e.record()
-            torch.cuda.synchronize()
-            best = min(best, s.elapsed_time(e) * 1e3)
-        return best
-
-    both = timed(lambda: (flush.add_(1), fn()))
-    alone = timed(lambda: flush.add_(1))
-    return (both - alone) / reps
+        best = min(best, s.elapsed_time(e) * 1e3)
+    del g
+    return best / (rounds * len(fns))
 
 
 def probe_sweep():
     from spilltune_b200 import codec, ops
     dev = torch.device("cuda")
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     r = 16
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     for (N, K) in [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336)]:
         g = torch.Generator(device=dev).manual_seed(1)
-        w = codec.encode(torch.randn(N, K, generator=g, device=dev) * 0.02, "nf4-g128")
+        w0 = codec.encode(torch.randn(N, K, generator=g, device=dev) * 0.02, "nf4-g128")
         A = torch.randn(r, K, generator=g, device=dev) * 0.01
         B = torch.randn(N, r, generator=g, device=dev) * 0.01
+        wbytes = N * K // 2 + 4 * N * K // 128
         for M in (1, 16, 256, 2048, 8192):
-            x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
-            dy = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
-            f = lambda: ops.fwd(x, w, A, B, 2.0)
-            b = lambda: ops.bwd(dy, x, w, A, B, 2.0)
-            for _ in range(2):
+            footprint = wbytes + 4 * M * (N + K)  # weights, X, dY, Y, dX
+            C = max(2, -(-3 * l2 // footprint))
+            ws = [w0] + [codec.PackedWeight(w0.payload.clone(), w0.scales.clone(), w0.lut, w0.shape, w0.codec)
+                         for _ in range(C - 1)]
+            xs = [torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16) for _ in range(C)]
+            dys = [torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16) for _ in range(C)]
+            fs = [lambda x=x, w=w: ops.fwd(x, w, A, B, 2.0) for x, w in zip(xs, ws)]
+            bs = [lambda x=x, w=w, dy=dy: ops.bwd(dy, x, w, A, B, 2.0) for x, w, dy in zip(xs, ws, dys)]
+            for f, b in zip(fs[:2], bs[:2]):
                 f()
                 b()
             torch.cuda.synchronize()
-            tf, tb = _graph_us(f, flush), _graph_us(b, flush)
-            wbytes = N * K // 2 + 4 * N * K // 128
+            rounds = max(1, 40 // C)
+            tf, tb = _graph_us(fs, rounds), _graph_us(bs, rounds)
             fl_f = 2 * M * N * K + 2 * M * K * r + 2 * M * r * N
             fl_b = 2 * M * N * K + 4 * M * N * r + 6 * M * K * r
-            print(json.dumps({"N": N, "K": K, "M": M, "fwd_us": round(tf, 1), "bwd_us": round(tb, 1),
+            print(json.dumps({"N": N, "K": K, "M": M, "copies": C, "fwd_us": round(tf, 1), "bwd_us": round(tb, 1),
                               "fwd_tflops": round(fl_f / tf / 1e6, 1), "bwd_tflops": round(fl_b / tb / 1e6, 1),
                               "fwd_weight_tbs": round(wbytes / tf / 1e6, 3),
                               "bwd_weight_tbs": round(wbytes / tb / 1e6, 3)}), flush=True)
+            del ws, xs, dys, fs, bs
+            torch.cuda.empty_cache()
 
 
 def probe_op(a):

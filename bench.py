@@ -101,6 +101,25 @@ def barrier(world):
         dist.barrier()
 
 
+def host_link_gbs(dev, nbytes, reps=5):
+    """Pinned host -> device copy bandwidth for one buffer of nbytes (best of reps, CUDA
+    events on a stream of its own): the link the slot session's copies use."""
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    best = float("inf")
+    with torch.cuda.stream(stream):
+        for _ in range(reps + 1):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            dst.copy_(src, non_blocking=True)
+            e.record(stream)
+            e.synchronize()
+            best = min(best, s.elapsed_time(e) / 1e3)
+    del src, dst
+    return nbytes / best / 1e9
+
+
 def max_over_ranks(x, world):
     if world == 1:
         return x
@@ -818,6 +837,9 @@ def main():
         sess = PackedSlotSession(host_layers, dev, slots=2, group=wgroup)
         if wgroup is not None:
             host_layers = None  # the session keeps this rank's shards only
+        # The host link the slot copies run over: a plain pinned-host -> device copy
+        # of one layer image and of 1 GiB, alone on a stream (outside the timed region).
+        link = {"layer_image": host_link_gbs(dev, sess.capacity), "1GiB": host_link_gbs(dev, 1 << 30)}
         x0_host = torch.randn(M, HIDDEN, dtype=torch.float32).to(torch.bfloat16).pin_memory()
         norm_host = torch.empty(1, dtype=torch.float32).pin_memory()
         estep = Step(sess.borrow, loras, bufs, world, opt)
@@ -847,6 +869,7 @@ def main():
         e2e = {"value": world * M / (ems / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": 4, "ms_per_step": ems,
                "slot_h2d_gbs": (sess.h2d_bytes / copy_s / 1e9) if copy_s > 0 else None,
+               "host_link_gbs": link,
                "weights": "pinned host, 2 VRAM slots, one-layer prefetch (fwd + bwd reload)"}
         if wgroup is not None:
             e2e["weights"] = (f"pinned host, 1/{world} of each layer per rank, copied into 2 VRAM slots and "

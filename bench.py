@@ -314,8 +314,9 @@ class Step:
                     _y, ts = self._fwd(x[src], w, lora, gname, return_ts=True)
                     self.ops.bwd(dy[gname], x[src], w, lora.A, lora.B, self.scale, dA=lora.A.grad,
                                  dB=lora.B.grad, accumulate=False, ts=ts)
-                    # prepass(B), lora_down(Us), backward GEMM, lora_grad x 2
-                    self.launches += 5
+                    # prepass(B), lora_down(Us; with rank <= 16 also dB), backward GEMM,
+                    # lora_grad(dA) [, lora_grad(dB) above rank 16]
+                    self.launches += 4 if lora.A.shape[0] <= 16 else 5
                     if lora.mask is not None:
                         lora.B.grad.mul_(lora.mask)  # no gradient for the zero blocks
             # Data parallel: this layer's LoRA gradients are final; all-reduce

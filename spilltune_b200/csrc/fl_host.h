@@ -64,10 +64,16 @@ int launch_nf4dq_prologue(const uint8_t* absmax_q, const float* nested_absmax, c
 // Two launches: the factor prepass, then the projection as its programmatic
 // dependent.  pdl: the prepass is itself a dependent of the previous launch
 // (it reads only q, written before the chain).
+// lo2 / grad / grad_done: with grad != nullptr, rank <= 16 and no tile list, the
+// same pass over P also adds grad[r * rank + j] += sum_m P[m, r] * lo2[m * 64 + j]
+// (lo2 bf16 [M, 64], complete before this call; grad fp32, cleared by the caller
+// when it starts a sum) and sets *grad_done; otherwise *grad_done stays false and
+// the caller computes grad itself (launch_lora_grad).
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
                      float s, void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles = nullptr,
                      const int* tile_count = nullptr, int max_tiles = 0, int64_t q_expert_stride = 0,
-                     int experts = 1, bool pdl = false);
+                     int experts = 1, bool pdl = false, const void* lo2 = nullptr, float* grad = nullptr,
+                     bool* grad_done = nullptr);
 // Small-M form (M <= 16): parts[m][j][c] (j < rank) = sum of P[m, r] * Q(j, r),
 // Q(j, r) = q[j * q_sj + r * q_sr], over the 128 * lora_parts_per_cluster(R)
 // columns of partial c, exact FP32 (parts: M * 64 * R / (128 * per_cluster)

@@ -25,6 +25,11 @@
 //    plays logical k = {2c, 2c+1, 2c+8, 2c+9} of step i, for both operands.
 //  * The CTAs of a cluster split the reduction; their partial sums meet in
 //    distributed shared memory, each CTA finishing 1/split of the rows.
+//  * The backward's Us pass (P = dY, rank <= 16) also sums dB = dY^T . Ts: per
+//    unit each consumer warp takes 16 of its 64 columns over all 128 rows,
+//    reading the dY tile transposed (ldmatrix) with Ts fragments kept in
+//    registers, and adds the result into dB with global reductions, so dY
+//    crosses HBM once for both.
 #include <cuda_bf16.h>
 #include <cstdint>
 
@@ -153,12 +158,20 @@ __device__ __forceinline__ uint32_t word(const uint4& a, const uint4& b, int w) 
   return k == 0 ? q.x : k == 1 ? q.y : k == 2 ? q.z : q.w;
 }
 
-template <int NQ>
+// kGrad (NQ == 16 only): the launch also adds grad[r, j] += sum_m P[m, r] *
+// Lo2[m, j] (j < rank) for every r of its units, from the P tiles already in
+// shared memory: with P = dY and Lo2 = Ts that is dB = dY^T . Ts of the
+// reference's LoRA backward (training/recompute.py:102-127), so the backward
+// streams dY once for Us and dB instead of twice.
+template <int NQ, bool kGrad = false>
 __global__ void __launch_bounds__(kThreads)
     lora_down_kernel(const __grid_constant__ CUtensorMap tm_p,  // P [M, R] bf16, box {64, 128}, 128B swizzle
                      int M, int R, const __nv_bfloat16* __restrict__ qc, int64_t qc_es, int rank, float s,
                      __nv_bfloat16* __restrict__ out, int split, const int4* __restrict__ tiles,
-                     const int* __restrict__ tile_count, uint32_t* status) {
+                     const int* __restrict__ tile_count, uint32_t* status,
+                     const __nv_bfloat16* __restrict__ lo2,  // kGrad: [M, 64] bf16 (Ts), zero past the rank
+                     float* __restrict__ grad) {             // kGrad: [R, rank] fp32, added into
+  static_assert(!kGrad || NQ == 16, "the gradient pass keeps Lo2 fragments for rank <= 16 in registers");
   using C = Cfg<NQ>;
   constexpr int NT = NQ / 8;  // n-tiles of 8 rank columns
   // A launch of the stream that may overlap this one (programmatic dependent
@@ -247,6 +260,24 @@ __global__ void __launch_bounds__(kThreads)
     // The unit masks are the prepass grid's output, like qc: wait for that grid
     // (the producer does the same before loading qc).
     griddep_wait();
+    // kGrad: B fragments of Lo2 for the CTA's 128 rows (8 k-steps of 16 rows x
+    // two 8-column tiles), lane (g, c) holding rows 2c, 2c + 1 (+8) of column g.
+    uint32_t lo2f[kGrad ? 8 : 1][2][2];
+    if constexpr (kGrad) {
+      const uint16_t* l2 = reinterpret_cast<const uint16_t*>(lo2);
+      auto at = [&](int row, int col) -> uint32_t {
+        const int m = m0 + row;
+        return m < m_end ? static_cast<uint32_t>(l2[static_cast<size_t>(m) * 64 + col]) : 0u;
+      };
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+        for (int rt = 0; rt < 2; ++rt) {
+          const int col = 8 * rt + g, r0 = 16 * kk + 2 * c;
+          lo2f[kk][rt][0] = at(r0, col) | (at(r0 + 1, col) << 16);
+          lo2f[kk][rt][1] = at(r0 + 8, col) | (at(r0 + 9, col) << 16);
+        }
+    }
     for (int k = 0; k < n_units; ++k) {
       const int st = k % kStages;
       const uint32_t um = umask[u0 + k];
@@ -288,6 +319,33 @@ __global__ void __launch_bounds__(kThreads)
             mma_16816(acc[t][n], a0, a1, a2, a3, bl0, bl1);
           }
         }
+      }
+      if constexpr (kGrad) {
+        // grad rows r = 64u + 16 warp + [0, 16) over the CTA's 128 rows of P: A = P^T
+        // (16 r x 16 rows of P per k-step, transposed out of the swizzled tile by
+        // ldmatrix: matrix i covers r-half i & 1 and row-half i >> 1), B = Lo2.
+        float gacc[2][4];
+#pragma unroll
+        for (int rt = 0; rt < 2; ++rt) gacc[rt][0] = gacc[rt][1] = gacc[rt][2] = gacc[rt][3] = 0.f;
+        const uint32_t stage_s = smem_u32(stage);
+        const int mi = lane >> 3;
+        const int chunk = 2 * warp + (mi & 1);  // 16-byte chunk (8 r) of the 128-byte row
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int row = 16 * kk + 8 * (mi >> 1) + (lane & 7);
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(stage_s + row * 128 + ((chunk ^ (row & 7)) << 4), a0, a1, a2, a3);
+#pragma unroll
+          for (int rt = 0; rt < 2; ++rt) mma_16816(gacc[rt], a0, a1, a2, a3, lo2f[kk][rt][0], lo2f[kk][rt][1]);
+        }
+        const int rbase = (u0 + k) * 64 + 16 * warp + g;
+#pragma unroll
+        for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = rbase + 8 * (i >> 1), j = 8 * rt + 2 * c + (i & 1);
+            if (j < rank && r < R) atomicAdd(grad + static_cast<size_t>(r) * rank + j, gacc[rt][i]);
+          }
       }
       // The stage's values are in registers: hand it back to the producer.
       __syncwarp();
@@ -351,9 +409,10 @@ __global__ void __launch_bounds__(kThreads)
   if (split > 1) cluster_sync();
 }
 
-template <int NQ>
+template <int NQ, bool kGrad = false>
 static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64_t qc_es, int rank, float s,
-                     void* out, cudaStream_t stream, const int4* tiles, const int* tile_count, int max_tiles) {
+                     void* out, cudaStream_t stream, const int4* tiles, const int* tile_count, int max_tiles,
+                     const void* lo2 = nullptr, float* grad = nullptr) {
   const int blocks = tiles ? max_tiles : (M + kRows - 1) / kRows;
   if (blocks < 1) return FL_OK;
   constexpr int kSmem = Cfg<NQ>::kSmem;
@@ -364,11 +423,11 @@ static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64
   static int slots[64] = {0};
   if (!slots[dev]) {
     int sms = 0, per_sm = 0;
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&lora_down_kernel<NQ>),
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&lora_down_kernel<NQ, kGrad>),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lora_down_kernel<NQ>, kThreads, kSmem);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lora_down_kernel<NQ, kGrad>, kThreads, kSmem);
     if (e != cudaSuccess || per_sm < 1) return set_error(FL_ERR_CUDA, "lora_down: occupancy query failed");
     slots[dev] = sms * per_sm;
   }
@@ -396,8 +455,9 @@ static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64
   int rc = make_tensor_map_2d(&tm, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, R, M, static_cast<uint64_t>(R) * 2, 64,
                               kRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  cudaError_t le = cudaLaunchKernelEx(&cfg, lora_down_kernel<NQ>, tm, M, R, qc, qc_es, rank, s,
-                                      static_cast<__nv_bfloat16*>(out), split, tiles, tile_count, status_word(dev));
+  cudaError_t le = cudaLaunchKernelEx(&cfg, lora_down_kernel<NQ, kGrad>, tm, M, R, qc, qc_es, rank, s,
+                                      static_cast<__nv_bfloat16*>(out), split, tiles, tile_count, status_word(dev),
+                                      static_cast<const __nv_bfloat16*>(lo2), grad);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }
@@ -648,7 +708,9 @@ size_t lora_factor_bytes(int64_t R, int rank) {
 
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank, float s,
                      void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles, const int* tile_count,
-                     int max_tiles, int64_t q_expert_stride, int experts, bool pdl) {
+                     int max_tiles, int64_t q_expert_stride, int experts, bool pdl, const void* lo2, float* grad,
+                     bool* grad_done) {
+  if (grad_done) *grad_done = false;
   if (R % 64 != 0) return set_error(FL_ERR_ARG, "lora_down: reduction dim %d not a multiple of 64", R);
   if (rank < 1 || rank > 64) return set_error(FL_ERR_ARG, "lora_down: rank %d outside [1, 64]", rank);
   if ((reinterpret_cast<uintptr_t>(P) | reinterpret_cast<uintptr_t>(out64) |
@@ -684,6 +746,14 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
     if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down prepass: %s", cudaGetErrorString(e));
   }
   const int64_t qc_es = static_cast<int64_t>(lora_factor_bytes(R, rank) / 2);
+  if (nq == 16 && grad != nullptr && lo2 != nullptr && tiles == nullptr) {
+    if ((reinterpret_cast<uintptr_t>(lo2) & 15u) != 0)
+      return set_error(FL_ERR_ARG, "lora_down: Lo2 must be 16-byte aligned");
+    const int rc = ld::launch_nq<16, true>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles,
+                                           lo2, grad);
+    if (rc == FL_OK && grad_done) *grad_done = true;
+    return rc;
+  }
   if (nq == 16) return ld::launch_nq<16>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
   if (nq == 32) return ld::launch_nq<32>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
   return ld::launch_nq<64>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);

@@ -442,6 +442,16 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Four 8x8 b16 matrices from shared memory, each transposed on the way (lane
+// 8i + r gives the address of row r of matrix i; register i receives matrix i
+// in the warp-MMA fragment layout).
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                  uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
 // 32-bit load from this CTA's shared memory at a shared-window address.
 __device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
   uint32_t v;

@@ -64,11 +64,12 @@ int launch_nf4dq_prologue(const uint8_t* absmax_q, const float* nested_absmax, c
 // Two launches: the factor prepass, then the projection as its programmatic
 // dependent.  pdl: the prepass is itself a dependent of the previous launch
 // (it reads only q, written before the chain).
-// lo2 / grad / grad_done: with grad != nullptr, rank <= 16 and no tile list, the
-// same pass over P also adds grad[r * rank + j] += sum_m P[m, r] * lo2[m * 64 + j]
-// (lo2 bf16 [M, 64], complete before this call; grad fp32, cleared by the caller
-// when it starts a sum) and sets *grad_done; otherwise *grad_done stays false and
-// the caller computes grad itself (launch_lora_grad).
+// lo2 / grad / grad_done: with grad != nullptr and rank <= 16 the same pass over P
+// also adds grad[r * rank + j] += sum_m P[m, r] * lo2[m * 64 + j] (lo2 bf16
+// [M, 64], complete before this call; grad fp32, cleared by the caller when it
+// starts a sum; grouped: expert e's rows into grad + e * q_expert_stride) and sets
+// *grad_done; otherwise *grad_done stays false and the caller computes grad
+// itself (launch_lora_grad).
 int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, int64_t q_sr, int rank,
                      float s, void* out64, void* qc_scratch, cudaStream_t stream, const int4* tiles = nullptr,
                      const int* tile_count = nullptr, int max_tiles = 0, int64_t q_expert_stride = 0,

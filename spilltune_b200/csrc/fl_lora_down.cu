@@ -170,7 +170,8 @@ __global__ void __launch_bounds__(kThreads)
                      __nv_bfloat16* __restrict__ out, int split, const int4* __restrict__ tiles,
                      const int* __restrict__ tile_count, uint32_t* status,
                      const __nv_bfloat16* __restrict__ lo2,  // kGrad: [M, 64] bf16 (Ts), zero past the rank
-                     float* __restrict__ grad) {             // kGrad: [R, rank] fp32, added into
+                     float* __restrict__ grad,               // kGrad: [R, rank] fp32 per expert, added into
+                     int64_t grad_es) {                      // kGrad, grouped: floats from one expert's grad to the next
   static_assert(!kGrad || NQ == 16, "the gradient pass keeps Lo2 fragments for rank <= 16 in registers");
   using C = Cfg<NQ>;
   constexpr int NT = NQ / 8;  // n-tiles of 8 rank columns
@@ -196,6 +197,7 @@ __global__ void __launch_bounds__(kThreads)
     m0 = t.y;
     m_end = min(t.z, M);
     qc += t.x * qc_es;
+    if constexpr (kGrad) grad += t.x * grad_es;
   }
   const int64_t plane = static_cast<int64_t>(NQ) * R;
   const int units = R / 64;
@@ -412,7 +414,7 @@ __global__ void __launch_bounds__(kThreads)
 template <int NQ, bool kGrad = false>
 static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64_t qc_es, int rank, float s,
                      void* out, cudaStream_t stream, const int4* tiles, const int* tile_count, int max_tiles,
-                     const void* lo2 = nullptr, float* grad = nullptr) {
+                     const void* lo2 = nullptr, float* grad = nullptr, int64_t grad_es = 0) {
   const int blocks = tiles ? max_tiles : (M + kRows - 1) / kRows;
   if (blocks < 1) return FL_OK;
   constexpr int kSmem = Cfg<NQ>::kSmem;
@@ -457,7 +459,7 @@ static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64
   if (rc) return rc;
   cudaError_t le = cudaLaunchKernelEx(&cfg, lora_down_kernel<NQ, kGrad>, tm, M, R, qc, qc_es, rank, s,
                                       static_cast<__nv_bfloat16*>(out), split, tiles, tile_count, status_word(dev),
-                                      static_cast<const __nv_bfloat16*>(lo2), grad);
+                                      static_cast<const __nv_bfloat16*>(lo2), grad, grad_es);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }
@@ -746,11 +748,12 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
     if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "lora_down prepass: %s", cudaGetErrorString(e));
   }
   const int64_t qc_es = static_cast<int64_t>(lora_factor_bytes(R, rank) / 2);
-  if (nq == 16 && grad != nullptr && lo2 != nullptr && tiles == nullptr) {
+  if (nq == 16 && grad != nullptr && lo2 != nullptr) {
     if ((reinterpret_cast<uintptr_t>(lo2) & 15u) != 0)
       return set_error(FL_ERR_ARG, "lora_down: Lo2 must be 16-byte aligned");
+    // Grouped launches: expert e's gradient sits one factor's size after e - 1's.
     const int rc = ld::launch_nq<16, true>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles,
-                                           lo2, grad);
+                                           lo2, grad, q_expert_stride);
     if (rc == FL_OK && grad_done) *grad_done = true;
     return rc;
   }

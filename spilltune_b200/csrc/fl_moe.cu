@@ -256,16 +256,22 @@ int fl_grouped_bwd(const uint16_t* dY, const uint16_t* X, const int32_t* seg, in
   const int r = static_cast<int>(rows), n = static_cast<int>(N), k = static_cast<int>(K);
   if ((rc = launch_moe_plan(seg, experts, r, kBwdRows, (k + 255) / 256, t_bwd, p.bwd_tiles, counts + 0, status, st)))
     return rc;
+  bool db_done = false;
   if (rank > 0) {
     if ((rc = launch_moe_plan(seg, experts, r, kDownRows, 1, t_down, p.down_tiles, counts + 1, status, st))) return rc;
     if ((rc = launch_moe_plan(seg, experts, r, kGradRows, 1, t_grad, p.grad_tiles, counts + 2, status, st))) return rc;
-    // Us = bf16(s * dY . B_e): Q(j, n) = B_e[n * rank + j], B_e = B + e * N * rank
-    if ((rc = launch_lora_down(dY, r, n, B, 1, rank, rank, scale, us, ws + p.off_qb, st, t_down, counts + 1,
-                               p.down_tiles, static_cast<int64_t>(N) * rank, experts)))
-      return rc;
     // Ts = bf16(s * X . A_e^T): Q(j, k) = A_e[j * K + k]
     if ((rc = launch_lora_down(X, r, k, A, K, 1, rank, scale, ts, ws + p.off_qa, st, t_down, counts + 1,
                                p.down_tiles, static_cast<int64_t>(rank) * K, experts)))
+      return rc;
+    // Us = bf16(s * dY . B_e): Q(j, n) = B_e[n * rank + j], B_e = B + e * N * rank; with
+    // rank <= 16 the same pass over dY adds dB_e[n, j] += sum_{m in e} dY[m, n] Ts[m, j].
+    if (!accumulate) {
+      const cudaError_t e = cudaMemsetAsync(dB, 0, static_cast<size_t>(experts) * N * rank * sizeof(float), st);
+      if (e != cudaSuccess) return set_error(FL_ERR_CUDA, "fl_grouped_bwd: dB clear: %s", cudaGetErrorString(e));
+    }
+    if ((rc = launch_lora_down(dY, r, n, B, 1, rank, rank, scale, us, ws + p.off_qb, st, t_down, counts + 1,
+                               p.down_tiles, static_cast<int64_t>(N) * rank, experts, false, ts, dB, &db_done)))
       return rc;
   }
   if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, r, n, k, status, st, t_bwd, counts + 0,
@@ -276,9 +282,11 @@ int fl_grouped_bwd(const uint16_t* dY, const uint16_t* X, const int32_t* seg, in
     if ((rc = launch_lora_grad(X, r, k, us, rank, dA, 1, K, accumulate, st, t_grad, counts + 2, p.grad_tiles,
                                static_cast<int64_t>(rank) * K, static_cast<int64_t>(experts) * rank * K)))
       return rc;
-    // dB_e[n, j] = sum_{m in e} dY[m, n] Ts[m, j]
-    if ((rc = launch_lora_grad(dY, r, n, ts, rank, dB, rank, 1, accumulate, st, t_grad, counts + 2, p.grad_tiles,
-                               static_cast<int64_t>(N) * rank, static_cast<int64_t>(experts) * N * rank)))
+    // dB_e[n, j] = sum_{m in e} dY[m, n] Ts[m, j], unless the Us pass summed it (it was
+    // cleared above, so this adds into it)
+    if (!db_done && (rc = launch_lora_grad(dY, r, n, ts, rank, dB, rank, 1, 1, st, t_grad, counts + 2,
+                                           p.grad_tiles, static_cast<int64_t>(N) * rank,
+                                           static_cast<int64_t>(experts) * N * rank)))
       return rc;
   }
   return FL_OK;

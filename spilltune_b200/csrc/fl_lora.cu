@@ -2,8 +2,8 @@
 // fl_lora_down.cu):
 //
 //   lora_grad : out(p, j) (+)= sum_m P[m, p] * Lo[m, j]          (fp32 out)
-//               dA = Us^T . X  (P = X),  dB = dY^T . Ts (P = dY; for a dense
-//               call of rank <= 16 lora_down sums dB in its pass over dY)
+//               dA = Us^T . X  (P = X),  dB = dY^T . Ts (P = dY; at rank <= 16
+//               lora_down sums dB in its pass over dY instead)
 //   (reference: the FP32 autograd of F.linear(F.linear(x.float(), A), B),
 //   training/recompute.py:102-127)
 //

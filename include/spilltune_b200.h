@@ -139,7 +139,10 @@ int fl_bwd(const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N, int64_t 
  * (F.linear(F.linear(x, A), B) in finetune/lora.py:219-220; its backward in
  * training/recompute.py:102-127).  fl_fwd leaves exactly these bytes in the
  * first M * 128 bytes of its workspace whenever this function reads them, so
- * the results equal fl_bwd's bit for bit while X . A^T is not recomputed.
+ * the results equal fl_bwd's while X . A^T is not recomputed: dX bit for bit,
+ * dA and dB up to the order of their FP32 sums (both are summed with atomic
+ * adds, and with rank <= 16 this entry point sums dB in the same pass over dY
+ * that forms Us).
  * Ts is not read when rank == 0, or when M <= 16 with K % 512 == 0 and the
  * group-128 layout (the decode-step kernels, which form Ts themselves); it may
  * then be NULL, as it may always be (then this is fl_bwd).  Ts must be 16-byte

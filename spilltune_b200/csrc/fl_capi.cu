@@ -232,15 +232,16 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
     return launch_smallm_bwd(dY, X, uparts, tparts, scale, payload, scales, lut16, A, rank, dX, dA, dB, accumulate,
                              (int)M, (int)N, (int)K, st);
   }
-  // One chain of programmatic dependent launches after the gradient clears:
-  // [prepass(A) -> lora_down(Ts), unless the caller passed the forward's Ts] ->
-  // prepass(B) -> lora_down(Us; with rank <= 16 it also adds dB = dY^T . Ts from
-  // the same dY tiles) -> backward GEMM -> lora_grad(dA) [-> lora_grad(dB) when
-  // lora_down did not].  Each kernel waits for the previous grid before reading
-  // what the chain produced (a prepass finishes no earlier than the launch before
-  // it, so Ts is complete when lora_down(Us) reads it); the gradient kernels
-  // start once the GEMM has seen Us complete and fill the SMs its last tiles
-  // leave idle.
+  // One chain of programmatic dependent launches after the gradient clears.
+  // Given the forward's Ts: prepass(B) -> lora_down(Us; with rank <= 16 it also
+  // adds dB = dY^T . Ts from the same dY tiles) -> backward GEMM -> lora_grad(dA)
+  // [-> lora_grad(dB) above rank 16].  Without it: prepass(B) -> lora_down(Us) ->
+  // prepass(A) -> lora_down(Ts) -> backward GEMM -> lora_grad(dA) ->
+  // lora_grad(dB) (computing Ts first so that one pass could also sum dB
+  // serialises the two low-rank passes, which measured slower).  Each kernel
+  // waits for the previous grid before reading what the chain produced; the
+  // gradient kernels start once the GEMM has seen Us and Ts complete and fill
+  // the SMs its last tiles leave idle.
   if (rank > 0 && ts_in != nullptr) ts = reinterpret_cast<uint8_t*>(const_cast<uint16_t*>(ts_in));  // read only
   if (rank > 0 && !accumulate) {
     cudaError_t e = cudaMemsetAsync(dA, 0, static_cast<size_t>(rank) * K * sizeof(float), st);
@@ -249,14 +250,17 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
   }
   bool db_done = false;
   if (rank > 0) {
+    // Us = bf16(s * dY . B): Q(j, n) = B[n * rank + j]; given Ts, also dB[n, j] +=
+    // sum_m dY[m, n] Ts[m, j] in the same pass when the rank allows it.
+    const bool have_ts = ts_in != nullptr;
+    if ((rc = launch_lora_down(dY, (int)M, (int)N, B, 1, rank, rank, scale, us, qc_b, st, nullptr, nullptr, 0, 0, 1,
+                               /*pdl=*/false, have_ts ? ts : nullptr, have_ts ? dB : nullptr, &db_done)))
+      return rc;
     // Ts = bf16(s * X . A^T): Q(j, k) = A[j * K + k], unless the caller kept
     // the forward's.
-    if (ts_in == nullptr && (rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, qc_a, st)))
-      return rc;
-    // Us = bf16(s * dY . B): Q(j, n) = B[n * rank + j]; and dB[n, j] += sum_m dY[m, n] Ts[m, j]
-    // in the same pass when the rank allows it.
-    if ((rc = launch_lora_down(dY, (int)M, (int)N, B, 1, rank, rank, scale, us, qc_b, st, nullptr, nullptr, 0, 0, 1,
-                               /*pdl=*/ts_in == nullptr, ts, dB, &db_done)))
+    if (!have_ts &&
+        (rc = launch_lora_down(X, (int)M, (int)K, A, K, 1, rank, scale, ts, qc_a, st, nullptr, nullptr, 0, 0, 1,
+                               /*pdl=*/true)))
       return rc;
   }
   if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, (int)M, (int)N, (int)K, status, st,

@@ -74,6 +74,7 @@ def parse():
     p.add_argument("--iters", type=int, default=1)
     p.add_argument("--time", action="store_true")
     p.add_argument("--experts", type=int, default=1)
+    p.add_argument("--ts", action="store_true", help="--op bwd: pass the forward's Ts (fl_bwd_ts, the step's path)")
     p.add_argument("--top-k", type=int, default=8)
     p.add_argument("--sweep", action="store_true", help="kernel sweep: 4 Llama-3-8B shapes x M in {1..8192}")
     return p.parse_args()
@@ -611,9 +612,10 @@ def probe_op(a):
         }[a.op]
     else:
         out = torch.empty(a.N, a.K, dtype=torch.bfloat16, device=dev)
+        ts = ops.fwd(x, w, A, B, 2.0, return_ts=True)[1] if a.ts and a.op == "bwd" and a.rank else None
         fn = {
             "fwd": lambda: ops.fwd(x, w, A, B, 2.0),
-            "bwd": lambda: ops.bwd(dy, x, w, A, B, 2.0),
+            "bwd": (lambda: ops.bwd(dy, x, w, A, B, 2.0, ts=ts)) if ts is not None else (lambda: ops.bwd(dy, x, w, A, B, 2.0)),
             "dequant": lambda: ops.dequant(w, out=out),
         }[a.op]
     for _ in range(2):

@@ -55,7 +55,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=["llama3-8b", "qwen3-30b-a3b"], default="llama3-8b",
-                   help="llama3-8b: the headline step (BASELINE config 3); qwen3-30b-a3b: config 4's MoE stack")
+                   help="llama3-8b: the headline step (Llama-3-8B stack, 32 layers); qwen3-30b-a3b: the Qwen3-MoE 30B-A3B stack")
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--tokens", type=int, default=8192, help="tokens per GPU per step (micro-batch 4 x seq 2048)")
     p.add_argument("--codec", default="nf4-g128")
@@ -639,14 +639,14 @@ def probe_op(a):
                       "tflops": flops / us / 1e6 if flops else None}))
 
 
-# ---------------------------------------------------------------- Qwen3-30B-A3B
+# ---------------------------------------------------------------- Qwen3-30B-A3B MoE stack
 MOE = {"layers": 48, "hidden": 2048, "q": 4096, "kv": 512, "experts": 128, "top_k": 8, "inter": 768, "rank": 8,
        "alpha": 16.0, "tokens": 8192}
 
 
 def run_moe(args, world, rank, local):
-    """The frozen-linear stack of a Qwen3-30B-A3B-shaped model (BASELINE
-    config 4: 48 layers, hidden 2048, 32 x 128 query heads, 4 KV heads, 128
+    """The frozen-linear stack of a Qwen3-30B-A3B-shaped model (the MoE
+    training configuration: 48 layers, hidden 2048, 32 x 128 query heads, 4 KV heads, 128
     experts top-8 with expert intermediate 768; NF4 group-128 records; LoRA
     rank 8 on the attention projections and per expert on gate_up / down;
     seq 4096 x micro-batch 2 = 8192 tokens per GPU).  Per layer: q/k/v fused

@@ -1,6 +1,6 @@
 """Tiny-Llama LoRA streaming training for end-to-end parity -- test infrastructure.
 
-The workload is BASELINE config 1 run for 50 optimizer steps: a random Llama
+The workload is the tiny-Llama training configuration run for 50 optimizer steps: a random Llama
 (2 decoder layers, hidden 256, 4 heads of 64, 2 KV heads, SwiGLU 768, vocab
 2048, RMSNorm eps 1e-6, RoPE theta 1e4), frozen decoder matrices stored
 int4-sym-g128, LoRA rank 8 alpha 16 on the reference's default dense targets
@@ -39,7 +39,7 @@ RANK, ALPHA, LR, SEED, TOKEN_CHUNK = 8, 16.0, 1e-4, 42, 64
 MODEL_SEED, DATA_SEED = 1234, 99
 TARGETS = ("self_attn.q_proj", "self_attn.v_proj", "self_attn.o_proj")  # reference adapters/targets.py:3-9
 ALL7 = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj", "mlp.gate_proj",
-        "mlp.up_proj", "mlp.down_proj")  # LoRA on every projection
+        "mlp.up_proj", "mlp.down_proj")  # the tiny-Llama configuration: LoRA on every projection
 MATRICES = {"self_attn.q_proj": (HEADS * HEAD_DIM, HIDDEN), "self_attn.k_proj": (KV_HEADS * HEAD_DIM, HIDDEN),
             "self_attn.v_proj": (KV_HEADS * HEAD_DIM, HIDDEN), "self_attn.o_proj": (HIDDEN, HEADS * HEAD_DIM),
             "mlp.gate_proj": (INTER, HIDDEN), "mlp.up_proj": (INTER, HIDDEN), "mlp.down_proj": (HIDDEN, INTER)}

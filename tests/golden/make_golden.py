@@ -32,7 +32,7 @@ reference; they only read these committed vectors.
   after step 50, and checksums of the initial A (to confirm the tests draw the
   same initial state).
 * ``tiny_llama_train_all7.npz`` — the same with LoRA on all seven projections
-  through a registered adapter (``_all7_factory``).
+  (the tiny-Llama training configuration) through a registered adapter (``_all7_factory``).
 """
 import os
 import sys
@@ -222,7 +222,7 @@ def _all7_factory():
 def tiny_llama_training(targets="qvo"):
     """The reference engine on the tiny Llama (see tests/e2e_tiny.py); targets
     "qvo" uses the stock llama adapter (LoRA on q, v, o), "all7" a registered
-    adapter with LoRA on all seven projections."""
+    adapter with LoRA on all seven projections (the tiny-Llama training configuration)."""
     import json
     import tempfile
     from safetensors.torch import save_file

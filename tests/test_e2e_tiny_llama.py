@@ -36,7 +36,7 @@ import oracle.linear as ol
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 # LoRA targets of each fixture: the reference's default dense targets, and all seven
-# projections through a registered adapter.
+# projections (the tiny-Llama training configuration) through a registered adapter.
 PLANS = {"qvo": ("tiny_llama_train.npz", t.TARGETS), "all7": ("tiny_llama_train_all7.npz", t.ALL7)}
 KWARG = {"self_attn.q_proj": "lora_q", "self_attn.k_proj": "lora_k", "self_attn.v_proj": "lora_v",
          "self_attn.o_proj": "lora_o", "mlp.gate_proj": "lora_gate", "mlp.up_proj": "lora_up",

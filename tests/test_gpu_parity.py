@@ -1,12 +1,12 @@
 """GPU parity of the CUDA path (through the C ABI) against the CPU oracle.
 
-Bars:
+Bars (the project's correctness requirements):
   * dequantized weights bit-exact with decode_into;
   * Y, dX, dA, dB within rel-L2 <= 1e-2 of the FP32 reference
     (oracle.linear.*_fp32 on the oracle-decoded weight).  The tests also hold a
     tighter 5e-3 line: the kernels accumulate in fp32, so only the bf16 output
     rounding and the bf16 low-rank operands separate them from the FP32 shadow.
-At the BASELINE sweep's full sizes the CPU cannot run the whole product, so the
+At the kernel sweep's full sizes the CPU cannot run the whole product, so the
 check samples token rows (the oracle computes those rows exactly) and checks
 row independence of the GPU result.
 """
@@ -212,7 +212,7 @@ def test_reference_golden_through_cuda_path(cuda_lib):
 
 @pytest.mark.parametrize("N,K", [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336)])
 def test_full_size_sampled_rows(cuda_lib, N, K):
-    """BASELINE sweep shapes at M=2048: oracle-exact rows + row independence."""
+    """Kernel-sweep shapes at M=2048: oracle-exact rows + row independence."""
     from spilltune_b200 import ops
     M, rank, s = 2048, 16, 2.0
     pw, x, A, B, dy = _problem(M, N, K, rank, "nf4-g128", seed=N + K, fstd=0.01)

@@ -55,6 +55,10 @@ def _worker_reduce(rank, world, port, q):
         dist.all_reduce(w.grad)
         out["dp_grad"] = w.grad.clone()
         out["ref_grad"] = torch.cat(xs).sum(0) / sum(counts)
+        # Plain NumPy copies: torch tensors put on a queue travel as shared-memory
+        # handles, which vanish if this process exits before the parent reads them.
+        out["grads"] = [[g.numpy() for g in gl] for gl in out["grads"]]
+        out["dp_grad"], out["ref_grad"] = out["dp_grad"].numpy(), out["ref_grad"].numpy()
         q.put((rank, out))
     finally:
         if dist.is_initialized():
@@ -76,10 +80,10 @@ def test_two_rank_gradient_reduction_sharding_and_normalisation():
         out = res[r]
         assert out["buckets"] == 3 and out["bytes"] == 3 * 4 * (64 + 96)
         for l, (ga, gb) in enumerate(out["grads"]):
-            assert torch.equal(ga, torch.full((4, 16), float(1 + l + 2 + l)))       # (1+l) + (2+l)
-            assert torch.equal(gb, torch.full((24, 4), float(10 + l + 20 + l)))
+            assert torch.equal(torch.from_numpy(ga), torch.full((4, 16), float(1 + l + 2 + l)))  # (1+l) + (2+l)
+            assert torch.equal(torch.from_numpy(gb), torch.full((24, 4), float(10 + l + 20 + l)))
         assert out["global_tokens"] == 28
-        assert torch.allclose(out["dp_grad"], out["ref_grad"], atol=1e-6)
+        assert torch.allclose(torch.from_numpy(out["dp_grad"]), torch.from_numpy(out["ref_grad"]), atol=1e-6)
     assert sorted(res[0]["mine"] + res[1]["mine"]) == [0, 1, 2, 3, 4]
     assert not set(res[0]["mine"]) & set(res[1]["mine"])
 

@@ -77,6 +77,7 @@ def parse():
     p.add_argument("--ts", action="store_true", help="--op bwd: pass the forward's Ts (fl_bwd_ts, the step's path)")
     p.add_argument("--top-k", type=int, default=8)
     p.add_argument("--sweep", action="store_true", help="kernel sweep: 4 Llama-3-8B shapes x M in {1..8192}")
+    p.add_argument("--sweep-m", default="1,16,256,2048,8192", help="--sweep: token counts, comma separated")
     return p.parse_args()
 
 
@@ -554,7 +555,7 @@ def _graph_us(fns, rounds=4):
     return best / (rounds * len(fns))
 
 
-def probe_sweep():
+def probe_sweep(ms=(1, 16, 256, 2048, 8192)):
     from spilltune_b200 import codec, ops
     dev = torch.device("cuda")
     r = 16
@@ -565,7 +566,7 @@ def probe_sweep():
         A = torch.randn(r, K, generator=g, device=dev) * 0.01
         B = torch.randn(N, r, generator=g, device=dev) * 0.01
         wbytes = N * K // 2 + 4 * N * K // 128
-        for M in (1, 16, 256, 2048, 8192):
+        for M in ms:
             footprint = wbytes + 4 * M * (N + K)  # weights, X, dY, Y, dX
             C = max(2, -(-3 * l2 // footprint))
             ws = [w0] + [codec.PackedWeight(w0.payload.clone(), w0.scales.clone(), w0.lut, w0.shape, w0.codec)
@@ -772,7 +773,7 @@ def main():
         from spilltune_b200 import build
         build.build()
         if args.sweep:
-            probe_sweep()
+            probe_sweep(tuple(int(m) for m in args.sweep_m.split(",")))
         else:
             probe_op(args)
         return 0

@@ -87,6 +87,16 @@ int fl_dequant(const uint8_t* payload, const float* scales, const float* lut16, 
  * padded to 16); 0 when rank == 0. */
 size_t fl_fwd_workspace_bytes(int64_t M, int64_t K, int rank);
 
+/* fl_fwd_workspace_bytes plus room for FP32 partial sums when the call has too
+ * few 256 x 256 output tiles to occupy the GPU (few tokens or few output
+ * columns, e.g. 256 tokens of a 4096-wide projection): the tile GEMM then also
+ * splits its reduction over K into 2-16 slices and a second kernel adds them in
+ * slice order.  Given a workspace this large, fl_fwd and fl_fwd_nf4dq split;
+ * given one of fl_fwd_workspace_bytes, they do not (results then differ only
+ * in the order of the FP32 sums: each slice is summed on its own).  No
+ * counterpart in the reference (one cuBLAS F.linear per projection). */
+size_t fl_fwd_workspace_bytes_split(int64_t M, int64_t N, int64_t K, int rank);
+
 /*
  * Frozen projection forward with the LoRA branch
  *   Y[M,N] = X[M,K] . W^T + scale * (X . A^T) . B^T
@@ -102,7 +112,8 @@ size_t fl_fwd_workspace_bytes(int64_t M, int64_t K, int rank);
  * Ts = bf16(scale * X . A^T).
  * Requires K % 128 == 0, rank <= 64, 16-byte aligned pointers, bias-free
  * projections.  workspace: >= fl_fwd_workspace_bytes(M, K, rank) bytes,
- * 16-byte aligned (may be NULL when rank == 0).
+ * 16-byte aligned (may be NULL when rank == 0); fl_fwd_workspace_bytes_split
+ * bytes let a call with few output tiles split its reduction.
  */
 int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, const float* scales,
            const float* lut16, int64_t N, const float* A, const float* B, int rank, float scale, uint16_t* Y,
@@ -114,6 +125,11 @@ int fl_fwd(const uint16_t* X, int64_t M, int64_t K, const uint8_t* payload, cons
  * 64-row units (the block-diagonal B of projections stacked over one input)
  * costs correspondingly less low-rank work. */
 size_t fl_bwd_workspace_bytes(int64_t M, int64_t N, int64_t K, int rank);
+
+/* The same for fl_bwd / fl_bwd_ts / the NF4-DQ64 backward: room for FP32
+ * partial sums of dX when its 256 x 256 tiles are too few, the reduction over
+ * N then split into slices (dX's summation order changes; dA and dB do not). */
+size_t fl_bwd_workspace_bytes_split(int64_t M, int64_t N, int64_t K, int rank);
 
 /*
  * Recomputed-backward of the same projection (the autograd VJP that

@@ -34,6 +34,8 @@ SIGNATURES = {
     "fl_fwd_workspace_bytes": ([_I64, _I64, _INT], _SZ),
     "fl_fwd": ([_P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _INT, _F, _P, _P, _SZ, _P], _INT),
     "fl_bwd_workspace_bytes": ([_I64, _I64, _I64, _INT], _SZ),
+    "fl_fwd_workspace_bytes_split": ([_I64, _I64, _I64, _INT], _SZ),
+    "fl_bwd_workspace_bytes_split": ([_I64, _I64, _I64, _INT], _SZ),
     "fl_bwd": ([_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _INT, _F, _P, _P, _P, _INT, _P, _SZ, _P], _INT),
     "fl_bwd_ts": ([_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _INT, _F, _P, _P, _P, _P, _INT, _P, _SZ, _P], _INT),
     "fl_fwd_noalloc": ([_P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _INT, _F, _P, _P], _INT),

@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libspilltune_b200.so")
-SOURCES = ["fl_capi.cu", "fl_dequant.cu", "fl_lora.cu", "fl_lora_down.cu", "fl_gemm.cu", "fl_gemm_bwd.cu", "fl_smallm.cu", "fl_smallm_bwd.cu", "fl_noalloc.cu", "fl_moe.cu", "fl_head.cu"]
+SOURCES = ["fl_capi.cu", "fl_dequant.cu", "fl_lora.cu", "fl_lora_down.cu", "fl_gemm.cu", "fl_gemm_bwd.cu", "fl_smallm.cu", "fl_smallm_bwd.cu", "fl_noalloc.cu", "fl_moe.cu", "fl_head.cu", "fl_split.cu"]
 HEADERS = ["fl_ptx.cuh", "fl_codebook.cuh", "fl_host.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -73,7 +73,7 @@ using namespace fl;
 
 extern "C" {
 
-int fl_version(void) { return 300; }  // 0.3.0: fl_wait_selftest, CE target status bit
+int fl_version(void) { return 310; }  // 0.3.1: reduction splits (fl_*_workspace_bytes_split)
 
 int fl_wait_selftest(uint64_t limit_ns, void* stream) {
   if (limit_ns == 0 || limit_ns > kWaitLimitNs)
@@ -135,6 +135,54 @@ size_t fl_bwd_workspace_bytes(int64_t M, int64_t N, int64_t K, int rank) {
   return static_cast<size_t>(M) * 256 + lora_factor_bytes(N, rank) + lora_factor_bytes(K, rank);
 }
 
+}  // extern "C"
+
+// Reduction splits of the tile GEMMs (fl_split.cu): output tiles x splits
+// fill the CTA pairs when the output alone has too few tiles.  The FP32
+// partial sums sit after the call's other scratch, 256-byte aligned.
+static size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+static bool small_m_path(int layout, int64_t M, int64_t K);
+
+// The GEMM is launched while the chain's low-rank kernels still run (it waits
+// for their output only at its LoRA stage), so their CTAs take SMs first: the
+// split keeps the GEMM's pairs within the SMs they leave, or a second wave of
+// pairs would finish last.
+static int pairs_beside(int lowrank_ctas) {
+  const int p = device_pairs() - (lowrank_ctas + 1) / 2;
+  return p > 1 ? p : 1;
+}
+
+static int fwd_ksplit(int layout, int64_t M, int64_t N, int64_t K, int rank) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || M > (1 << 30) || small_m_path(layout, M, K)) return 1;
+  const int ld = rank > 0 ? lora_down_ctas((int)M, (int)K, rank) : 0;
+  return gemm_ksplit(((N + 255) / 256) * ((M + 255) / 256), K / 64, pairs_beside(ld));
+}
+
+// Counted for the low-rank pass over dY that precedes the GEMM when the caller
+// passes the forward's Ts (fl_bwd_ts, the autograd path; fl_bwd runs a second
+// one over X beside it).  Both entry points split alike, so their dX stay
+// bit-identical.
+static int bwd_ksplit(int layout, int64_t M, int64_t N, int64_t K, int rank) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % 64 != 0 || M > (1 << 30) || small_m_path(layout, M, K)) return 1;
+  const int ld = rank > 0 ? lora_down_ctas((int)M, (int)N, rank) : 0;
+  return gemm_ksplit(((K + 255) / 256) * ((M + 255) / 256), N / 64, pairs_beside(ld));
+}
+
+extern "C" {
+
+size_t fl_fwd_workspace_bytes_split(int64_t M, int64_t N, int64_t K, int rank) {
+  const size_t base = fl_fwd_workspace_bytes(M, K, rank);
+  const int ks = fwd_ksplit(kLayoutG128, M, N, K, rank);
+  return ks > 1 ? align256(base) + static_cast<size_t>(ks) * M * N * sizeof(float) : base;
+}
+
+size_t fl_bwd_workspace_bytes_split(int64_t M, int64_t N, int64_t K, int rank) {
+  const size_t base = fl_bwd_workspace_bytes(M, N, K, rank);
+  const int ks = bwd_ksplit(kLayoutG128, M, N, K, rank);
+  return ks > 1 ? align256(base) + static_cast<size_t>(ks) * M * K * sizeof(float) : base;
+}
+
 static int check_common(const char* who, int64_t M, int64_t N, int64_t K, int rank, const void* payload,
                         const float* scales, const float* lut16) {
   if (M <= 0 || N <= 0 || K <= 0) return set_error(FL_ERR_ARG, "%s: dims must be positive", who);
@@ -185,8 +233,19 @@ static int fwd_impl(const char* who, int layout, const uint16_t* X, int64_t M, i
   }
   // Chain prepass -> lora_down -> GEMM: each waits for the previous grid only
   // before it reads that grid's output (the GEMM: before its LoRA stage).
+  // Few output tiles: also split the reduction when the caller's workspace
+  // has room for the partial sums (fl_fwd_workspace_bytes_split).
+  int ks = fwd_ksplit(layout, M, N, K, rank);
+  float* part = nullptr;
+  if (ks > 1) {
+    const size_t off = align256(fl_fwd_workspace_bytes(M, K, rank));
+    if (workspace && aligned16(workspace) && workspace_bytes >= off + static_cast<size_t>(ks) * M * N * sizeof(float))
+      part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off);
+    else
+      ks = 1;
+  }
   return launch_fwd_gemm(X, workspace, payload, scales, lut16, B, rank, Y, (int)M, (int)N, (int)K, status, st,
-                         nullptr, nullptr, 1, 0, layout, /*pdl=*/true);
+                         nullptr, nullptr, 1, 0, layout, /*pdl=*/true, part, ks);
 }
 
 static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint16_t* X, int64_t M, int64_t N,
@@ -238,7 +297,8 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
   // [-> lora_grad(dB) above rank 16].  Without it: prepass(B) -> lora_down(Us) ->
   // prepass(A) -> lora_down(Ts) -> backward GEMM -> lora_grad(dA) ->
   // lora_grad(dB) (computing Ts first so that one pass could also sum dB
-  // serialises the two low-rank passes, which measured slower).  Each kernel
+  // serialises the two low-rank passes, which measured slower).  A split of
+  // the GEMM's reduction adds its reduce kernel right after the GEMM.  Each kernel
   // waits for the previous grid before reading what the chain produced; the
   // gradient kernels start once the GEMM has seen Us and Ts complete and fill
   // the SMs its last tiles leave idle.
@@ -263,8 +323,20 @@ static int bwd_impl(const char* who, int layout, const uint16_t* dY, const uint1
                                /*pdl=*/true)))
       return rc;
   }
+  // Few dX tiles: also split the reduction over N when the workspace has room
+  // (fl_bwd_workspace_bytes_split); the split reduce then follows the GEMM in
+  // the chain, and releases the gradient kernels at once.
+  int ks = bwd_ksplit(layout, M, N, K, rank);
+  float* part = nullptr;
+  if (ks > 1) {
+    const size_t off = align256(fl_bwd_workspace_bytes(M, N, K, rank));
+    if (workspace && aligned16(workspace) && workspace_bytes >= off + static_cast<size_t>(ks) * M * K * sizeof(float))
+      part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + off);
+    else
+      ks = 1;
+  }
   if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, (int)M, (int)N, (int)K, status, st,
-                            nullptr, nullptr, 1, 0, layout, /*pdl=*/true)))
+                            nullptr, nullptr, 1, 0, layout, /*pdl=*/true, part, ks)))
     return rc;
   if (rank > 0) {
     // dA[j, k] = sum_m Us[m, j] X[m, k]

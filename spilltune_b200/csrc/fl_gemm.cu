@@ -82,6 +82,10 @@ struct GemmArgs {
   // over expert-sorted token rows, its length on the device; null for one weight.
   const int4* tiles;
   const int* tile_count;
+  // Dense launches with a split reduction: ksplit > 1 slices of K / ksplit,
+  // FP32 sums to part[kpart][M][N] (Y is then formed by the split reduce).
+  float* part;
+  int ksplit;
 };
 
 struct __align__(16) GemmBarriers {
@@ -106,7 +110,7 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 // kGroupM token tiles x several weight tiles, so an activation tile is
 // requested by a handful of pairs at once instead of by every SM.
 struct Tile {
-  int expert, m0, m_end, w_tile;
+  int expert, m0, m_end, w_tile, kpart;
 };
 __device__ __forceinline__ Tile tile_at(const GemmArgs& args, int t, int num_w, int num_m) {
   Tile r;
@@ -116,7 +120,11 @@ __device__ __forceinline__ Tile tile_at(const GemmArgs& args, int t, int num_w, 
     r.m0 = v.y;
     r.m_end = v.z;
     r.w_tile = v.w;
+    r.kpart = 0;
   } else {
+    // The slices of one output tile are consecutive tiles (they run together).
+    r.kpart = t % args.ksplit;
+    t /= args.ksplit;
     const int band = t / (kGroupM * num_w);
     const int first_m = band * kGroupM;
     const int rows_in_band = min(kGroupM, num_m - first_m);
@@ -160,8 +168,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_pairs = gridDim.x >> 1;
   const int num_w = (L + 2 * kLanes - 1) / (2 * kLanes);
   const int num_m = (M + kTok - 1) / kTok;
-  const int n_tiles = args.tiles != nullptr ? *args.tile_count : num_w * num_m;
-  const int n_main = R / kStageK;
+  const int n_tiles = args.tiles != nullptr ? *args.tile_count : num_w * num_m * args.ksplit;
+  const int n_main = R / kStageK / args.ksplit;  // stages of one tile's reduction slice
   const bool has_lora = args.rank > 0;
   const int n_iter = n_main + (has_lora ? 1 : 0);
   volatile uint32_t* abort_word = &bars->abort_word;
@@ -212,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if (it < n_main) {
-            const int r0 = it * kStageK;
+            const int r0 = (tile.kpart * n_main + it) * kStageK;
             mbar_arrive_expect_tx(&bars->full[s], kXBytes + kQBytes);
             tma_load_2d(xs + s * kXBytes, &tm_act, r0, mh, &bars->full[s]);
             tma_load_2d(qs + s * kQBytes, &tm_code, r0 / 2, wrow0 + l0, &bars->full[s]);  // 128 rows x 32 B
@@ -307,14 +315,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && mbar_wait_warp(&bars->accum, tl & 1, abort_word, args.status, kStatusTimeoutAccum)) {
         tc_fence_after();
         // The kGroups warps of each lane quarter take the 32-column token
-        // chunks round robin: ys[token][row].
+        // chunks round robin: ys[token][row], or with a split reduction the
+        // FP32 sums straight to part[kpart][token][n] (a warp's 32 rows n are
+        // 128 contiguous bytes of each token row).
+        const int n = l0 + row;
 #pragma unroll 1
         for (int c = 32 * grp; c < kTok; c += 32 * kGroups) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem_base + lane_addr + c, v);
           tmem_wait_ld();
+          if (args.ksplit > 1) {
+            if (n < N) {
+              float* dst = args.part + (static_cast<size_t>(tile.kpart) * M + tile.m0 + c) * N + n;
+              const int live = min(32, M - tile.m0 - c);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) ys[(c + j) * kLanes + row] = __float2bfloat16_rn(__uint_as_float(v[j]));
+              for (int j = 0; j < 32; ++j)
+                if (j < live) dst[static_cast<size_t>(j) * N] = __uint_as_float(v[j]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ys[(c + j) * kLanes + row] = __float2bfloat16_rn(__uint_as_float(v[j]));
+          }
         }
         tc_fence_before();
         drained = true;
@@ -326,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
       fence_proxy_async_smem();
       named_barrier_sync(1, 32 * kEpiWarps);
-      if (!drained) return;
+      if (!drained || args.ksplit > 1) return;
       const int rows_here = min(tile.m0 + kTok, M) - tile.m0;
       const bool partial = tile.m_end < tile.m0 + rows_here;
       if (args.tma_store && !partial) {
@@ -377,7 +398,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (layout 1).  A stage pair is one group, or two blocks.
       constexpr bool kBlock64 = kLayout == kLayoutNf4Dq64;
       const int spr = kBlock64 ? 2 * groups_per_row : groups_per_row;
-      const float* srow = args.scales + static_cast<size_t>(wrow0 + (valid ? n : 0)) * spr;
+      // This tile's reduction slice: 128-groups [kpart * tile_groups, + tile_groups).
+      const int tile_groups = n_main / 2;
+      const float* srow = args.scales + static_cast<size_t>(wrow0 + (valid ? n : 0)) * spr +
+                          (kBlock64 ? 2 : 1) * tile.kpart * tile_groups;
+      const bool lora_here = tile.kpart == 0;  // a split sums the LoRA stage once
       // The groups take the stage pairs of the CTA pair's whole stage sequence in
       // turn (tile tl starts a new pair, number tl * pairs_per_tile), not afresh
       // per tile: consecutive stages of one group are then never more than
@@ -385,8 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // whose barrier is two phases behind (the parity wait would pass).
       const int first = (grp - (tl * pairs_per_tile) % kGroups + kGroups) % kGroups;
       const int pit0 = 2 * first;
-      float next_scale = (valid && first < groups_per_row) ? __ldg(srow + (kBlock64 ? 2 * first : first)) : 0.0f;
-      float next_scale2 = (kBlock64 && valid && first < groups_per_row) ? __ldg(srow + 2 * first + 1) : 0.0f;
+      float next_scale = (valid && first < tile_groups) ? __ldg(srow + (kBlock64 ? 2 * first : first)) : 0.0f;
+      float next_scale2 = (kBlock64 && valid && first < tile_groups) ? __ldg(srow + 2 * first + 1) : 0.0f;
       for (int pit = pit0; pit < n_iter || (pit == pit0 && tl > 0); pit += 2 * kGroups) {
         if (pit < n_iter && ok) {
           ProductTable table;
@@ -396,11 +421,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (kBlock64) {
               sc_a = next_scale;
               sc_b = next_scale2;
-              next_scale = (valid && g_next < groups_per_row) ? __ldg(srow + 2 * g_next) : 0.0f;
-              next_scale2 = (valid && g_next < groups_per_row) ? __ldg(srow + 2 * g_next + 1) : 0.0f;
+              next_scale = (valid && g_next < tile_groups) ? __ldg(srow + 2 * g_next) : 0.0f;
+              next_scale2 = (valid && g_next < tile_groups) ? __ldg(srow + 2 * g_next + 1) : 0.0f;
             } else {
               table = make_table(lut_s, next_scale);
-              next_scale = (valid && g_next < groups_per_row) ? __ldg(srow + g_next) : 0.0f;
+              next_scale = (valid && g_next < tile_groups) ? __ldg(srow + g_next) : 0.0f;
             }
           }
           for (int it = pit; it < pit + 2 && it < n_iter; ++it) {
@@ -439,8 +464,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 const int c0 = 2 * j, c1 = c0 + 1;
-                const float a = (valid && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c0) : 0.f;
-                const float b = (valid && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c1) : 0.f;
+                const float a = (valid && lora_here && c0 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c0) : 0.f;
+                const float b = (valid && lora_here && c1 < args.rank) ? __ldg(args.lora + static_cast<size_t>(wrow0 + n) * args.rank + c1) : 0.f;
                 v[j] = pack_bf16x2(a, b);
               }
             }
@@ -562,9 +587,11 @@ int resident_pairs(const void* kernel, int threads, int smem, int* pairs) {
 int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
                     const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles,
-                    int layout, bool pdl) {
+                    int layout, bool pdl, float* part, int ksplit) {
   if (layout != kLayoutG128 && layout != kLayoutNf4Dq64) return set_error(FL_ERR_ARG, "fwd gemm: unknown layout");
   if (layout != kLayoutG128 && tiles) return set_error(FL_ERR_UNSUPPORTED, "grouped launches use layout 0");
+  if (ksplit < 1 || (ksplit > 1 && (tiles || !part || (K / kStageK) % (2 * ksplit) != 0)))
+    return set_error(FL_ERR_ARG, "fwd gemm: invalid reduction split %d", ksplit);
   CUtensorMap tm_act, tm_low, tm_code;
   int rc = make_tensor_map_2d(&tm_act, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, static_cast<uint64_t>(K) * 2, 64,
                               kTokHalf, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -600,9 +627,12 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
   a.tma_store = tma_store ? 1 : 0;
   a.tiles = tiles;
   a.tile_count = tile_count;
-  // Persistent CTA pairs (each tile: 256 W rows x 256 tokens), no more than
-  // can be resident at once.
-  const int tiles_max = tiles ? max_tiles : ((N + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok);
+  a.part = part;
+  a.ksplit = ksplit;
+  // Persistent CTA pairs (each tile: 256 W rows x 256 tokens x one reduction
+  // slice), no more than can be resident at once.
+  const int tiles_max =
+      tiles ? max_tiles : ((N + 2 * kLanes - 1) / (2 * kLanes)) * ((M + kTok - 1) / kTok) * ksplit;
   int pairs = 0;
   const void* kfn = layout == kLayoutG128 ? reinterpret_cast<const void*>(&fl_tc_gemm_kernel<kLayoutG128>)
                                           : reinterpret_cast<const void*>(&fl_tc_gemm_kernel<kLayoutNf4Dq64>);
@@ -627,6 +657,7 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
                        ? cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<kLayoutG128>, tm_act, tm_low, tm_code, tm_out, a)
                        : cudaLaunchKernelEx(&cfg, fl_tc_gemm_kernel<kLayoutNf4Dq64>, tm_act, tm_low, tm_code, tm_out, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "fwd gemm launch: %s", cudaGetErrorString(le));
+  if (ksplit > 1) return launch_split_reduce(part, ksplit, static_cast<int64_t>(M) * N, y, stream);
   return FL_OK;
 }
 

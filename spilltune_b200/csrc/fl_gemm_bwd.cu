@@ -76,6 +76,10 @@ struct Args {
   int M, N, K, rank;
   const int4* tiles;    // MoE: {expert, first row, end row, column tile}; null for one weight
   const int* tile_count;
+  // Dense launches with a split reduction: ksplit > 1 slices of N / ksplit,
+  // FP32 sums to part[kpart][M][K] (dX is then formed by the split reduce).
+  float* part;
+  int ksplit;
 };
 
 // Byte offset of 16-byte chunk j (k = 8j..8j+7 within the CTA's 64-k half
@@ -85,7 +89,7 @@ __device__ __forceinline__ uint32_t b_offset(int r, int khalf, int j) {
 }
 
 struct Tile {
-  int expert, m0, m_end, k_tile;
+  int expert, m0, m_end, k_tile, kpart;
 };
 // Tile t: grouped launches read the list; dense ones walk bands of kGroupM
 // token tiles x all column tiles, so a band's dY slab is read by pairs that
@@ -98,7 +102,11 @@ __device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int 
     r.m0 = v.y;
     r.m_end = v.z;
     r.k_tile = v.w;
+    r.kpart = 0;
   } else {
+    // The slices of one output tile are consecutive tiles (they run together).
+    r.kpart = t % args.ksplit;
+    t /= args.ksplit;
     const int band = t / (kGroupM * num_k);
     const int first_m = band * kGroupM;
     const int rows_in_band = min(kGroupM, num_m - first_m);
@@ -136,8 +144,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_pairs = gridDim.x >> 1;
   const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
   const int num_m = (M + 2 * kTokHalf - 1) / (2 * kTokHalf);
-  const int n_tiles = args.tiles != nullptr ? *args.tile_count : num_k * num_m;
-  const int n_main = N / kStageN;
+  const int n_tiles = args.tiles != nullptr ? *args.tile_count : num_k * num_m * args.ksplit;
+  const int n_main = N / kStageN / args.ksplit;  // stages of one tile's reduction slice
   const bool has_lora = args.rank > 0;
   const int n_iter = n_main + (has_lora ? 1 : 0);
   volatile uint32_t* abort_word = &bars->abort_word;
@@ -188,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if (it < n_main) {
-            const int n0 = it * kStageN;
+            const int n0 = (tile.kpart * n_main + it) * kStageN;
             mbar_arrive_expect_tx(&bars->full[s], kABytes + kQBytes);
             tma_load_2d(as + s * kABytes, &tm_dy, n0, mh, &bars->full[s]);
             tma_load_2d(qs + s * kQBytes, &tm_code, kb / 2, wrow0 + n0, &bars->full[s]);
@@ -284,7 +292,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x32(tmem_base + b * kAccCols + lane_addr + c, acc);
           tmem_wait_ld();
           const int kcol = k0 + c;
-          if (m < tile.m_end && kcol < K) {
+          if (args.ksplit > 1) {
+            // FP32 sums of this reduction slice: 128 contiguous bytes per thread.
+            if (m < tile.m_end && kcol < K) {
+              float4* dst = reinterpret_cast<float4*>(args.part + (static_cast<size_t>(tile.kpart) * M + m) * K + kcol);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                dst[j] = make_float4(__uint_as_float(acc[4 * j]), __uint_as_float(acc[4 * j + 1]),
+                                     __uint_as_float(acc[4 * j + 2]), __uint_as_float(acc[4 * j + 3]));
+            }
+          } else if (m < tile.m_end && kcol < K) {
             uint4* dst = reinterpret_cast<uint4*>(args.out + static_cast<size_t>(m) * K + kcol);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -317,6 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int wrow0 = tile.expert * N;
       const float* alora = args.alora + static_cast<size_t>(tile.expert) * args.rank * K;
       const bool tile_valid = kb < K;
+      const int nbase = tile.kpart * n_main * kStageN;  // first reduction row of the tile's slice
       // Layout 0: the CTA's 128 columns share one 128-group scale; layout 1:
       // each thread's 64 columns are one 64-block.
       constexpr bool kBlock64 = kLayout == kLayoutNf4Dq64;
@@ -327,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // rotation of the groups ahead, so the gather has landed when used.
       auto load_scale = [&](int it) {
         return (tile_valid && it < n_main)
-                   ? __ldg(args.scales + static_cast<size_t>(wrow0 + it * kStageN + r) * spr + gsc)
+                   ? __ldg(args.scales + static_cast<size_t>(wrow0 + nbase + it * kStageN + r) * spr + gsc)
                    : 0.0f;
       };
       // The groups take the stage pairs of the CTA pair's whole stage sequence
@@ -380,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
                 break;
               }
-              const bool live = tile_valid && r < args.rank;
+              const bool live = tile_valid && tile.kpart == 0 && r < args.rank;  // a split sums it once
               const float* src = alora + static_cast<size_t>(live ? r : 0) * K + kb + 64 * khalf;
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
@@ -435,12 +453,14 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles,
-                    int layout, bool pdl) {
+                    int layout, bool pdl, float* part, int ksplit) {
   using namespace bwd;
   if (layout != kLayoutG128 && layout != kLayoutNf4Dq64) return set_error(FL_ERR_ARG, "bwd gemm: unknown layout");
   if (layout != kLayoutG128 && tiles) return set_error(FL_ERR_UNSUPPORTED, "grouped launches use layout 0");
   if ((K * 2) % 16 != 0 || N % kStageN != 0 || K % 128 != 0)
     return set_error(FL_ERR_ARG, "bwd gemm: needs N %% 64 == 0 and K %% 128 == 0");
+  if (ksplit < 1 || (ksplit > 1 && (tiles || !part || (N / kStageN) % ksplit != 0)))
+    return set_error(FL_ERR_ARG, "bwd gemm: invalid reduction split %d", ksplit);
   CUtensorMap tm_dy, tm_us, tm_code;
   int rc = make_tensor_map_2d(&tm_dy, dy, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, static_cast<uint64_t>(N) * 2, 64,
                               kTokHalf, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -467,8 +487,11 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   a.rank = rank;
   a.tiles = tiles;
   a.tile_count = tile_count;
+  a.part = part;
+  a.ksplit = ksplit;
   const int tiles_max = tiles ? max_tiles
-                              : ((K + 2 * kColHalf - 1) / (2 * kColHalf)) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf));
+                              : ((K + 2 * kColHalf - 1) / (2 * kColHalf)) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf)) *
+                                    ksplit;
   int pairs = 0;
   const void* kfn = layout == kLayoutG128 ? reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutG128>)
                                           : reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutNf4Dq64>);
@@ -493,6 +516,7 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
                        ? cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutG128>, tm_dy, tm_us, tm_code, a)
                        : cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutNf4Dq64>, tm_dy, tm_us, tm_code, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "bwd gemm launch: %s", cudaGetErrorString(le));
+  if (ksplit > 1) return launch_split_reduce(part, ksplit, static_cast<int64_t>(M) * K, dx, stream);
   return FL_OK;
 }
 

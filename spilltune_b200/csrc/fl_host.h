@@ -24,10 +24,29 @@ uint32_t* status_word(int device);  // device status word of the calling device
 // Grouped (MoE) form: `tiles`/`tile_count` from launch_moe_plan, the weight a
 // stacked [experts, N, K] record, blora [experts, N, rank]; grid sized for
 // `max_tiles`.  tiles == nullptr: one weight, experts = 1.
+// Split of the reduction (dense launches only): with ksplit > 1 tile t covers
+// reduction stages [t.kpart * S, (t.kpart + 1) * S), S = K / 64 / ksplit, and
+// writes its FP32 sums to part[kpart][M][N] instead of Y (the LoRA stage is
+// summed by kpart 0 only); launch_split_reduce then forms Y.
 int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const float* scales, const float* lut,
                     const float* blora, int rank, void* y, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
-                    int experts = 1, int max_tiles = 0, int layout = 0, bool pdl = false);
+                    int experts = 1, int max_tiles = 0, int layout = 0, bool pdl = false, float* part = nullptr,
+                    int ksplit = 1);
+
+// Reduction split of a dense tile GEMM with `tiles` output tiles of `stages`
+// 64-wide reduction stages, `pairs` CTA pairs free for it: 1, or the largest
+// power of two (<= 16) for which tiles * split <= pairs and every split keeps an
+// even number, at least 8, of stages; no split below 32 stages (the reduce
+// launch would cost more than the shorter tiles save).  Output tiles that
+// would leave most pairs idle (few tokens, few output columns) then use them all.
+int gemm_ksplit(int64_t tiles, int64_t stages, int pairs);
+int device_pairs();  // SMs / 2 of the current device (74 when it cannot be queried)
+// out[i] = bf16(part[0][i] + part[1][i] + ... + part[split-1][i]), i < plane,
+// summed in that order (fl_split.cu).  Launched as a programmatic dependent of
+// the GEMM that wrote `part`: it releases its own dependents at once and waits
+// for the previous grid before reading.
+int launch_split_reduce(const float* part, int split, int64_t plane, void* out, cudaStream_t stream);
 
 // 2-CTA clusters of `kernel` that can be resident at once on the current
 // device (also raises the kernel's dynamic shared-memory limit to `smem`).
@@ -45,10 +64,14 @@ int moe_max_tiles(int total_rows, int experts, int rows, int col_tiles);
 // dX[M,K] = dY . W + Us . Alora (fl_gemm_bwd.cu).  pdl: Us comes from the chain
 // (the previous launch completes after it); dependents are released only once
 // Us and Ts are complete (the gradient kernels read them without waiting).
+// ksplit > 1 (dense only): tile t sums reduction rows n in [t.kpart * S * 64,
+// (t.kpart + 1) * S * 64), S = N / 64 / ksplit, into part[kpart][M][K] (FP32;
+// the LoRA stage in kpart 0 only), for launch_split_reduce.
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
-                    int experts = 1, int max_tiles = 0, int layout = 0, bool pdl = false);
+                    int experts = 1, int max_tiles = 0, int layout = 0, bool pdl = false, float* part = nullptr,
+                    int ksplit = 1);
 
 int launch_dequant(const uint8_t* payload, const float* scales, const float* lut, int64_t numel, void* out,
                    cudaStream_t stream, int layout = 0);
@@ -91,6 +114,10 @@ int launch_lora_parts2(const void* P0, int R0, const float* q0, int64_t q0_sj, i
 // 128-wide pieces summed into one partial (R1 > 0: the common size for both).
 int lora_parts_per_cluster(int R0, int R1 = 0);
 int lora_nq(int rank);                           // rank padded to 16, 32 or 64
+// CTAs of the tiled launch_lora_down grid for M rows (one per SM at most);
+// 0 for the small-M form.  A tile GEMM launched as its programmatic dependent
+// shares the GPU with these.
+int lora_down_ctas(int M, int R, int rank);
 size_t lora_factor_bytes(int64_t R, int rank);   // converted-factor scratch for a reduction of R
 
 // out(p, j) (+)= sum_m P[m, p] * Q[m, j]  (P bf16 [M, Pdim], Q bf16 [M, 64]),
@@ -98,8 +125,9 @@ size_t lora_factor_bytes(int64_t R, int rank);   // converted-factor scratch for
 // Grouped (MoE) form: token slices {expert, first row, end row, 0} over
 // expert-sorted rows; slice t accumulates into out + tiles[t].x * out_expert_stride
 // (out then holds all experts: `out_total` floats are cleared when !accumulate).
-// pdl: launched after the backward GEMM or another lora_grad of the chain (P and
-// Q complete; a chain clears `out` before its first launch).
+// pdl: launched after the backward GEMM (or the split reduce that follows it)
+// or another lora_grad of the chain (P and Q complete; a chain clears `out`
+// before its first launch).
 int launch_lora_grad(const void* P, int M, int Pdim, const void* Q, int rank, float* out, int64_t o_sp,
                      int64_t o_sj, int accumulate, cudaStream_t stream, const int4* tiles = nullptr,
                      const int* tile_count = nullptr, int max_tiles = 0, int64_t out_expert_stride = 0,

@@ -411,6 +411,35 @@ __global__ void __launch_bounds__(kThreads)
   if (split > 1) cluster_sync();
 }
 
+// CTAs of lora_down_kernel<NQ, kGrad> resident on the current device at once
+// (sets the kernel's shared-memory limit once per device); 0 on failure.
+template <int NQ, bool kGrad>
+static int resident_slots() {
+  constexpr int kSmem = Cfg<NQ>::kSmem;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  static int slots[64] = {0};
+  if (!slots[dev]) {
+    int sms = 0, per_sm = 0;
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&lora_down_kernel<NQ, kGrad>),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lora_down_kernel<NQ, kGrad>, kThreads, kSmem);
+    if (e != cudaSuccess || per_sm < 1) return 0;
+    slots[dev] = sms * per_sm;
+  }
+  return slots[dev];
+}
+
+// Split the reduction across a cluster while the grid still fits in one
+// wave of resident CTAs and every slice keeps at least two 64-wide units.
+static int cluster_split(int blocks, int R, int slots) {
+  int split = 1;
+  while (split < kMaxSplit && blocks * split * 2 <= slots && (R / 64) >= 4 * split) split *= 2;
+  return split;
+}
+
 template <int NQ, bool kGrad = false>
 static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64_t qc_es, int rank, float s,
                      void* out, cudaStream_t stream, const int4* tiles, const int* tile_count, int max_tiles,
@@ -421,22 +450,9 @@ static int launch_nq(const void* P, int M, int R, const __nv_bfloat16* qc, int64
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return set_error(FL_ERR_CUDA, "lora_down: no current device");
-  // Per device: the kernel's shared-memory limit and how many CTAs fit on the GPU at once.
-  static int slots[64] = {0};
-  if (!slots[dev]) {
-    int sms = 0, per_sm = 0;
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&lora_down_kernel<NQ, kGrad>),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess)
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lora_down_kernel<NQ, kGrad>, kThreads, kSmem);
-    if (e != cudaSuccess || per_sm < 1) return set_error(FL_ERR_CUDA, "lora_down: occupancy query failed");
-    slots[dev] = sms * per_sm;
-  }
-  // Split the reduction across a cluster while the grid still fits in one
-  // wave of resident CTAs and every slice keeps at least two 64-wide units.
-  int split = 1;
-  while (split < kMaxSplit && blocks * split * 2 <= slots[dev] && (R / 64) >= 4 * split) split *= 2;
+  const int slots = resident_slots<NQ, kGrad>();
+  if (slots < 1) return set_error(FL_ERR_CUDA, "lora_down: occupancy query failed");
+  const int split = cluster_split(blocks, R, slots);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(blocks * split);
   cfg.blockDim = dim3(kThreads);
@@ -760,6 +776,16 @@ int launch_lora_down(const void* P, int M, int R, const float* q, int64_t q_sj, 
   if (nq == 16) return ld::launch_nq<16>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
   if (nq == 32) return ld::launch_nq<32>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
   return ld::launch_nq<64>(P, M, R, qc, qc_es, rank, s, out64, stream, tiles, tile_count, max_tiles);
+}
+
+int lora_down_ctas(int M, int R, int rank) {
+  using namespace ld;
+  if (M <= lds::kMaxRows || rank < 1 || rank > 64 || R % 64 != 0) return 0;
+  const int blocks = (M + kRows - 1) / kRows;
+  const int nq = lora_nq(rank);
+  const int slots = nq == 16 ? resident_slots<16, false>() : nq == 32 ? resident_slots<32, false>()
+                                                                       : resident_slots<64, false>();
+  return blocks * cluster_split(blocks, R, slots > 0 ? slots : 148);
 }
 
 }  // namespace fl

@@ -73,9 +73,15 @@ def keeps_ts(layout, M, K, rank):
     return rank > 0 and M > 0 and not (layout == 0 and M <= 16 and K % 512 == 0)
 
 
-def launch_fwd(layout, x2, payload, scales, lut, N, A=None, B=None, scale=0.0):
+def launch_fwd(layout, x2, payload, scales, lut, N, A=None, B=None, scale=0.0, split_reduction=True):
     """One forward call on raw record parts: x2 bf16 [M, K] contiguous ->
-    (Y bf16 [M, N], workspace uint8 or None).  A/B fp32 [rank, K] / [N, rank]."""
+    (Y bf16 [M, N], workspace uint8 or None).  A/B fp32 [rank, K] / [N, rank].
+
+    split_reduction: give the call room to split its reduction when it has few
+    output tiles (fl_fwd_workspace_bytes_split); False keeps one pass per
+    output tile (the summation order of the grouped kernels).  When the split
+    was possible the returned workspace is a copy of just its Ts rows, so a
+    saved Ts does not hold the partial-sum scratch."""
     M, K = x2.shape
     rank = 0 if A is None else A.shape[0]
     _need_cuda(x2, payload, A, B)
@@ -86,11 +92,15 @@ def launch_fwd(layout, x2, payload, scales, lut, N, A=None, B=None, scale=0.0):
         A = A.detach().contiguous()
         B = B.detach().contiguous()
     y = torch.empty((M, N), dtype=torch.bfloat16, device=x2.device)
-    ws_bytes = _lib.load().fl_fwd_workspace_bytes(M, K, rank)
+    lib = _lib.load()
+    base = lib.fl_fwd_workspace_bytes(M, K, rank)
+    ws_bytes = lib.fl_fwd_workspace_bytes_split(M, N, K, rank) if split_reduction and M else base
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device) if ws_bytes else None
     if M:
         _lib.call(_FWD_ENTRY[layout], _ptr(x2), M, K, _ptr(payload), _ptr(scales), _ptr(lut), N, _ptr(A), _ptr(B),
                   rank, float(scale), _ptr(y), _ptr(ws), ws_bytes, _stream())
+    if ws_bytes > base and keeps_ts(layout, M, K, rank):
+        ws = ws[:M * 128].clone()
     return y, ws
 
 
@@ -100,8 +110,9 @@ def ts_view(ws, M):
 
 
 def launch_bwd(layout, dy2, x2, payload, scales, lut, K, A=None, B=None, scale=0.0, dA=None, dB=None,
-               accumulate=False, ts=None):
-    """One backward call on raw record parts -> (dX bf16 [M, K], dA, dB)."""
+               accumulate=False, ts=None, split_reduction=True):
+    """One backward call on raw record parts -> (dX bf16 [M, K], dA, dB).
+    split_reduction as for launch_fwd (dX's reduction over N)."""
     M, N = dy2.shape
     rank = 0 if A is None else A.shape[0]
     _need_cuda(dy2, x2, payload, A, B)
@@ -120,7 +131,9 @@ def launch_bwd(layout, dy2, x2, payload, scales, lut, K, A=None, B=None, scale=0
         if dB is None:
             dB = torch.empty((N, rank), dtype=torch.float32, device=dy2.device)
             accumulate = False
-    ws_bytes = _lib.load().fl_bwd_workspace_bytes(M, N, K, rank)
+    lib = _lib.load()
+    ws_bytes = (lib.fl_bwd_workspace_bytes_split if split_reduction and M else lib.fl_bwd_workspace_bytes)(
+        M, N, K, rank)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dy2.device) if ws_bytes else None
     if ts is not None and rank:
         if ts.dtype != torch.bfloat16 or tuple(ts.shape) != (M, 64) or not ts.is_contiguous():
@@ -141,7 +154,7 @@ def launch_bwd(layout, dy2, x2, payload, scales, lut, K, A=None, B=None, scale=0
     return dx, dA, dB
 
 
-def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0, return_ts=False):
+def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0, return_ts=False, split_reduction=True):
     """Y = x . W^T + scale * (x . A^T) . B^T  (bf16 out; plain frozen linear if A is None).
 
     return_ts: also return Ts = bf16(scale * x . A^T) ([tokens, 64] bf16, zero past
@@ -149,11 +162,13 @@ def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0, return_ts=False):
     intermediate the reference's autograd keeps from the forward for grad_B
     (finetune/lora.py:219-220).  None when rank == 0 or when the decode-step
     kernels take the call (<= 16 tokens, K % 512 == 0: they form Ts themselves).
+    split_reduction=False: no split of the reduction for few output tiles (see
+    launch_fwd; the grouped kernels' summation order).
     """
     N, K = _matrix_shape(weight)
     x2 = _flat(x, K)
     rank = 0 if A is None else A.shape[0]
-    y, ws = launch_fwd(0, x2, weight.payload, weight.scales, weight.lut, N, A, B, scale)
+    y, ws = launch_fwd(0, x2, weight.payload, weight.scales, weight.lut, N, A, B, scale, split_reduction)
     y = y.view(*x.shape[:-1], N)
     if not return_ts:
         return y
@@ -161,17 +176,19 @@ def fwd(x, weight: PackedWeight, A=None, B=None, scale=0.0, return_ts=False):
     return y, (ts_view(ws, M) if keeps_ts(0, M, K, rank) else None)
 
 
-def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False, ts=None):
+def bwd(dy, x, weight: PackedWeight, A=None, B=None, scale=0.0, dA=None, dB=None, accumulate=False, ts=None,
+        split_reduction=True):
     """Returns (dX, dA, dB) of fwd(); dA/dB are fp32 (accumulated into when given and accumulate).
 
     ts: the Ts that ``fwd(..., return_ts=True)`` returned for the same x, A and
-    scale; X . A^T is then not recomputed (results identical)."""
+    scale; X . A^T is then not recomputed (results identical).
+    split_reduction: as for fwd (dX's reduction over N)."""
     N, K = _matrix_shape(weight)
     dy2 = _flat(dy, N)
     rank = 0 if A is None else A.shape[0]
     x2 = _flat(x, K) if rank else None
     dx, dA, dB = launch_bwd(0, dy2, x2, weight.payload, weight.scales, weight.lut, K, A, B, scale, dA, dB,
-                            accumulate, ts)
+                            accumulate, ts, split_reduction)
     return dx.view(*dy.shape[:-1], K), dA, dB
 
 

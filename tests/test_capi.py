@@ -53,6 +53,27 @@ def test_version_and_workspace_sizes(lib):
     assert lib.fl_bwd_workspace_bytes(100, 384, 256, 8) == 100 * 256 + 4 * 16 * (384 + 256) + mask(384) + mask(256)
 
 
+def test_split_workspace_sizes(lib):
+    """Room for the FP32 partial sums only when the output has too few 256 x 256 tiles for
+    the 74 CTA pairs of a B200 (the count the query assumes without a device, too)."""
+    a256 = lambda b: (b + 255) // 256 * 256
+    fwd, fwd_s = lib.fl_fwd_workspace_bytes, lib.fl_fwd_workspace_bytes_split
+    bwd, bwd_s = lib.fl_bwd_workspace_bytes, lib.fl_bwd_workspace_bytes_split
+    # Enough tiles, or the decode-step kernels: no split.
+    assert fwd_s(8192, 14336, 4096, 16) == fwd(8192, 4096, 16)
+    assert fwd_s(16, 4096, 4096, 16) == fwd(16, 4096, 16)
+    assert bwd_s(8192, 14336, 4096, 16) == bwd(8192, 14336, 4096, 16)
+    # 256 tokens of a 4096-wide projection: 16 tiles x 4 slices of 16 stages.
+    assert fwd_s(256, 4096, 4096, 16) == a256(fwd(256, 4096, 16)) + 4 * 256 * 4096 * 4
+    assert fwd_s(256, 4096, 14336, 0) == 4 * 256 * 4096 * 4
+    # 4 tiles: 8 slices (each keeps 8 stages of 64).
+    assert fwd_s(256, 1024, 4096, 0) == 8 * 256 * 1024 * 4
+    # Backward: dX [M, K] tiles, reduction over N.
+    assert bwd_s(256, 14336, 4096, 16) == a256(bwd(256, 14336, 4096, 16)) + 4 * 256 * 4096 * 4
+    assert bwd_s(2048, 1024, 4096, 0) == bwd(2048, 1024, 4096, 0)  # 16 x 8 = 128 dX tiles: no split
+    assert fwd_s(2048, 1024, 4096, 0) == 2 * 2048 * 1024 * 4  # 4 x 8 = 32 Y tiles: 2 slices
+
+
 def _fwd(lib, M=16, K=256, N=128, rank=0, ptr=1024, ws=0):
     P = ptr
     return lib.fl_fwd(P, M, K, P, P, P, N, P if rank else None, P if rank else None, rank, 2.0, P,

@@ -93,7 +93,9 @@ def test_grouped_fwd(cuda_lib, codec_name, lengths, N, K, rank):
         a, b = seg[e], seg[e + 1]
         if a == b:
             continue
-        dense = ops.fwd(xc, _expert_view(pwc, e), None if A is None else Ac[e], None if B is None else Bc[e], s)
+        # Without a split of the reduction: the grouped kernel sums each output tile in one pass too.
+        dense = ops.fwd(xc, _expert_view(pwc, e), None if A is None else Ac[e], None if B is None else Bc[e], s,
+                        split_reduction=False)
         assert torch.equal(y[a:b], dense[a:b]), e
     ref = om.grouped_linear_fp32(x, seg, _decode_cpu(pw), A, B, s)
     err = ol.rel_l2(y.cpu(), ref)
@@ -117,7 +119,7 @@ def test_grouped_bwd(cuda_lib, codec_name, lengths, N, K, rank):
             if a == b:
                 assert torch.count_nonzero(dA[e]) == 0 and torch.count_nonzero(dB[e]) == 0
                 continue
-            ddx, _, _ = ops.bwd(dyc, xc, pe, Ac[e], Bc[e], s)
+            ddx, _, _ = ops.bwd(dyc, xc, pe, Ac[e], Bc[e], s, split_reduction=False)
             _, edA, edB = ops.bwd(dyc[a:b].contiguous(), xc[a:b].contiguous(), pe, Ac[e], Bc[e], s)
             # A segment of <= 16 rows takes the decode-step backward when run alone, whose
             # Us / Ts are exact FP32 sums (the grouped path's low-rank kernel carries ~16
@@ -128,7 +130,7 @@ def test_grouped_bwd(cuda_lib, codec_name, lengths, N, K, rank):
         elif a == b:
             continue
         else:
-            ddx, _, _ = ops.bwd(dyc, None, pe)
+            ddx, _, _ = ops.bwd(dyc, None, pe, split_reduction=False)
         assert torch.equal(dx[a:b], ddx[a:b]), e
     rdx, rdA, rdB = om.grouped_linear_grads_fp32(dy, x, seg, _decode_cpu(pw), A, B, s)
     errs = [ol.rel_l2(dx.cpu(), rdx)]

@@ -230,9 +230,52 @@ def test_full_size_sampled_rows(cuda_lib, N, K):
     rdA = s * (gf @ B).t() @ xf
     rdB = s * gf.t() @ (xf @ A.t())
     assert ol.rel_l2(dA.cpu(), rdA) <= TIGHT and ol.rel_l2(dB.cpu(), rdB) <= TIGHT
-    # Row independence: a 256-token slice through the kernel equals the same rows of the full call.
-    y_slice = ops.fwd(xc[256:512].contiguous(), pwc, Ac, Bc, s)
-    assert torch.equal(y_slice, y[256:512])
+    # Row independence: a 256-token slice through the kernel equals the same rows of the full
+    # call (both without a split of the reduction, whose slice count depends on the token count).
+    y1 = ops.fwd(xc, pwc, Ac, Bc, s, split_reduction=False)
+    y_slice = ops.fwd(xc[256:512].contiguous(), pwc, Ac, Bc, s, split_reduction=False)
+    assert torch.equal(y_slice, y1[256:512])
+    # A split changes only the order of the FP32 sums.
+    assert ol.rel_l2(y.cpu(), y1.cpu()) <= 1e-3
+
+
+# Calls whose output has too few 256 x 256 tiles for the GPU's CTA pairs: the
+# forward splits its reduction over K, the backward dX's over N (slices at rank
+# 16 on a B200: fwd 4 / bwd 4; fwd 8; fwd 4; bwd 4; fwd 4 with ragged token and
+# output tiles; fwd 4 beside a wider low-rank grid).
+SPLIT_CASES = [(256, 4096, 4096), (256, 1024, 4096), (256, 4096, 14336), (256, 14336, 4096), (300, 384, 2048),
+               (512, 1024, 4096)]
+
+
+@pytest.mark.parametrize("M,N,K", SPLIT_CASES)
+def test_split_reduction_parity(cuda_lib, M, N, K):
+    """Split calls against the FP32 shadow on sampled rows (forward, and the backward from
+    the forward's Ts), and against the same call without a split: only the order of the
+    FP32 sums differs, so the bf16 outputs agree to within a rounding step."""
+    from spilltune_b200 import ops
+    lib = cuda_lib
+    rank, s = 16, 2.0
+    assert (lib.fl_fwd_workspace_bytes_split(M, N, K, rank) > lib.fl_fwd_workspace_bytes(M, K, rank)
+            or lib.fl_bwd_workspace_bytes_split(M, N, K, rank) > lib.fl_bwd_workspace_bytes(M, N, K, rank))
+    pw, x, A, B, dy = _problem(M, N, K, rank, "nf4-g128", seed=M + N + 3 * K, fstd=0.01)
+    pwc, xc, Ac, Bc, dyc = pw.to("cuda"), x.cuda(), A.cuda(), B.cuda(), dy.cuda()
+    y, ts = ops.fwd(xc, pwc, Ac, Bc, s, return_ts=True)
+    dx, dA, dB = ops.bwd(dyc, xc, pwc, Ac, Bc, s, ts=ts)
+    y1 = ops.fwd(xc, pwc, Ac, Bc, s, split_reduction=False)
+    dx1, dA1, dB1 = ops.bwd(dyc, xc, pwc, Ac, Bc, s, split_reduction=False)
+    torch.cuda.synchronize()
+    W = _decode_cpu(pw)
+    rows = torch.tensor(sorted({0, 1, 127, 128, 255, M // 2, M - 1}))
+    assert ol.rel_l2(y[rows.cuda()].cpu(), ol.lora_forward_fp32(x[rows], W, A, B, s)) <= TIGHT
+    ref_dx, _, _ = ol.lora_backward_fp32(x[rows], W, A, B, s, dy[rows])
+    assert ol.rel_l2(dx[rows.cuda()].cpu(), ref_dx) <= TIGHT
+    xf, gf = x.float(), dy.float()
+    assert ol.rel_l2(dA.cpu(), s * (gf @ B).t() @ xf) <= TIGHT
+    assert ol.rel_l2(dB.cpu(), s * gf.t() @ (xf @ A.t())) <= TIGHT
+    assert ol.rel_l2(y.cpu(), y1.cpu()) <= 1e-3 and ol.rel_l2(dx.cpu(), dx1.cpu()) <= 1e-3
+    assert ol.rel_l2(dA.cpu(), dA1.cpu()) < 1e-5 and ol.rel_l2(dB.cpu(), dB1.cpu()) < 1e-5
+    # Same inputs, same split: the same bits (fixed order of the partial sums).
+    assert torch.equal(ops.fwd(xc, pwc, Ac, Bc, s), y)
 
 
 def test_no_kernel_reported_timeouts(cuda_lib):

@@ -103,7 +103,8 @@ def test_prologue_and_dequant_bit_exact(cuda_lib, N, K):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("M,N,K,rank", [(256, 256, 256, 0), (300, 384, 512, 16), (16, 1024, 1024, 8),
-                                        (3, 640, 384, 4), (2048, 4096, 4096, 16)])
+                                        (3, 640, 384, 4), (2048, 4096, 4096, 16),
+                                        (256, 1024, 4096, 16)])  # reduction split: 8 slices fwd, 2 bwd
 def test_fwd_bwd_parity(cuda_lib, M, N, K, rank):
     from spilltune_b200 import nf4dq
     rec, _, W = _staged(N, K, M + N)

@@ -78,6 +78,8 @@ def parse():
     p.add_argument("--top-k", type=int, default=8)
     p.add_argument("--sweep", action="store_true", help="kernel sweep: 4 Llama-3-8B shapes x M in {1..8192}")
     p.add_argument("--sweep-m", default="1,16,256,2048,8192", help="--sweep: token counts, comma separated")
+    p.add_argument("--no-split", action="store_true",
+                   help="--op/--sweep: calls never split their reduction (the one-pass-per-tile order)")
     return p.parse_args()
 
 
@@ -555,7 +557,7 @@ def _graph_us(fns, rounds=4):
     return best / (rounds * len(fns))
 
 
-def probe_sweep(ms=(1, 16, 256, 2048, 8192)):
+def probe_sweep(ms=(1, 16, 256, 2048, 8192), split=True):
     from spilltune_b200 import codec, ops
     dev = torch.device("cuda")
     r = 16
@@ -573,8 +575,9 @@ def probe_sweep(ms=(1, 16, 256, 2048, 8192)):
                          for _ in range(C - 1)]
             xs = [torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16) for _ in range(C)]
             dys = [torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16) for _ in range(C)]
-            fs = [lambda x=x, w=w: ops.fwd(x, w, A, B, 2.0) for x, w in zip(xs, ws)]
-            bs = [lambda x=x, w=w, dy=dy: ops.bwd(dy, x, w, A, B, 2.0) for x, w, dy in zip(xs, ws, dys)]
+            fs = [lambda x=x, w=w: ops.fwd(x, w, A, B, 2.0, split_reduction=split) for x, w in zip(xs, ws)]
+            bs = [lambda x=x, w=w, dy=dy: ops.bwd(dy, x, w, A, B, 2.0, split_reduction=split)
+                  for x, w, dy in zip(xs, ws, dys)]
             for f, b in zip(fs[:2], bs[:2]):
                 f()
                 b()
@@ -614,9 +617,10 @@ def probe_op(a):
     else:
         out = torch.empty(a.N, a.K, dtype=torch.bfloat16, device=dev)
         ts = ops.fwd(x, w, A, B, 2.0, return_ts=True)[1] if a.ts and a.op == "bwd" and a.rank else None
+        sp = not a.no_split
         fn = {
-            "fwd": lambda: ops.fwd(x, w, A, B, 2.0),
-            "bwd": (lambda: ops.bwd(dy, x, w, A, B, 2.0, ts=ts)) if ts is not None else (lambda: ops.bwd(dy, x, w, A, B, 2.0)),
+            "fwd": lambda: ops.fwd(x, w, A, B, 2.0, split_reduction=sp),
+            "bwd": lambda: ops.bwd(dy, x, w, A, B, 2.0, ts=ts, split_reduction=sp),
             "dequant": lambda: ops.dequant(w, out=out),
         }[a.op]
     for _ in range(2):
@@ -773,7 +777,7 @@ def main():
         from spilltune_b200 import build
         build.build()
         if args.sweep:
-            probe_sweep(tuple(int(m) for m in args.sweep_m.split(",")))
+            probe_sweep(tuple(int(m) for m in args.sweep_m.split(",")), split=not args.no_split)
         else:
             probe_op(args)
         return 0

@@ -156,7 +156,7 @@ static int pairs_beside(int lowrank_ctas) {
 static int fwd_ksplit(int layout, int64_t M, int64_t N, int64_t K, int rank) {
   if (M <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || M > (1 << 30) || small_m_path(layout, M, K)) return 1;
   const int ld = rank > 0 ? lora_down_ctas((int)M, (int)K, rank) : 0;
-  return gemm_ksplit(((N + 255) / 256) * ((M + 255) / 256), K / 64, pairs_beside(ld));
+  return gemm_ksplit(((N + 255) / 256) * ((M + 255) / 256), K / 64, pairs_beside(ld), device_pairs());
 }
 
 // Counted for the low-rank pass over dY that precedes the GEMM when the caller
@@ -166,7 +166,7 @@ static int fwd_ksplit(int layout, int64_t M, int64_t N, int64_t K, int rank) {
 static int bwd_ksplit(int layout, int64_t M, int64_t N, int64_t K, int rank) {
   if (M <= 0 || N <= 0 || K <= 0 || N % 64 != 0 || M > (1 << 30) || small_m_path(layout, M, K)) return 1;
   const int ld = rank > 0 ? lora_down_ctas((int)M, (int)N, rank) : 0;
-  return gemm_ksplit(((K + 255) / 256) * ((M + 255) / 256), N / 64, pairs_beside(ld));
+  return gemm_ksplit(((K + 255) / 256) * ((M + 255) / 256), N / 64, pairs_beside(ld), device_pairs());
 }
 
 extern "C" {

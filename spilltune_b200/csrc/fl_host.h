@@ -35,12 +35,14 @@ int launch_fwd_gemm(const void* x, const void* ts, const uint8_t* codes, const f
                     int ksplit = 1);
 
 // Reduction split of a dense tile GEMM with `tiles` output tiles of `stages`
-// 64-wide reduction stages, `pairs` CTA pairs free for it: 1, or the largest
-// power of two (<= 16) for which tiles * split <= pairs and every split keeps an
-// even number, at least 8, of stages; no split below 32 stages (the reduce
-// launch would cost more than the shorter tiles save).  Output tiles that
-// would leave most pairs idle (few tokens, few output columns) then use them all.
-int gemm_ksplit(int64_t tiles, int64_t stages, int pairs);
+// 64-wide reduction stages: 1, or the largest power of two (<= 16) for which
+// every split keeps an even number, at least 8, of stages and tiles * split
+// pairs fit in `pairs_free` (the CTA pairs beside the chain's low-rank
+// kernels) -- in `pairs_all` when each slice still has >= 64 stages.  No split
+// below 32 stages (the reduce launch would cost more than the shorter tiles
+// save).  Output tiles that would leave most pairs idle (few tokens, few
+// output columns) then use them all.
+int gemm_ksplit(int64_t tiles, int64_t stages, int pairs_free, int pairs_all);
 int device_pairs();  // SMs / 2 of the current device (74 when it cannot be queried)
 // out[i] = bf16(part[0][i] + part[1][i] + ... + part[split-1][i]), i < plane,
 // summed in that order (fl_split.cu).  Launched as a programmatic dependent of

@@ -68,11 +68,16 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restri
   }
 }
 
-int gemm_ksplit(int64_t tiles, int64_t stages, int pairs) {
+int gemm_ksplit(int64_t tiles, int64_t stages, int pairs_free, int pairs_all) {
   int split = 1;
   if (stages < 32) return split;
-  while (split < 16 && tiles * 2 * split <= pairs && stages % (4 * split) == 0 && stages / (2 * split) >= 8)
+  while (split < 16 && stages % (4 * split) == 0 && stages / (2 * split) >= 8) {
+    // Slices of >= 64 stages outlast the chain's low-rank kernels many times
+    // over: pairs that start only once those finish still end close to the rest.
+    const int limit = stages / (2 * split) >= 64 ? pairs_all : pairs_free;
+    if (tiles * 2 * split > limit) break;
     split *= 2;
+  }
   return split;
 }
 

@@ -45,15 +45,31 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 namespace sm {
 
 constexpr int kGroups = 4;                       // 128-wide scale groups per chunk
-constexpr int kWarps = 2 * kGroups;              // consumer warps: group x tile half
-constexpr int kThreads = 32 * (kWarps + 1);      // + one TMA producer warp
 constexpr int kChunkK = 512;                     // reduction columns per ring slot
-constexpr int kTableBytes = 256 * 32 * 4;        // [byte][lane] bf16 pairs
-constexpr int kTilesPerWarp = 2;                 // 16-row tiles per warp: 64 rows per CTA
+constexpr int kTilesPerWarp = 2;                 // 16-row tiles per warp
 // After the main loop the table's space holds Ts [16][65] (rows padded so the
 // 16 tokens of a warp's reads fall in different banks) and Blora rows [rows][64] (fp32).
 constexpr int kTsStride = 65;
-static_assert((16 * kTsStride + 32 * kTilesPerWarp * 64) * 4 <= kTableBytes, "epilogue staging");
+
+// Q row slabs of 16 * TW rows per CTA, each slab's chunk split over the kGroups
+// scale groups: kGroups * Q consumer warps + one TMA producer warp.  The byte
+// table holds a copy per lane of every entry: entry e of lane l at
+// e * kRowStride + 4 l.  Q = 2 (64 rows, two CTAs per SM): 128-byte entry rows
+// in a static array (its address a link-time constant), the lookup address an
+// OR of the shifted byte and 4 l.  Q = 4 (128 rows, one CTA per SM): 256-byte
+// entry rows at the start of dynamic shared memory, so one byte permute forms
+// (byte << 8) | 4 l; the rows' upper halves stay unused.
+template <int Q>
+struct Layout {
+  static constexpr int kWarps = kGroups * Q;
+  static constexpr int kThreads = 32 * (kWarps + 1);
+  static constexpr int kRowStride = Q == 4 ? 256 : 128;
+  static constexpr int kTableBytes = 256 * kRowStride;
+  static constexpr int kRows = 16 * kTilesPerWarp * Q;
+  static constexpr int kCtasPerSm = Q == 4 ? 1 : 2;
+  static_assert(Q == 2 || Q == 4, "two or four row slabs");
+  static_assert((16 * kTsStride + kRows * 64) * 4 <= kTableBytes, "epilogue staging");
+};
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -90,34 +106,47 @@ __host__ __device__ constexpr int slot_bytes(int rows, int nt) {
   return rows * 128 * 2 + 8 * x_box_bytes(nt) + rows * 16;
 }
 __host__ __device__ constexpr int slot_stride(int rows, int nt) { return (slot_bytes(rows, nt) + 1023) / 1024 * 1024; }
-// Dynamic shared memory: ring | full and empty mbarriers + abort word.  After the main
-// loop the ring's space holds the partial sums [group][rows][16].  The byte table is a
-// static shared array (its address a link-time constant, so a lookup's address needs
-// no add): kTableBytes more per CTA.
+// Dynamic shared memory: [Q = 4: the byte table] | ring | full and empty mbarriers +
+// abort word.  After the main loop the ring's space holds the partial sums
+// [group][rows][16].  With Q = 2 the byte table is a static shared array.
 __host__ __device__ constexpr int smem_bytes(int rows, int nt, int slots) {
   return 1024 + slots * slot_stride(rows, nt) + 2 * slots * 8 + 16;
+}
+template <int Q>
+__host__ __device__ constexpr int dyn_smem_bytes(int nt, int slots) {
+  return (Q == 4 ? Layout<Q>::kTableBytes : 0) + smem_bytes(Layout<Q>::kRows, nt, slots);
 }
 __host__ __device__ constexpr int red_bytes(int rows) { return kGroups * rows * 16 * 4; }
 
 // NT: 8-token tiles, 1 (M <= 8) or 2 (M <= 16).  TW: 16-row tiles per warp,
 // unrolled so the MMA chains of different tiles interleave; with one tile and
 // one token tile the k-steps alternate between two partial sums (PS = 2).
-template <int NT, int TW>
-__global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
+// Q: row slabs (Layout above).
+template <int NT, int TW, int Q>
+__global__ void __launch_bounds__(Layout<Q>::kThreads, Layout<Q>::kCtasPerSm)
     smallm_kernel(const __grid_constant__ CUtensorMap tm_codes,   // [N, K/2] u8, box {128, rows}, 128B swizzle
                   const __grid_constant__ CUtensorMap tm_x,       // [M, K] bf16, box {64, 8 NT}, 128B swizzle
                   const __grid_constant__ CUtensorMap tm_scales,  // [N, K/128] fp32, box {4, rows}
                   const Args args) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(1024) uint32_t s_table[kTableBytes / 4];  // [256][32] bf16 pairs
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using L = Layout<Q>;
+  constexpr int kWarps = L::kWarps;
+  constexpr int kThreads = L::kThreads;
+  uint8_t* table;
+  if constexpr (Q == 4) {
+    table = smem_raw;
+  } else {
+    __shared__ __align__(1024) uint32_t s_table[L::kTableBytes / 4];  // [256][32] bf16 pairs
+    table = reinterpret_cast<uint8_t*>(s_table);
+  }
+  const uintptr_t ring0 = reinterpret_cast<uintptr_t>(smem_raw) + (Q == 4 ? L::kTableBytes : 0);
+  uint8_t* smem = reinterpret_cast<uint8_t*>((ring0 + 1023) & ~uintptr_t(1023));
   constexpr int PS = TW * NT <= 1 ? 2 : 1;
-  constexpr int rows = 32 * TW;
+  constexpr int rows = L::kRows;
   constexpr int sbytes = slot_stride(rows, NT);
   constexpr int kXOff = rows * 256;                    // activation boxes within a slot
   constexpr int kSOff = kXOff + 8 * x_box_bytes(NT);   // scales within a slot
   uint8_t* ring = smem;                                                    // slots x sbytes
-  uint8_t* table = reinterpret_cast<uint8_t*>(s_table);
   float* red = reinterpret_cast<float*>(ring);                             // [group][rows][16], after the loop
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + args.slots * sbytes);  // [slots]: TMA bytes landed
   uint64_t* empty = full + args.slots;                                      // [slots]: every consumer warp done
@@ -132,7 +161,7 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
   // partial sums use the same map.
   const int pg = (g >> 1) | ((g & 1) << 2);
   const int grp = warp & (kGroups - 1);  // scale group of every chunk
-  const int half = warp / kGroups;       // tiles [half * TW, half * TW + TW) of the CTA
+  const int half = warp / kGroups;       // row slab: tiles [half * TW, half * TW + TW) of the CTA
   const int split = args.split;
   const int kslice = split > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   const int n0 = (blockIdx.x / split) * rows;
@@ -170,28 +199,38 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
   };
   if (threadIdx.x == 0)
     for (int i = 0; i < args.slots && i < n_ch; ++i) issue(i);
-  // Per-lane byte table: entry e of lane l at table + 128 e + 4 l holds the
-  // bf16 pair {lut[e & 15], lut[e >> 4]}.  Lane l of warp w builds entry
-  // 32 w + l, then the warp writes its 32 entries, one copy per lane.
+  // Per-lane byte table: entry e of lane l at table + kRowStride e + 4 l holds
+  // the bf16 pair {lut[e & 15], lut[e >> 4]}.  Warp w builds entries
+  // [E w, E w + E), E = 256 / kWarps, then writes them, one copy per lane.
   if (warp < kWarps) {
+    constexpr int E = 256 / kWarps;
     const float mine = __ldg(args.lut + (lane & 15));
-    const int e = 32 * warp + lane;
+    const int e = E * warp + (lane % E);
     const uint32_t packed =
         pack_bf16x2(__shfl_sync(0xffffffffu, mine, e & 15), __shfl_sync(0xffffffffu, mine, e >> 4));
-    uint32_t* tw = reinterpret_cast<uint32_t*>(table) + 32 * warp * 32 + lane;
+    uint32_t* tw = reinterpret_cast<uint32_t*>(table + E * warp * L::kRowStride) + lane;
 #pragma unroll 8
-    for (int j = 0; j < 32; ++j) tw[j * 32] = __shfl_sync(0xffffffffu, packed, j);
+    for (int j = 0; j < E; ++j) tw[j * (L::kRowStride / 4)] = __shfl_sync(0xffffffffu, packed, j);
   }
   __syncthreads();
-  // Byte b of payload word w -> the pair of elements 2b, 2b + 1, at entry byte * 128 + lane * 4
-  // (bits 7..14 and 2..6: an OR).
-  const uint32_t tab0 = smem_u32(s_table);
+  // Byte b of payload word w -> the pair of elements 2b, 2b + 1, at entry
+  // byte * kRowStride + lane * 4.
+  const uint32_t tab0 = smem_u32(table);
   const uint32_t lane4 = static_cast<uint32_t>(lane) * 4;
   auto decode = [&](uint32_t w, uint32_t* out) {
-    out[0] = lds_u32(tab0 + (((w << 7) & 0x7F80u) | lane4));
-    out[1] = lds_u32(tab0 + (((w >> 1) & 0x7F80u) | lane4));
-    out[2] = lds_u32(tab0 + (((w >> 9) & 0x7F80u) | lane4));
-    out[3] = lds_u32(tab0 + (((w >> 17) & 0x7F80u) | lane4));
+    if constexpr (Q == 4) {
+      // (byte << 8) | lane4 in one permute: result bytes {lane4.b0, w.b_i, 0, 0}.
+      out[0] = lds_u32(tab0 + __byte_perm(w, lane4, 0x5504u));
+      out[1] = lds_u32(tab0 + __byte_perm(w, lane4, 0x5514u));
+      out[2] = lds_u32(tab0 + __byte_perm(w, lane4, 0x5524u));
+      out[3] = lds_u32(tab0 + __byte_perm(w, lane4, 0x5534u));
+    } else {
+      // bits 7..14 and 2..6: an OR.
+      out[0] = lds_u32(tab0 + (((w << 7) & 0x7F80u) | lane4));
+      out[1] = lds_u32(tab0 + (((w >> 1) & 0x7F80u) | lane4));
+      out[2] = lds_u32(tab0 + (((w >> 9) & 0x7F80u) | lane4));
+      out[3] = lds_u32(tab0 + (((w >> 17) & 0x7F80u) | lane4));
+    }
   };
 
   float acc[TW][NT][4];
@@ -364,20 +403,29 @@ __global__ void __launch_bounds__(kThreads, TW == 1 ? 3 : 2)
   if (split > 1) cluster_sync();  // peers' partials stay valid until rank 0 has read them
 }
 
-// CTAs of smallm_kernel<NT, TW> resident per SM with `slots` ring slots (sets
+// Split of the reduction across a cluster while the grid still fits in one
+// wave of `slots` resident CTAs and every CTA keeps two 512-wide chunks.
+static int cluster_split(int blocks, int chunks, int slots) {
+  int split = 1;
+  while (split < 8 && blocks * split * 2 <= slots && chunks >= 2 * split) split *= 2;
+  return split;
+}
+
+// CTAs of smallm_kernel<NT, TW, Q> resident per SM with `slots` ring slots (sets
 // the kernel's shared-memory limit once per device and ring depth).
-template <int NT, int TW>
+template <int NT, int TW, int Q>
 static int resident_per_sm(int slots, int* per_sm) {
   static int cache[64][9] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || slots < 1 || slots > 8)
     return set_error(FL_ERR_CUDA, "small-M: no current device");
   if (!cache[dev][slots]) {
-    const int smem = smem_bytes(32 * TW, NT, slots);
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&smallm_kernel<NT, TW>),
+    const int smem = dyn_smem_bytes<Q>(NT, slots);
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&smallm_kernel<NT, TW, Q>),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     int n = 0;
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, smallm_kernel<NT, TW>, kThreads, smem);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, smallm_kernel<NT, TW, Q>, Layout<Q>::kThreads, smem);
     if (e != cudaSuccess || n < 1) return set_error(FL_ERR_CUDA, "small-M occupancy query failed");
     cache[dev][slots] = n;
   }
@@ -385,29 +433,29 @@ static int resident_per_sm(int slots, int* per_sm) {
   return FL_OK;
 }
 
-template <int NT, int TW>
+template <int NT, int TW, int Q>
 static int launch_tw(Args a, const void* codes, const float* scales, bool pdl, cudaStream_t stream) {
-  constexpr int rows = 32 * TW;
+  using L = Layout<Q>;
+  constexpr int rows = L::kRows;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
     sms = 148;
   // Ring depth: the most slots that still fit next to the table at the
   // occupancy the registers allow.
-  constexpr int want_ctas = TW == 1 ? 3 : 2;
+  constexpr int want_ctas = L::kCtasPerSm;
   int slots = 2;
-  while (slots < 6 && want_ctas * (smem_bytes(rows, NT, slots + 1) + kTableBytes + 1024) <= 233472) ++slots;
-  if (want_ctas * (smem_bytes(rows, NT, slots) + kTableBytes + 1024) > 233472 ||
+  while (slots < 6 && want_ctas * (smem_bytes(rows, NT, slots + 1) + L::kTableBytes + 1024) <= 233472) ++slots;
+  if (want_ctas * (smem_bytes(rows, NT, slots) + L::kTableBytes + 1024) > 233472 ||
       red_bytes(rows) > slots * slot_stride(rows, NT))
     return set_error(FL_ERR_CUDA, "small-M: shared-memory plan does not fit");
   int per_sm = 1;
-  int rc = resident_per_sm<NT, TW>(slots, &per_sm);
+  int rc = resident_per_sm<NT, TW, Q>(slots, &per_sm);
   if (rc) return rc;
   const int blocks = (a.N + rows - 1) / rows;
   // Too few row blocks for one full wave: split the reduction across a cluster.
   const int chunks = a.K / kChunkK;
-  int split = 1;
-  while (split < 8 && blocks * split * 2 <= per_sm * sms && chunks >= 2 * split) split *= 2;
+  const int split = cluster_split(blocks, chunks, per_sm * sms);
   a.split = split;
   a.slots = slots;
   CUtensorMap tc, tx, ts;
@@ -422,8 +470,8 @@ static int launch_tw(Args a, const void* codes, const float* scales, bool pdl, c
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(blocks * split);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem_bytes(rows, NT, slots);
+  cfg.blockDim = dim3(L::kThreads);
+  cfg.dynamicSmemBytes = dyn_smem_bytes<Q>(NT, slots);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -434,7 +482,7 @@ static int launch_tw(Args a, const void* codes, const float* scales, bool pdl, c
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  cudaError_t le = cudaLaunchKernelEx(&cfg, smallm_kernel<NT, TW>, tc, tx, ts, a);
+  cudaError_t le = cudaLaunchKernelEx(&cfg, smallm_kernel<NT, TW, Q>, tc, tx, ts, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "small-M launch: %s", cudaGetErrorString(le));
   return FL_OK;
 }
@@ -467,8 +515,20 @@ int launch_smallm_fwd(const void* X, const float* lora_parts, float s, const uin
   a.slots = 2;
   // With a LoRA term the preceding launch produced Ts: start while it runs.
   const bool pdl = rank > 0;
-  if (M <= 8) return launch_tw<1, kTilesPerWarp>(a, codes, scales, pdl, stream);
-  return launch_tw<2, kTilesPerWarp>(a, codes, scales, pdl, stream);
+  // One token tile (M <= 8): 128-row CTAs with the byte-permute table (Q = 4)
+  // when each CTA still streams at least four chunks.  Measured against Q = 2
+  // (back-to-back calls over cold copies): 14336x4096 18.5 -> 17.7 us,
+  // 4096x14336 22.3 -> 21.8 us, 6144x4096 14.3 -> 14.0 us; with two chunks per
+  // CTA (4096x4096, 1024x4096) and with two token tiles Q = 4 was 2-6% slower.
+  if (M <= 8) {
+    int sms = 148;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
+    const int chunks = K / kChunkK;
+    const bool long_ctas = chunks / cluster_split((N + 127) / 128, chunks, sms) >= 4;
+    return long_ctas ? launch_tw<1, kTilesPerWarp, 4>(a, codes, scales, pdl, stream)
+                     : launch_tw<1, kTilesPerWarp, 2>(a, codes, scales, pdl, stream);
+  }
+  return launch_tw<2, kTilesPerWarp, 2>(a, codes, scales, pdl, stream);
 }
 
 }  // namespace fl

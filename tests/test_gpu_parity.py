@@ -323,6 +323,10 @@ SMALLM_CASES = [
     (7, 640, 384, 16),       # K % 512 != 0: the tile GEMM
     (16, 8, 128, 4),         # one group, 8 valid rows (tile GEMM)
     (2, 29568, 4096, 0),     # 924 row blocks: no split
+    # <= 8 tokens with >= 4 chunks per CTA: 128-row CTAs with the byte-permute table
+    (4, 14300, 4096, 8),     # last row block ragged
+    (1, 4096, 14336, 16),    # reduction split over a 4-CTA cluster (7 chunks each)
+    (6, 6144, 4096, 64),     # 2-CTA cluster, rank 64
 ]
 
 

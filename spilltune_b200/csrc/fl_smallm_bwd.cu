@@ -47,8 +47,7 @@ constexpr int kCols = 128;                        // dX columns (W columns) per 
 constexpr int kChunkN = 64;                       // reduction rows (W rows) per ring slot
 constexpr int kWarps = 8;                         // consumer warps, 16 columns each
 constexpr int kThreads = 32 * (kWarps + 1);       // + one TMA producer warp
-constexpr int kSlots = 6;
-constexpr int kTableBytes = 256 * 32 * 4;         // [byte][lane] bf16 pairs
+constexpr int kTableBytes = 256 * 256;           // [byte][256-byte row: lane] bf16 pairs
 constexpr int kCodeBytes = kChunkN * kCols / 2;   // 64 rows x 64 B
 constexpr int kScaleBytes = kChunkN * 16;         // 64 rows x 4 groups (fp32)
 constexpr int kRedBytes = kCols * 16 * 4;         // fp32 partial dX [column][16 tokens]
@@ -57,14 +56,18 @@ constexpr int kUsStride = 65;                     // fp32 Us rows, padded agains
 __host__ __device__ constexpr int dy_bytes(int nt) { return 8 * nt * 128; }  // [8 NT tokens][64 n] bf16
 __host__ __device__ constexpr int slot_bytes(int nt) { return kCodeBytes + dy_bytes(nt) + kScaleBytes; }
 __host__ __device__ constexpr int slot_stride(int nt) { return (slot_bytes(nt) + 1023) / 1024 * 1024; }
-// Dynamic shared memory: ring | table | partial dX | full and empty mbarriers + abort word.
+// Ring depth: the most slots that keep two CTAs per SM next to the 64 KiB table.
+__host__ __device__ constexpr int slots_of(int nt) { return nt == 2 ? 5 : 6; }
+// Dynamic shared memory: table (at offset 0: a constant address) | ring | partial dX |
+// full and empty mbarriers + abort word.
 __host__ __device__ constexpr int smem_bytes(int nt) {
-  return 1024 + kSlots * slot_stride(nt) + kTableBytes + kRedBytes + 2 * kSlots * 8 + 16;
+  return kTableBytes + 1024 + slots_of(nt) * slot_stride(nt) + kRedBytes + 2 * slots_of(nt) * 8 + 16;
 }
+static_assert(2 * (smem_bytes(1) + 1024) <= 233472 && 2 * (smem_bytes(2) + 1024) <= 233472, "two CTAs per SM");
 // After the main loop the table's space holds A columns [rank][128] and the
 // ring's space Us, Ts [16][kUsStride] and X columns [16][128] (fp32).
 static_assert(64 * kCols * 4 <= kTableBytes, "A staging");
-static_assert((2 * 16 * kUsStride + 16 * kCols) * 4 <= kSlots * kCodeBytes, "Us, Ts, X staging");
+static_assert((2 * 16 * kUsStride + 16 * kCols) * 4 <= slots_of(2) * kCodeBytes, "Us, Ts, X staging");
 
 struct Args {
   const __nv_bfloat16* dY;  // [M, N]
@@ -105,13 +108,14 @@ __global__ void __launch_bounds__(kThreads, 2)
                       const __grid_constant__ CUtensorMap tm_scales,  // [N, K/128] fp32, box {4, 64}
                       const Args args) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kSlots = slots_of(NT);
   constexpr int sbytes = slot_stride(NT);
   constexpr int kDyOff = kCodeBytes;
   constexpr int kSOff = kCodeBytes + dy_bytes(NT);
-  uint8_t* ring = smem;
-  uint8_t* table = ring + kSlots * sbytes;
-  float* red = reinterpret_cast<float*>(table + kTableBytes);                   // [column][16]
+  uint8_t* table = smem_raw;
+  uint8_t* ring = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + kTableBytes + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(ring + kSlots * sbytes);                // [column][16]
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + kRedBytes);
   uint64_t* empty = full + kSlots;
   volatile uint32_t* abort_word = reinterpret_cast<volatile uint32_t*>(empty + kSlots);
@@ -149,16 +153,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();  // barriers initialised
   if (threadIdx.x == 0)
     for (int i = 0; i < kSlots && i < n_ch; ++i) issue(i);
-  // Per-lane byte table (as the small-M forward): entry e of lane l at
-  // table + 128 e + 4 l holds the bf16 pair {lut[e & 15], lut[e >> 4]}.
+  // Per-lane byte table: entry e of lane l at table + 256 e + 4 l holds the
+  // bf16 pair {lut[e & 15], lut[e >> 4]} (the upper half of each 256-byte
+  // row stays unused: one byte permute then forms a lookup's whole address).
   if (warp < kWarps) {
     const float mine = __ldg(args.lut + (lane & 15));
     const int e = 32 * warp + lane;
     const uint32_t packed =
         pack_bf16x2(__shfl_sync(0xffffffffu, mine, e & 15), __shfl_sync(0xffffffffu, mine, e >> 4));
-    uint32_t* tw = reinterpret_cast<uint32_t*>(table) + 32 * warp * 32 + lane;
+    uint32_t* tw = reinterpret_cast<uint32_t*>(table) + 32 * warp * 64 + lane;
 #pragma unroll 8
-    for (int j = 0; j < 32; ++j) tw[j * 32] = __shfl_sync(0xffffffffu, packed, j);
+    for (int j = 0; j < 32; ++j) tw[j * 64] = __shfl_sync(0xffffffffu, packed, j);
   }
   __syncthreads();
 
@@ -185,11 +190,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else {
     // ------------------------------------------------------------ consumers
-    const uint32_t tab = smem_u32(table) + static_cast<uint32_t>(lane) * 4;
-    // prmt selector moving byte c4 of a word to bits 8..15 (the rest zero):
-    // (that >> 1) is the byte's table offset, 128 per entry.
-    const uint32_t sel = 0x4404u | (static_cast<uint32_t>(c4) << 4);
-    auto lookup = [&](uint32_t w) { return lds_u32(tab + (prmt(w, 0u, sel) >> 1)); };
+    const uint32_t tab0 = smem_u32(table);
+    const uint32_t lane4 = static_cast<uint32_t>(lane) * 4;
+    // prmt selector giving {lane4 byte 0, byte c4 of the word, 0, 0}: the
+    // lookup's offset (byte << 8) | 4 lane in one instruction.
+    const uint32_t sel = 0x5504u | (static_cast<uint32_t>(c4) << 4);
+    auto lookup = [&](uint32_t w) { return lds_u32(tab0 + prmt(w, lane4, sel)); };
     const int gcol = cb & 3;  // this CTA's group within the 4-group scale box
     for (int k = 0; k < n_ch && ok; ++k) {
       const int sl = k % kSlots;

@@ -54,11 +54,11 @@ constexpr int kTsStride = 65;
 // Q row slabs of 16 * TW rows per CTA, each slab's chunk split over the kGroups
 // scale groups: kGroups * Q consumer warps + one TMA producer warp.  The byte
 // table holds a copy per lane of every entry: entry e of lane l at
-// e * kRowStride + 4 l.  Q = 2 (64 rows, two CTAs per SM): 128-byte entry rows
-// in a static array (its address a link-time constant), the lookup address an
-// OR of the shifted byte and 4 l.  Q = 4 (128 rows, one CTA per SM): 256-byte
-// entry rows at the start of dynamic shared memory, so one byte permute forms
-// (byte << 8) | 4 l; the rows' upper halves stay unused.
+// e * kRowStride + 4 l, at the start of dynamic shared memory (a constant
+// address).  Q = 2 (64 rows, two CTAs per SM): 128-byte entry rows, a lookup's
+// offset a byte permute (byte << 8) | 8 l shifted right by one.  Q = 4 (128
+// rows, one CTA per SM): 256-byte entry rows, so the permute (byte << 8) | 4 l
+// is the offset itself; the rows' upper halves stay unused.
 template <int Q>
 struct Layout {
   static constexpr int kWarps = kGroups * Q;
@@ -114,7 +114,7 @@ __host__ __device__ constexpr int smem_bytes(int rows, int nt, int slots) {
 }
 template <int Q>
 __host__ __device__ constexpr int dyn_smem_bytes(int nt, int slots) {
-  return (Q == 4 ? Layout<Q>::kTableBytes : 0) + smem_bytes(Layout<Q>::kRows, nt, slots);
+  return Layout<Q>::kTableBytes + smem_bytes(Layout<Q>::kRows, nt, slots);
 }
 __host__ __device__ constexpr int red_bytes(int rows) { return kGroups * rows * 16 * 4; }
 
@@ -132,14 +132,8 @@ __global__ void __launch_bounds__(Layout<Q>::kThreads, Layout<Q>::kCtasPerSm)
   using L = Layout<Q>;
   constexpr int kWarps = L::kWarps;
   constexpr int kThreads = L::kThreads;
-  uint8_t* table;
-  if constexpr (Q == 4) {
-    table = smem_raw;
-  } else {
-    __shared__ __align__(1024) uint32_t s_table[L::kTableBytes / 4];  // [256][32] bf16 pairs
-    table = reinterpret_cast<uint8_t*>(s_table);
-  }
-  const uintptr_t ring0 = reinterpret_cast<uintptr_t>(smem_raw) + (Q == 4 ? L::kTableBytes : 0);
+  uint8_t* table = smem_raw;
+  const uintptr_t ring0 = reinterpret_cast<uintptr_t>(smem_raw) + L::kTableBytes;
   uint8_t* smem = reinterpret_cast<uint8_t*>((ring0 + 1023) & ~uintptr_t(1023));
   constexpr int PS = TW * NT <= 1 ? 2 : 1;
   constexpr int rows = L::kRows;
@@ -216,20 +210,21 @@ __global__ void __launch_bounds__(Layout<Q>::kThreads, Layout<Q>::kCtasPerSm)
   // Byte b of payload word w -> the pair of elements 2b, 2b + 1, at entry
   // byte * kRowStride + lane * 4.
   const uint32_t tab0 = smem_u32(table);
-  const uint32_t lane4 = static_cast<uint32_t>(lane) * 4;
+  // Permute result bytes {x.b0, w.b_i, 0, 0} = (byte_i << 8) | x.
+  const uint32_t lanex = static_cast<uint32_t>(lane) * (Q == 4 ? 4 : 8);
   auto decode = [&](uint32_t w, uint32_t* out) {
     if constexpr (Q == 4) {
-      // (byte << 8) | lane4 in one permute: result bytes {lane4.b0, w.b_i, 0, 0}.
-      out[0] = lds_u32(tab0 + __byte_perm(w, lane4, 0x5504u));
-      out[1] = lds_u32(tab0 + __byte_perm(w, lane4, 0x5514u));
-      out[2] = lds_u32(tab0 + __byte_perm(w, lane4, 0x5524u));
-      out[3] = lds_u32(tab0 + __byte_perm(w, lane4, 0x5534u));
+      // 256-byte rows: (byte << 8) | 4 lane is the offset itself.
+      out[0] = lds_u32(tab0 + __byte_perm(w, lanex, 0x5504u));
+      out[1] = lds_u32(tab0 + __byte_perm(w, lanex, 0x5514u));
+      out[2] = lds_u32(tab0 + __byte_perm(w, lanex, 0x5524u));
+      out[3] = lds_u32(tab0 + __byte_perm(w, lanex, 0x5534u));
     } else {
-      // bits 7..14 and 2..6: an OR.
-      out[0] = lds_u32(tab0 + (((w << 7) & 0x7F80u) | lane4));
-      out[1] = lds_u32(tab0 + (((w >> 1) & 0x7F80u) | lane4));
-      out[2] = lds_u32(tab0 + (((w >> 9) & 0x7F80u) | lane4));
-      out[3] = lds_u32(tab0 + (((w >> 17) & 0x7F80u) | lane4));
+      // 128-byte rows: ((byte << 8) | 8 lane) >> 1.
+      out[0] = lds_u32(tab0 + (__byte_perm(w, lanex, 0x5504u) >> 1));
+      out[1] = lds_u32(tab0 + (__byte_perm(w, lanex, 0x5514u) >> 1));
+      out[2] = lds_u32(tab0 + (__byte_perm(w, lanex, 0x5524u) >> 1));
+      out[3] = lds_u32(tab0 + (__byte_perm(w, lanex, 0x5534u) >> 1));
     }
   };
 

@@ -54,8 +54,9 @@ def parse():
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["llama3-8b", "qwen3-30b-a3b"], default="llama3-8b",
-                   help="llama3-8b: the headline step (Llama-3-8B stack, 32 layers); qwen3-30b-a3b: the Qwen3-MoE 30B-A3B stack")
+    p.add_argument("--workload", choices=["llama3-8b", "qwen3-30b-a3b", "deepseek-v3-6l"], default="llama3-8b",
+                   help="llama3-8b: the headline step (Llama-3-8B stack, 32 layers); qwen3-30b-a3b: the Qwen3-MoE "
+                        "30B-A3B stack; deepseek-v3-6l: DeepSeek-V3 truncated to 6 layers (3 dense, 3 MoE)")
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--tokens", type=int, default=8192, help="tokens per GPU per step (micro-batch 4 x seq 2048)")
     p.add_argument("--codec", default="nf4-g128")
@@ -765,14 +766,180 @@ def run_moe(args, world, rank, local):
     return 0
 
 
+DSV3 = {"hidden": 7168, "heads": 128, "q_lora": 1536, "kv_lora": 512, "nope": 128, "rope": 64, "v_head": 128,
+        "dense_inter": 18432, "dense_layers": 3, "moe_layers": 3, "experts": 256, "top_k": 8, "expert_inter": 2048,
+        "groups": 8, "group_k": 4, "route_scale": 2.5, "rank": 16, "alpha": 32.0, "tokens": 4096}
+
+
+def run_deepseek(args, world, rank, local):
+    """The frozen-linear stack of DeepSeek-V3 truncated to 6 layers (3 dense with
+    intermediate 18432, then 3 MoE with 256 routed experts top-8 of intermediate
+    2048 plus one shared expert; hidden 7168; MLA attention with 128 heads,
+    q_lora_rank 1536, kv_lora_rank 512, qk_nope 128, qk_rope 64, v_head 128;
+    NF4 group-128 records; LoRA rank 16 on every projection, per expert for the
+    routed ones; seq 4096 x micro-batch 1 = 4096 tokens per GPU).  Per layer:
+    q_a_proj and kv_a_proj_with_mqa over the same input as one call (N = 1536 +
+    576), q_b_proj (24576 x 1536), kv_b_proj (32768 x 512), o_proj (7168 x 16384);
+    dense layers gate, up (18432 x 7168) and down (7168 x 18432); MoE layers the
+    shared expert's gate/up as one call (4096 x 7168) and down (7168 x 2048), and
+    the grouped routed experts gate_up [256, 4096, 7168] and down [256, 7168, 2048]
+    over the 32768 routed rows, routed by DeepSeek-V3's group-limited sigmoid
+    router (moe.deepseek_route) from random router weights.  Step = forward,
+    recomputed forward and backward of every call, then AdamW.  The records hold
+    random NF4 codes and scales (19 GB packed, resident in HBM): the kernels' work
+    does not depend on the values, and encoding 11 B expert weights per layer from
+    FP32 would need tens of GB of temporaries.  Inputs and upstream gradients are
+    synthetic per-call buffers in two alternating sets; attention, norms, router,
+    gather, SiLU and combine are outside the frozen-linear stack."""
+    import math
+    from spilltune_b200 import build, codec, moe, ops
+    build.build()
+    dev = torch.device("cuda", local)
+    c = DSV3
+    T = args.tokens if args.tokens != 8192 else c["tokens"]
+    H, E, k, I, r = c["hidden"], c["experts"], c["top_k"], c["expert_inter"], c["rank"]
+    qb_n = c["heads"] * (c["nope"] + c["rope"])
+    kvb_n = c["heads"] * (c["nope"] + c["v_head"])
+    o_k = c["heads"] * c["v_head"]
+    kva_n = c["kv_lora"] + c["rope"]
+    scale = c["alpha"] / r
+    rows = T * k
+    g = torch.Generator(device=dev).manual_seed(4321)
+    lut = codec.NF4_LUT.to(dev)
+
+    def record(*shape):
+        groups = math.prod(shape) // 128
+        payload = torch.randint(0, 256, (groups * 64,), generator=g, device=dev, dtype=torch.uint8)
+        scales = torch.rand(groups, generator=g, device=dev) * 0.02 + 0.004
+        return codec.PackedWeight(payload, scales, lut, shape, codec.NF4)
+
+    def lora(n_experts, N, K, rk=r):
+        shape_a = (n_experts, rk, K) if n_experts else (rk, K)
+        shape_b = (n_experts, N, rk) if n_experts else (N, rk)
+        A = (torch.randn(*shape_a, generator=g, device=dev) * 0.01).requires_grad_(True)
+        B = (torch.randn(*shape_b, generator=g, device=dev) * 0.01).requires_grad_(True)
+        A.grad, B.grad = torch.zeros_like(A), torch.zeros_like(B)
+        return A, B
+
+    layers = []
+    for li in range(c["dense_layers"] + c["moe_layers"]):
+        moe_layer = li >= c["dense_layers"]
+        # q_a and kv_a as one call: A = [A_qa; A_kva], B block-diagonal (gradient masked).
+        A_a = (torch.randn(2 * r, H, generator=g, device=dev) * 0.01).requires_grad_(True)
+        B_a = torch.zeros(c["q_lora"] + kva_n, 2 * r, device=dev)
+        mask = torch.zeros_like(B_a)
+        B_a[:c["q_lora"], :r] = torch.randn(c["q_lora"], r, generator=g, device=dev) * 0.01
+        B_a[c["q_lora"]:, r:] = torch.randn(kva_n, r, generator=g, device=dev) * 0.01
+        mask[:c["q_lora"], :r] = 1.0
+        mask[c["q_lora"]:, r:] = 1.0
+        B_a.requires_grad_(True)
+        A_a.grad, B_a.grad = torch.zeros_like(A_a), torch.zeros_like(B_a)
+        lay = {"moe": moe_layer, "mask": mask,
+               "w": {"a": record(c["q_lora"] + kva_n, H), "qb": record(qb_n, c["q_lora"]),
+                     "kvb": record(kvb_n, c["kv_lora"]), "o": record(H, o_k)},
+               "lora": {"a": (A_a, B_a), "qb": lora(0, qb_n, c["q_lora"]), "kvb": lora(0, kvb_n, c["kv_lora"]),
+                        "o": lora(0, H, o_k)}}
+        if moe_layer:
+            lay["w"].update({"sgu": record(2 * I, H), "sdn": record(H, I)})
+            lay["lora"].update({"sgu": lora(0, 2 * I, H), "sdn": lora(0, H, I)})
+            lay["gate_up"], lay["down"] = record(E, 2 * I, H), record(E, H, I)
+            lay["lora"].update({"gate_up": lora(E, 2 * I, H), "down": lora(E, H, I)})
+            router = torch.randn(E, H, generator=g, device=dev) * 0.02
+            bias = torch.randn(E, generator=g, device=dev) * 0.01
+            _w, idx = moe.deepseek_route(torch.randn(T, H, generator=g, device=dev), router, bias, groups=c["groups"],
+                                         group_k=c["group_k"], top_k=k, normalize=True, scale=c["route_scale"])
+            lay["segs"] = moe.expert_segments(idx, E)
+        else:
+            DI = c["dense_inter"]
+            lay["w"].update({"gate": record(DI, H), "up": record(DI, H), "down_d": record(H, DI)})
+            lay["lora"].update({"gate": lora(0, DI, H), "up": lora(0, DI, H), "down_d": lora(0, H, DI)})
+        layers.append(lay)
+    gi = torch.Generator(device=dev).manual_seed(100 + rank)
+    rnd = lambda *shape: torch.randn(*shape, generator=gi, device=dev).to(torch.bfloat16)  # noqa: E731
+    # Inputs of each dense call (name -> [T, K]) and their upstream gradients ([T, N]).
+    dense_in = {"a": H, "qb": c["q_lora"], "kvb": c["kv_lora"], "o": o_k, "gate": H, "up": H,
+                "down_d": c["dense_inter"], "sgu": H, "sdn": I}
+    dense_out = {"a": c["q_lora"] + kva_n, "qb": qb_n, "kvb": kvb_n, "o": H, "gate": c["dense_inter"],
+                 "up": c["dense_inter"], "down_d": H, "sgu": 2 * I, "sdn": H}
+    bufs = []
+    for _ in range(2):
+        b = {("x", n): rnd(T, K) for n, K in dense_in.items()}
+        b.update({("d", n): rnd(T, N) for n, N in dense_out.items()})
+        b.update({"xs": rnd(rows, H), "act": rnd(rows, I), "d_gu": rnd(rows, 2 * I), "d_dn": rnd(rows, H)})
+        bufs.append(b)
+    params = [t for lay in layers for AB in lay["lora"].values() for t in AB]
+    opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
+
+    def names(lay):
+        return ["a", "qb", "kvb", "o"] + (["sgu", "sdn"] if lay["moe"] else ["gate", "up", "down_d"])
+
+    def step():
+        for li, lay in enumerate(layers):
+            b = bufs[li % 2]
+            for n in names(lay):
+                ops.fwd(b[("x", n)], lay["w"][n], *lay["lora"][n], scale)
+            if lay["moe"]:
+                moe.grouped_fwd(b["xs"], lay["segs"], lay["gate_up"], *lay["lora"]["gate_up"], scale)
+                moe.grouped_fwd(b["act"], lay["segs"], lay["down"], *lay["lora"]["down"], scale)
+        for li in reversed(range(len(layers))):
+            lay, b = layers[li], bufs[li % 2]
+            if lay["moe"]:
+                for name, x, d in (("down", b["act"], b["d_dn"]), ("gate_up", b["xs"], b["d_gu"])):
+                    A, B = lay["lora"][name]
+                    moe.grouped_fwd(x, lay["segs"], lay[name], A, B, scale)  # recompute
+                    moe.grouped_bwd(d, x, lay["segs"], lay[name], A, B, scale, dA=A.grad, dB=B.grad)
+            for n in reversed(names(lay)):
+                A, B = lay["lora"][n]
+                x = b[("x", n)]
+                _y, ts = ops.fwd(x, lay["w"][n], A, B, scale, return_ts=True)  # recompute
+                ops.bwd(b[("d", n)], x, lay["w"][n], A, B, scale, dA=A.grad, dB=B.grad, ts=ts)
+            lay["lora"]["a"][1].grad.mul_(lay["mask"])
+        opt.step()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        torch.cuda.nvtx.range_push("timed_step")
+        for _ in range(args.steps):
+            step()
+        torch.cuda.nvtx.range_pop()
+        t1.record()
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    # Weights each token passes per layer (LoRA terms are small and not counted): forward,
+    # recompute and backward (dX) each 2 FLOPs per weight per token.
+    attn = (c["q_lora"] + kva_n) * H + qb_n * c["q_lora"] + kvb_n * c["kv_lora"] + H * o_k
+    w_dense = attn + 3 * c["dense_inter"] * H
+    w_moe = attn + 3 * I * H + k * 3 * I * H
+    step_flops = 3 * 2.0 * T * (c["dense_layers"] * w_dense + c["moe_layers"] * w_moe)
+    packed = sum(w.payload.numel() + 4 * w.scales.numel() for lay in layers
+                 for w in list(lay["w"].values()) + ([lay["gate_up"], lay["down"]] if lay["moe"] else []))
+    line = {"metric": "train tokens/s (DeepSeek-V3-6L NF4 LoRA frozen-linear stack)", "value": T / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "deepseek-v3-6l frozen-linear stack: 3 dense + 3 MoE layers x (q_a/kv_a fused, "
+                                   "q_b, kv_b, o; dense gate, up, down | shared gate_up, down + grouped routed experts "
+                                   f"gate_up and down over {rows} routed rows), fwd + recompute + bwd + AdamW",
+                       "layers": len(layers), "tokens_per_gpu": T, "micro_batch": 1, "seq_len": 4096, "experts": E,
+                       "top_k": k, "expert_inter": I, "rank": r, "alpha": c["alpha"], "codec": "nf4-g128",
+                       "parallelism": "dp1", "packed_gb": round(packed / 1e9, 2),
+                       "weights": "random NF4 codes and scales, resident in HBM (no e2e streaming in this mode)"},
+            "step_tflops": step_flops / (ms / 1e3) / 1e12, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- main
 def main():
     args = parse()
-    if args.workload == "qwen3-30b-a3b":
+    if args.workload in ("qwen3-30b-a3b", "deepseek-v3-6l"):
         world, rank, local = init_dist()
         if world > 1:
-            raise SystemExit("the qwen3-30b-a3b workload runs on one GPU")
-        return run_moe(args, world, rank, local)
+            raise SystemExit(f"the {args.workload} workload runs on one GPU")
+        return (run_moe if args.workload == "qwen3-30b-a3b" else run_deepseek)(args, world, rank, local)
     if args.op or args.sweep:
         from spilltune_b200 import build
         build.build()

@@ -243,9 +243,9 @@ def test_full_size_sampled_rows(cuda_lib, N, K):
 # forward splits its reduction over K, the backward dX's over N (slices at rank
 # 16 on a B200: fwd 4 / bwd 4; fwd 8; fwd 4; bwd 4; fwd 4 with ragged token and
 # output tiles; fwd 4 beside a wider low-rank grid; fwd 2 and bwd 2 with slices
-# long enough to use every pair).
+# long enough to use every pair; bwd 2 for DeepSeek-V3's kv_b_proj at 4096 tokens).
 SPLIT_CASES = [(256, 4096, 4096), (256, 1024, 4096), (256, 4096, 14336), (256, 14336, 4096), (300, 384, 2048),
-               (512, 1024, 4096), (512, 4096, 14336), (512, 14336, 4096)]
+               (512, 1024, 4096), (512, 4096, 14336), (512, 14336, 4096), (4096, 32768, 512)]
 
 
 @pytest.mark.parametrize("M,N,K", SPLIT_CASES)

@@ -38,14 +38,7 @@ namespace bwd {
 constexpr int kTokHalf = 128;              // tokens per CTA (A rows)
 constexpr int kColHalf = 128;              // W columns k per CTA (B rows)
 constexpr int kStageN = 64;                // reduction rows n per stage
-constexpr int kStages = 6;
 constexpr int kGroupM = 4;                 // token tiles per band: a band's pairs fit in one wave, so each dY slab is read once
-constexpr int kGroups = 3;                 // decode warp groups
-constexpr int kThreads = 64 + 128 * kGroups;
-constexpr int kEpiWarps = 4 * kGroups;
-// A decode group's consecutive stages are at most 2 * kGroups apart; at most
-// kStages keeps its parity waits on a ring slot within one phase.
-static_assert(2 * kGroups <= kStages, "decode-group rotation longer than the stage ring");
 constexpr int kAccCols = 256;              // fp32 accumulator columns (pair N)
 constexpr int kTmemCols = 2 * kAccCols;    // two accumulators: tile t+1 accumulates while tile t drains
 constexpr int kABytes = kTokHalf * kStageN * 2;   // 16 KiB dY (or Us) tile
@@ -54,10 +47,11 @@ constexpr int kQBytes = kStageN * kColHalf / 2;   // 4 KiB packed codes
 constexpr uint32_t kBLbo = 1024;           // MN-direction atom stride (64 k per atom)
 constexpr uint32_t kBSbo = 2048;           // K-direction 8-row group stride
 
-struct __align__(16) Barriers {
-  uint64_t full[kStages];
-  uint64_t afull[kStages];
-  uint64_t empty[kStages];
+template <int S>
+struct __align__(16) BarriersT {
+  uint64_t full[S];
+  uint64_t afull[S];
+  uint64_t empty[S];
   uint64_t accum[2];        // accumulator b holds a finished tile (one phase per use)
   uint64_t acc_empty[2];    // leader: both CTAs' epilogue warps drained accumulator b
   uint32_t tmem_base;
@@ -65,7 +59,25 @@ struct __align__(16) Barriers {
   alignas(16) float lut[16];
 };
 
-constexpr int kSmemBytes = 1024 + kStages * (kABytes + kBBytes + kQBytes) + sizeof(Barriers);
+// kW token tiles of 256 per pair tile.  kW = 1: the two TMEM accumulators
+// alternate between tiles (tile t+1 accumulates while tile t drains).  kW = 2
+// (dense launches with many tokens): each decoded W stage feeds both
+// accumulators, tokens [m0, m0 + 256) and [m0 + 256, m0 + 512), halving the
+// decode per FLOP; the next tile waits for the drain, and the two dY tiles per
+// stage leave room for 4 stages and 2 decode groups.
+template <int kW>
+struct Cfg {
+  static constexpr int kStages = kW == 2 ? 4 : 6;
+  static constexpr int kGroups = kW == 2 ? 2 : 3;  // decode warp groups
+  static constexpr int kThreads = 64 + 128 * kGroups;
+  static constexpr int kEpiWarps = 4 * kGroups;
+  using Bars = BarriersT<kStages>;
+  static constexpr int kSmemBytes = 1024 + kStages * (kW * kABytes + kBBytes + kQBytes) + static_cast<int>(sizeof(Bars));
+  // A decode group's consecutive stages are at most 2 * kGroups apart; at most
+  // kStages keeps its parity waits on a ring slot within one phase.
+  static_assert(2 * kGroups <= kStages, "decode-group rotation longer than the stage ring");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
 
 struct Args {
   const float* scales;
@@ -94,7 +106,7 @@ struct Tile {
 // Tile t: grouped launches read the list; dense ones walk bands of kGroupM
 // token tiles x all column tiles, so a band's dY slab is read by pairs that
 // run together.
-__device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int num_m) {
+__device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int num_m, int tok_tile) {
   Tile r;
   if (args.tiles != nullptr) {
     const int4 v = args.tiles[t];
@@ -112,7 +124,7 @@ __device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int 
     const int rows_in_band = min(kGroupM, num_m - first_m);
     const int local = t - band * kGroupM * num_k;
     r.expert = 0;
-    r.m0 = (first_m + local % rows_in_band) * 2 * kTokHalf;
+    r.m0 = (first_m + local % rows_in_band) * tok_tile;
     r.m_end = args.M;
     r.k_tile = local / rows_in_band;
   }
@@ -122,16 +134,21 @@ __device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int 
 // Persistent: each CTA pair walks tiles pair, pair + P, ...; stage counters
 // run on across tiles and the two TMEM accumulators alternate, so the MMAs of
 // the next tile overlap the drain of the previous one.
-template <int kLayout>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int kLayout, int kW>
+__global__ void __launch_bounds__(Cfg<kW>::kThreads, 1)
     fl_bwd_ss_kernel(const __grid_constant__ CUtensorMap tm_dy,    // dY [M, N] bf16, box {64, 128}
                      const __grid_constant__ CUtensorMap tm_us,    // Us [M, 64] bf16, box {64, 128}
                      const __grid_constant__ CUtensorMap tm_code,  // payload [E*N, K/2] u8, box {64, 64}, 64B swizzle
                      const Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* as = smem;                                  // kStages x 16 KiB
-  uint8_t* bs = as + kStages * kABytes;                // kStages x 16 KiB
+  using C = Cfg<kW>;
+  constexpr int kStages = C::kStages;
+  constexpr int kGroups = C::kGroups;
+  constexpr int kEpiWarps = C::kEpiWarps;
+  using Barriers = typename C::Bars;
+  uint8_t* as = smem;                                  // kStages x kW x 16 KiB (stage s, token half h at s * kW + h)
+  uint8_t* bs = as + kStages * kW * kABytes;           // kStages x 16 KiB
   uint8_t* qs = bs + kStages * kBBytes;                // kStages x 4 KiB
   Barriers* bars = reinterpret_cast<Barriers*>(qs + kStages * kQBytes);
 
@@ -143,7 +160,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
   const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
-  const int num_m = (M + 2 * kTokHalf - 1) / (2 * kTokHalf);
+  constexpr int kTokTile = 2 * kTokHalf * kW;   // tokens per pair tile
+  const int num_m = (M + kTokTile - 1) / kTokTile;
   const int n_tiles = args.tiles != nullptr ? *args.tile_count : num_k * num_m * args.ksplit;
   const int n_main = N / kStageN / args.ksplit;  // stages of one tile's reduction slice
   const bool has_lora = args.rank > 0;
@@ -184,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       bool us_ready = false;
       for (int t = pair; t < n_tiles && ok; t += num_pairs) {
-        const Tile tile = tile_at(args, t, num_k, num_m);
+        const Tile tile = tile_at(args, t, num_k, num_m, kTokTile);
         const int kb = tile.k_tile * 2 * kColHalf + static_cast<int>(crank) * kColHalf;
         const int mh = tile.m0 + static_cast<int>(crank) * kTokHalf;
         const int wrow0 = tile.expert * N;
@@ -197,8 +215,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (it < n_main) {
             const int n0 = (tile.kpart * n_main + it) * kStageN;
-            mbar_arrive_expect_tx(&bars->full[s], kABytes + kQBytes);
-            tma_load_2d(as + s * kABytes, &tm_dy, n0, mh, &bars->full[s]);
+            mbar_arrive_expect_tx(&bars->full[s], kW * kABytes + kQBytes);
+#pragma unroll
+            for (int h = 0; h < kW; ++h)
+              tma_load_2d(as + (s * kW + h) * kABytes, &tm_dy, n0, mh + h * 2 * kTokHalf, &bars->full[s]);
             tma_load_2d(qs + s * kQBytes, &tm_code, kb / 2, wrow0 + n0, &bars->full[s]);
           } else {
             // Us comes from an earlier launch of the call chain (programmatic
@@ -210,8 +230,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               griddep_launch_dependents();
               us_ready = true;
             }
-            mbar_arrive_expect_tx(&bars->full[s], kABytes);
-            tma_load_2d(as + s * kABytes, &tm_us, 0, mh, &bars->full[s]);
+            mbar_arrive_expect_tx(&bars->full[s], kW * kABytes);
+#pragma unroll
+            for (int h = 0; h < kW; ++h)
+              tma_load_2d(as + (s * kW + h) * kABytes, &tm_us, 0, mh + h * 2 * kTokHalf, &bars->full[s]);
           }
         }
       }
@@ -230,13 +252,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0, tl = 0;
       bool ok = true;
       for (int t = pair; t < n_tiles && ok; t += num_pairs, ++tl) {
-        const int b = tl & 1;
-        // Accumulator b was last used by tile tl-2: both CTAs must have drained it.
-        if (tl >= 2 &&
-            !mbar_wait_cluster(&bars->acc_empty[b], ((tl >> 1) - 1) & 1, abort_word, args.status, kStatusTimeoutAccum))
+        // kW = 1: accumulator b was last used by tile tl-2; kW = 2: both were
+        // used by tile tl-1.  Both CTAs must have drained it.
+        const int b = kW == 2 ? 0 : (tl & 1);
+        const bool reused = kW == 2 ? tl >= 1 : tl >= 2;
+        const uint32_t ph_empty = kW == 2 ? ((tl - 1) & 1) : (((tl >> 1) - 1) & 1);
+        if (reused && !mbar_wait_cluster(&bars->acc_empty[b], ph_empty, abort_word, args.status, kStatusTimeoutAccum))
           break;
         tc_fence_after();
-        const uint32_t acc = tmem_base + b * kAccCols;
         for (int it = 0; it < n_iter; ++it, ++g) {
           const int s = g % kStages;
           const uint32_t ph = (g / kStages) & 1;
@@ -245,11 +268,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(as + s * kABytes));
           const uint64_t bdesc = sdesc_mnmajor_sw128(smem_u32(bs + s * kBBytes), kBLbo, kBSbo);
           const int ksteps = it < n_main ? kStageN / 16 : lora_k_steps;
-          for (int kk = 0; kk < ksteps; ++kk)
-            mma_ss2(acc, adesc + 2 * kk, bdesc + ((2 * kBSbo) >> 4) * kk, idesc, (it | kk) != 0 ? 1u : 0u);
+#pragma unroll
+          for (int h = 0; h < kW; ++h) {
+            const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(as + (s * kW + h) * kABytes));
+            const uint32_t acc = tmem_base + (kW == 2 ? h : b) * kAccCols;
+            for (int kk = 0; kk < ksteps; ++kk)
+              mma_ss2(acc, adesc + 2 * kk, bdesc + ((2 * kBSbo) >> 4) * kk, idesc, (it | kk) != 0 ? 1u : 0u);
+          }
           tc_commit2_mc(&bars->empty[s], 0x3);
         }
         tc_commit2_mc(&bars->accum[b], 0x3);
@@ -258,7 +285,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The last commit covers every MMA this thread issued.
         uint32_t dummy_abort = 0;
         const int last = tl - 1;
-        mbar_wait(&bars->accum[last & 1], (last >> 1) & 1, &dummy_abort, args.status, kStatusTimeoutAccum);
+        if (kW == 2)
+          mbar_wait(&bars->accum[0], last & 1, &dummy_abort, args.status, kStatusTimeoutAccum);
+        else
+          mbar_wait(&bars->accum[last & 1], (last >> 1) & 1, &dummy_abort, args.status, kStatusTimeoutAccum);
       }
     }
   } else {
@@ -281,15 +311,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // mh + 32q .. +32; each thread writes its token row's columns in 32-wide
     // chunks (64 contiguous bytes), the groups taking chunks round robin.
     auto epilogue = [&](const Tile& tile, int tl) {
-      const int b = tl & 1;
-      const int m = tile.m0 + static_cast<int>(crank) * kTokHalf + quarter * 32 + lane;
+      const int b = kW == 2 ? 0 : (tl & 1);
+      const uint32_t ph_acc = kW == 2 ? (tl & 1) : ((tl >> 1) & 1);
       const int k0 = tile.k_tile * 2 * kColHalf;
-      if (ok && mbar_wait_warp(&bars->accum[b], (tl >> 1) & 1, abort_word, args.status, kStatusTimeoutAccum)) {
+      if (ok && mbar_wait_warp(&bars->accum[b], ph_acc, abort_word, args.status, kStatusTimeoutAccum)) {
         tc_fence_after();
+#pragma unroll 1
+        for (int h = 0; h < kW; ++h) {
+        // Token half h of the tile: accumulator h (kW = 2) or b.
+        const int m = tile.m0 + h * 2 * kTokHalf + static_cast<int>(crank) * kTokHalf + quarter * 32 + lane;
+        const uint32_t acc_col = static_cast<uint32_t>((kW == 2 ? h : b) * kAccCols);
 #pragma unroll 1
         for (int c = 32 * grp; c < kAccCols; c += 32 * kGroups) {
           uint32_t acc[32];
-          tmem_ld_32x32b_x32(tmem_base + b * kAccCols + lane_addr + c, acc);
+          tmem_ld_32x32b_x32(tmem_base + acc_col + lane_addr + c, acc);
           tmem_wait_ld();
           const int kcol = k0 + c;
           if (args.ksplit > 1) {
@@ -314,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        }
         tc_fence_before();
       } else {
         ok = false;
@@ -329,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     Tile prev{};
     const int pairs_per_tile = (n_iter + 1) / 2;  // the last one a single stage when n_iter is odd
     for (int tt = pair; tt < n_tiles; tt += num_pairs, g0 += n_iter, ++tl) {
-      const Tile tile = tile_at(args, tt, num_k, num_m);
+      const Tile tile = tile_at(args, tt, num_k, num_m, kTokTile);
       const int kb = tile.k_tile * 2 * kColHalf + static_cast<int>(crank) * kColHalf;
       const int wrow0 = tile.expert * N;
       const float* alora = args.alora + static_cast<size_t>(tile.expert) * args.rank * K;
@@ -489,19 +525,31 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   a.tile_count = tile_count;
   a.part = part;
   a.ksplit = ksplit;
-  const int tiles_max = tiles ? max_tiles
-                              : ((K + 2 * kColHalf - 1) / (2 * kColHalf)) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf)) *
-                                    ksplit;
+  // 512-token pair tiles (each decoded W stage feeds both accumulators) for
+  // dense launches without a reduction split whose wide tiles still number
+  // at least two per CTA pair (the last wave's quantization stays small).
+  const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
+  const int64_t wide_tiles = static_cast<int64_t>(num_k) * ((M + 4 * kTokHalf - 1) / (4 * kTokHalf));
+  const bool wide = !tiles && ksplit == 1 && wide_tiles >= 2 * device_pairs();
+  const int tok_tile = (wide ? 4 : 2) * kTokHalf;
+  const int tiles_max = tiles ? max_tiles : num_k * ((M + tok_tile - 1) / tok_tile) * ksplit;
+  const void* kfn;
+  if (layout == kLayoutG128)
+    kfn = wide ? reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutG128, 2>)
+               : reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutG128, 1>);
+  else
+    kfn = wide ? reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutNf4Dq64, 2>)
+               : reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutNf4Dq64, 1>);
+  const int threads = wide ? Cfg<2>::kThreads : Cfg<1>::kThreads;
+  const int smem = wide ? Cfg<2>::kSmemBytes : Cfg<1>::kSmemBytes;
   int pairs = 0;
-  const void* kfn = layout == kLayoutG128 ? reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutG128>)
-                                          : reinterpret_cast<const void*>(&fl_bwd_ss_kernel<kLayoutNf4Dq64>);
-  if ((rc = resident_pairs(kfn, kThreads, kSmemBytes, &pairs))) return rc;
+  if ((rc = resident_pairs(kfn, threads, smem, &pairs))) return rc;
   if (pairs > tiles_max) pairs = tiles_max;
   if (pairs < 1) return FL_OK;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -512,9 +560,13 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl && rank > 0 ? 2 : 1;
-  cudaError_t le = layout == kLayoutG128
-                       ? cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutG128>, tm_dy, tm_us, tm_code, a)
-                       : cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutNf4Dq64>, tm_dy, tm_us, tm_code, a);
+  cudaError_t le;
+  if (layout == kLayoutG128)
+    le = wide ? cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutG128, 2>, tm_dy, tm_us, tm_code, a)
+              : cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutG128, 1>, tm_dy, tm_us, tm_code, a);
+  else
+    le = wide ? cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutNf4Dq64, 2>, tm_dy, tm_us, tm_code, a)
+              : cudaLaunchKernelEx(&cfg, fl_bwd_ss_kernel<kLayoutNf4Dq64, 1>, tm_dy, tm_us, tm_code, a);
   if (le != cudaSuccess) return set_error(FL_ERR_CUDA, "bwd gemm launch: %s", cudaGetErrorString(le));
   if (ksplit > 1) return launch_split_reduce(part, ksplit, static_cast<int64_t>(M) * K, dx, stream);
   return FL_OK;

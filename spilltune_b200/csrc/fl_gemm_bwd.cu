@@ -20,11 +20,17 @@
 //     contiguous bytes per thread per 32-column chunk.
 //   * The extra LoRA stage uses A = the Us tile, B = bf16(Alora[0:64, k]).
 // Persistent CTA pairs over a static tile list with two TMEM accumulators
-// (512 columns): tile t+1 accumulates while tile t drains.
-// Warp roles (448 threads per CTA): warp 0 TMA producer, warp 1 TMEM owner (both
-// CTAs) + MMA issuer (leader), warps 2-13 three groups of four decode warps that
-// take turns on stages and drain the previous tile's accumulator after their
-// first stage pair of the next one.  Barriers as in fl_gemm.cu, with
+// (512 columns), in one of two forms (Cfg below):
+//   * 256-token tiles: tile t+1 accumulates while tile t drains; 6 stages,
+//     three decode groups (448 threads per CTA);
+//   * 512-token tiles (dense launches with many tokens): every decoded W stage
+//     feeds both accumulators (tokens m0.. and m0+256..), half the decode per
+//     FLOP; the next tile's MMAs wait for the drain; two dY tiles per stage
+//     leave room for 4 stages and two decode groups (320 threads per CTA).
+// Warp roles: warp 0 TMA producer, warp 1 TMEM owner (both CTAs) + MMA issuer
+// (leader), then the groups of four decode warps that take turns on stages
+// and drain the previous tile's accumulator(s) after their first stage pair
+// of the next one.  Barriers as in fl_gemm.cu, with
 // accum/acc_empty per accumulator.
 #include <cuda_bf16.h>
 #include <cstdint>

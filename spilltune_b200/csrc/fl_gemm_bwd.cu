@@ -495,7 +495,7 @@ int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles, const int* tile_count, int experts, int max_tiles,
-                    int layout, bool pdl, float* part, int ksplit) {
+                    int layout, bool pdl, float* part, int ksplit, bool grouped_wide) {
   using namespace bwd;
   if (layout != kLayoutG128 && layout != kLayoutNf4Dq64) return set_error(FL_ERR_ARG, "bwd gemm: unknown layout");
   if (layout != kLayoutG128 && tiles) return set_error(FL_ERR_UNSUPPORTED, "grouped launches use layout 0");
@@ -532,11 +532,16 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   a.part = part;
   a.ksplit = ksplit;
   // 512-token pair tiles (each decoded W stage feeds both accumulators) for
-  // dense launches without a reduction split whose wide tiles still number
-  // at least two per CTA pair (the last wave's quantization stays small).
+  // dense launches without a reduction split, with a reduction over N >=
+  // kBwdWideMinN (measured: 16-32 stages of 64 rows gained nothing or lost 1%,
+  // the next tile waiting for the drain; 64 and more stages gained 8-16%) and
+  // wide tiles still at least two per CTA pair (the last wave's quantization
+  // stays small); for grouped launches exactly when the caller planned 512-row
+  // tiles.
   const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
   const int64_t wide_tiles = static_cast<int64_t>(num_k) * ((M + 4 * kTokHalf - 1) / (4 * kTokHalf));
-  const bool wide = !tiles && ksplit == 1 && wide_tiles >= 2 * device_pairs();
+  const bool wide = tiles ? grouped_wide
+                          : (ksplit == 1 && N >= kBwdWideMinN && wide_tiles >= 2 * device_pairs());
   const int tok_tile = (wide ? 4 : 2) * kTokHalf;
   const int tiles_max = tiles ? max_tiles : num_k * ((M + tok_tile - 1) / tok_tile) * ksplit;
   const void* kfn;

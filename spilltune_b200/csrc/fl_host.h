@@ -69,11 +69,15 @@ int moe_max_tiles(int total_rows, int experts, int rows, int col_tiles);
 // ksplit > 1 (dense only): tile t sums reduction rows n in [t.kpart * S * 64,
 // (t.kpart + 1) * S * 64), S = N / 64 / ksplit, into part[kpart][M][K] (FP32;
 // the LoRA stage in kpart 0 only), for launch_split_reduce.
+// grouped_wide: a grouped launch whose tile list has 512-row tiles (launch_moe_plan with
+// rows = 512) runs the 512-token pair tiles (the caller decides, so the plan and the
+// kernel agree); dense launches choose them themselves.
+constexpr int kBwdWideMinN = 64 * 64;  // 512-token backward tiles need a reduction over N >= this
 int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const float* scales, const float* lut,
                     const float* alora, int rank, void* dx, int M, int N, int K, uint32_t* status,
                     cudaStream_t stream, const int4* tiles = nullptr, const int* tile_count = nullptr,
                     int experts = 1, int max_tiles = 0, int layout = 0, bool pdl = false, float* part = nullptr,
-                    int ksplit = 1);
+                    int ksplit = 1, bool grouped_wide = false);
 
 int launch_dequant(const uint8_t* payload, const float* scales, const float* lut, int64_t numel, void* out,
                    cudaStream_t stream, int layout = 0);

@@ -116,6 +116,7 @@ namespace {
 
 constexpr int kFwdRows = 256;   // forward GEMM pair tile: 256 tokens x 256 output columns
 constexpr int kBwdRows = 256;   // backward GEMM pair tile: 256 tokens x 256 input columns
+constexpr int kBwdWideRows = 512;  // ... or 512 tokens when the experts average >= 384 rows
 constexpr int kDownRows = 128;  // lora_down tile
 constexpr int kGradRows = 512;  // lora_grad token slice
 
@@ -254,7 +255,12 @@ int fl_grouped_bwd(const uint16_t* dY, const uint16_t* X, const int32_t* seg, in
   uint8_t* us = rank > 0 ? ws + p.off_us : nullptr;
   uint8_t* ts = rank > 0 ? ws + p.off_ts : nullptr;
   const int r = static_cast<int>(rows), n = static_cast<int>(N), k = static_cast<int>(K);
-  if ((rc = launch_moe_plan(seg, experts, r, kBwdRows, (k + 255) / 256, t_bwd, p.bwd_tiles, counts + 0, status, st)))
+  // Experts averaging >= 384 rows over a long reduction: 512-token tiles, each decoded
+  // W stage feeding both accumulators (the plan's tile count can only fall, so
+  // p.bwd_tiles still bounds it).
+  const bool wide = static_cast<int64_t>(rows) >= 384LL * experts && N >= kBwdWideMinN;
+  if ((rc = launch_moe_plan(seg, experts, r, wide ? kBwdWideRows : kBwdRows, (k + 255) / 256, t_bwd, p.bwd_tiles,
+                            counts + 0, status, st)))
     return rc;
   bool db_done = false;
   if (rank > 0) {
@@ -275,7 +281,7 @@ int fl_grouped_bwd(const uint16_t* dY, const uint16_t* X, const int32_t* seg, in
       return rc;
   }
   if ((rc = launch_bwd_gemm(dY, us, payload, scales, lut16, A, rank, dX, r, n, k, status, st, t_bwd, counts + 0,
-                            experts, p.bwd_tiles)))
+                            experts, p.bwd_tiles, /*layout=*/0, /*pdl=*/false, nullptr, 1, wide)))
     return rc;
   if (rank > 0) {
     // dA_e[j, k] = sum_{m in e} Us[m, j] X[m, k]

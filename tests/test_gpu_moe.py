@@ -76,6 +76,7 @@ CASES = [
     ([200, 90, 512, 33, 129, 0], 1536, 2048, 8),     # Qwen3-30B-A3B expert gate_up
     ([200, 90, 512, 33, 129, 0], 2048, 768, 8),      # ... and down
     ([600, 1, 1, 700], 512, 1024, 64),
+    ([512, 700, 300, 600], 4096, 1024, 16),         # >= 384 rows per expert, N >= 4096: 512-token backward tiles
     ([128, 0, 200, 64], 4096, 7168, 16),            # DeepSeek-V3 expert gate_up (2 x 2048), ~128 rows each
     ([128, 0, 200, 64], 7168, 2048, 16),            # ... and down
 ]

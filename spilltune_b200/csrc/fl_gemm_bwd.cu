@@ -534,14 +534,16 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   // 512-token pair tiles (each decoded W stage feeds both accumulators) for
   // dense launches without a reduction split, with a reduction over N >=
   // kBwdWideMinN (measured: 16-32 stages of 64 rows gained nothing or lost 1%,
-  // the next tile waiting for the drain; 64 and more stages gained 8-16%) and
-  // wide tiles still at least two per CTA pair (the last wave's quantization
-  // stays small); for grouped launches exactly when the caller planned 512-row
-  // tiles.
+  // the next tile waiting for the drain; 64 and more stages gained 8-16%), when
+  // the pairs' rounds of wide tiles, each costing 1.62 rounds of 256-token
+  // tiles (measured 1.53-1.62 at 8192 tokens), beat the rounds of 256-token
+  // tiles; for grouped launches exactly when the caller planned 512-row tiles.
   const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
-  const int64_t wide_tiles = static_cast<int64_t>(num_k) * ((M + 4 * kTokHalf - 1) / (4 * kTokHalf));
+  const int64_t P = device_pairs();
+  const int64_t narrow_rounds = (static_cast<int64_t>(num_k) * ((M + 2 * kTokHalf - 1) / (2 * kTokHalf)) + P - 1) / P;
+  const int64_t wide_rounds = (static_cast<int64_t>(num_k) * ((M + 4 * kTokHalf - 1) / (4 * kTokHalf)) + P - 1) / P;
   const bool wide = tiles ? grouped_wide
-                          : (ksplit == 1 && N >= kBwdWideMinN && wide_tiles >= 2 * device_pairs());
+                          : (ksplit == 1 && N >= kBwdWideMinN && 162 * wide_rounds < 100 * narrow_rounds);
   const int tok_tile = (wide ? 4 : 2) * kTokHalf;
   const int tiles_max = tiles ? max_tiles : num_k * ((M + tok_tile - 1) / tok_tile) * ksplit;
   const void* kfn;

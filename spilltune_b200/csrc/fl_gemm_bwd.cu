@@ -138,8 +138,9 @@ __device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int 
 }
 
 // Persistent: each CTA pair walks tiles pair, pair + P, ...; stage counters
-// run on across tiles and the two TMEM accumulators alternate, so the MMAs of
-// the next tile overlap the drain of the previous one.
+// run on across tiles.  kW = 1: the two TMEM accumulators alternate, so the
+// MMAs of the next tile overlap the drain of the previous one; kW = 2: both
+// hold one 512-token tile and the next tile's MMAs wait for its drain.
 template <int kLayout, int kW>
 __global__ void __launch_bounds__(Cfg<kW>::kThreads, 1)
     fl_bwd_ss_kernel(const __grid_constant__ CUtensorMap tm_dy,    // dY [M, N] bf16, box {64, 128}

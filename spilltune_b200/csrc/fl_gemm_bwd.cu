@@ -98,6 +98,10 @@ struct Args {
   // FP32 sums to part[kpart][M][K] (dX is then formed by the split reduce).
   float* part;
   int ksplit;
+  // 512-token launches: tiles [0, dense_full) are full 512-token tiles; the
+  // last round's remaining wide tiles follow as two 256-token halves each
+  // (one accumulator), so the last round costs about half.
+  int dense_full;
 };
 
 // Byte offset of 16-byte chunk j (k = 8j..8j+7 within the CTA's 64-k half
@@ -107,13 +111,14 @@ __device__ __forceinline__ uint32_t b_offset(int r, int khalf, int j) {
 }
 
 struct Tile {
-  int expert, m0, m_end, k_tile, kpart;
+  int expert, m0, m_end, k_tile, kpart, half;  // half: a 256-token tile of a 512-token launch
 };
 // Tile t: grouped launches read the list; dense ones walk bands of kGroupM
 // token tiles x all column tiles, so a band's dY slab is read by pairs that
 // run together.
 __device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int num_m, int tok_tile) {
   Tile r;
+  r.half = 0;
   if (args.tiles != nullptr) {
     const int4 v = args.tiles[t];
     r.expert = v.x;
@@ -122,6 +127,13 @@ __device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int 
     r.k_tile = v.w;
     r.kpart = 0;
   } else {
+    int sub = 0;
+    if (t >= args.dense_full) {  // (512-token launches) half h of wide tile dense_full + j
+      const int j = t - args.dense_full;
+      sub = j & 1;
+      t = args.dense_full + (j >> 1);
+      r.half = 1;
+    }
     // The slices of one output tile are consecutive tiles (they run together).
     r.kpart = t % args.ksplit;
     t /= args.ksplit;
@@ -130,7 +142,7 @@ __device__ __forceinline__ Tile tile_at(const Args& args, int t, int num_k, int 
     const int rows_in_band = min(kGroupM, num_m - first_m);
     const int local = t - band * kGroupM * num_k;
     r.expert = 0;
-    r.m0 = (first_m + local % rows_in_band) * tok_tile;
+    r.m0 = (first_m + local % rows_in_band) * tok_tile + sub * (tok_tile / 2);
     r.m_end = args.M;
     r.k_tile = local / rows_in_band;
   }
@@ -169,7 +181,9 @@ __global__ void __launch_bounds__(Cfg<kW>::kThreads, 1)
   const int num_k = (K + 2 * kColHalf - 1) / (2 * kColHalf);
   constexpr int kTokTile = 2 * kTokHalf * kW;   // tokens per pair tile
   const int num_m = (M + kTokTile - 1) / kTokTile;
-  const int n_tiles = args.tiles != nullptr ? *args.tile_count : num_k * num_m * args.ksplit;
+  // 512-token launches: the last round's wide tiles as two halves each.
+  const int n_dense = num_k * num_m * args.ksplit;
+  const int n_tiles = args.tiles != nullptr ? *args.tile_count : 2 * n_dense - min(args.dense_full, n_dense);
   const int n_main = N / kStageN / args.ksplit;  // stages of one tile's reduction slice
   const bool has_lora = args.rank > 0;
   const int n_iter = n_main + (has_lora ? 1 : 0);
@@ -222,10 +236,11 @@ __global__ void __launch_bounds__(Cfg<kW>::kThreads, 1)
           }
           if (it < n_main) {
             const int n0 = (tile.kpart * n_main + it) * kStageN;
-            mbar_arrive_expect_tx(&bars->full[s], kW * kABytes + kQBytes);
+            const int na = tile.half ? 1 : kW;  // dY tiles of this tile
+            mbar_arrive_expect_tx(&bars->full[s], na * kABytes + kQBytes);
 #pragma unroll
             for (int h = 0; h < kW; ++h)
-              tma_load_2d(as + (s * kW + h) * kABytes, &tm_dy, n0, mh + h * 2 * kTokHalf, &bars->full[s]);
+              if (h < na) tma_load_2d(as + (s * kW + h) * kABytes, &tm_dy, n0, mh + h * 2 * kTokHalf, &bars->full[s]);
             tma_load_2d(qs + s * kQBytes, &tm_code, kb / 2, wrow0 + n0, &bars->full[s]);
           } else {
             // Us comes from an earlier launch of the call chain (programmatic
@@ -237,10 +252,11 @@ __global__ void __launch_bounds__(Cfg<kW>::kThreads, 1)
               griddep_launch_dependents();
               us_ready = true;
             }
-            mbar_arrive_expect_tx(&bars->full[s], kW * kABytes);
+            const int na = tile.half ? 1 : kW;
+            mbar_arrive_expect_tx(&bars->full[s], na * kABytes);
 #pragma unroll
             for (int h = 0; h < kW; ++h)
-              tma_load_2d(as + (s * kW + h) * kABytes, &tm_us, 0, mh + h * 2 * kTokHalf, &bars->full[s]);
+              if (h < na) tma_load_2d(as + (s * kW + h) * kABytes, &tm_us, 0, mh + h * 2 * kTokHalf, &bars->full[s]);
           }
         }
       }
@@ -267,6 +283,7 @@ __global__ void __launch_bounds__(Cfg<kW>::kThreads, 1)
         if (reused && !mbar_wait_cluster(&bars->acc_empty[b], ph_empty, abort_word, args.status, kStatusTimeoutAccum))
           break;
         tc_fence_after();
+        const int na = tile_at(args, t, num_k, num_m, kTokTile).half ? 1 : kW;  // accumulators this tile fills
         for (int it = 0; it < n_iter; ++it, ++g) {
           const int s = g % kStages;
           const uint32_t ph = (g / kStages) & 1;
@@ -279,6 +296,7 @@ __global__ void __launch_bounds__(Cfg<kW>::kThreads, 1)
           const int ksteps = it < n_main ? kStageN / 16 : lora_k_steps;
 #pragma unroll
           for (int h = 0; h < kW; ++h) {
+            if (h >= na) break;
             const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(as + (s * kW + h) * kABytes));
             const uint32_t acc = tmem_base + (kW == 2 ? h : b) * kAccCols;
             for (int kk = 0; kk < ksteps; ++kk)
@@ -324,7 +342,7 @@ __global__ void __launch_bounds__(Cfg<kW>::kThreads, 1)
       if (ok && mbar_wait_warp(&bars->accum[b], ph_acc, abort_word, args.status, kStatusTimeoutAccum)) {
         tc_fence_after();
 #pragma unroll 1
-        for (int h = 0; h < kW; ++h) {
+        for (int h = 0; h < (tile.half ? 1 : kW); ++h) {
         // Token half h of the tile: accumulator h (kW = 2) or b.
         const int m = tile.m0 + h * 2 * kTokHalf + static_cast<int>(crank) * kTokHalf + quarter * 32 + lane;
         const uint32_t acc_col = static_cast<uint32_t>((kW == 2 ? h : b) * kAccCols);
@@ -558,7 +576,19 @@ int launch_bwd_gemm(const void* dy, const void* us, const uint8_t* codes, const 
   const int smem = wide ? Cfg<2>::kSmemBytes : Cfg<1>::kSmemBytes;
   int pairs = 0;
   if ((rc = resident_pairs(kfn, threads, smem, &pairs))) return rc;
-  if (pairs > tiles_max) pairs = tiles_max;
+  // 512-token launches whose last round would hold at most half a round of
+  // wide tiles run those tiles as two 256-token halves each: the pairs that
+  // take one finish in about 0.6 of a wide tile instead of a whole one.
+  int n_tiles = tiles_max;
+  a.dense_full = tiles ? 0 : tiles_max;
+  if (!tiles && wide && pairs > 0) {
+    const int full = (tiles_max / pairs) * pairs, rem = tiles_max - full;
+    if (full > 0 && rem > 0 && 2 * rem <= pairs) {
+      a.dense_full = full;
+      n_tiles = full + 2 * rem;
+    }
+  }
+  if (pairs > n_tiles) pairs = n_tiles;
   if (pairs < 1) return FL_OK;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
